@@ -1,0 +1,455 @@
+#!/usr/bin/env python
+"""Benchmark of the fused mixed-bit MoE path (one JSON line on rank 0).
+
+Headline workload: OLMoE-shaped 16-layer MoE stack, decode at
+batch 1, 8, 32 and 64. One step = one pass of the 16-layer stack at each batch
+size; layers are chained with the decoder's residual add fused into the combine
+(x <- x + moe_l(x)), each batch size replayed as one CUDA graph. ``value`` =
+algorithmic HBM bytes of all passes (packed weights + fp16 scales/zeros of every
+expert the routing hits, the gate weights, activations in/out) / device time, in
+GB/s, summed over ranks (``--gpus N`` runs N independent replicas: weak scaling).
+
+Also reported: per-batch GB/s and tokens/s, Qwen3-30B-A3B-shaped prefill (BASELINE
+config 2, Zipf-skewed router logits) tokens/s and TFLOP/s, the dominant stage's
+roofline from library stage timers, ``e2e`` through the public block API with
+pinned host buffers, the CPU fake-quant baseline (``cpu_baseline``), clocks.
+``--impl reference`` times the reference's CPU fake-quant path instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer prefill tokens/s + decode HBM GB/s (% roofline) at 1/2/4/8 B200"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batches", default="1,8,32,64")
+    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--prefill-layers", type=int, default=48)
+    ap.add_argument("--prefill-tokens", type=int, default=4096)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / "bench_clocks.csv"
+
+    def start(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpus):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in gpus:
+                continue
+            rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        loaded = [v for v in sm if v > 0.5 * max(sm)] if sm else []
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- our arm
+def build_stack(n_layers, device, seed0):
+    from robustgemq_b200 import synth
+    from robustgemq_b200.inference import QuantFusedOlmoeMoEBlock
+
+    cfg, shp = synth.olmoe_config()
+    blocks = []
+    for l in range(n_layers):
+        blocks.append(synth.random_block(QuantFusedOlmoeMoEBlock, cfg, shp["hidden"], shp["inter"],
+                                         shp["num_experts"], shp["mean_bits"], shp["group_size"], seed0 + l, device))
+    return blocks
+
+
+def stack_forward(blocks, x, one_token, time_stages=False):
+    from robustgemq_b200 import _lib
+
+    flags = _lib.FWD_RESIDUAL | (_lib.FWD_ONE_TOKEN if one_token else 0)
+    if time_stages:
+        flags |= _lib.FWD_TIME_STAGES
+    for blk in blocks:
+        x, _ = blk._run(x, flags, want_logits=False)
+    return x
+
+
+def stage_times(blk):
+    import ctypes
+
+    from robustgemq_b200 import _lib
+
+    arr = (ctypes.c_float * 6)()
+    _lib.check(_lib.load().gemq_layer_stage_times(blk.layer_handle(), arr))
+    return list(arr)
+
+
+def decode_bytes(blocks, expert_bytes, x, one_token):
+    """Algorithmic HBM bytes of one stack pass from its actual routing (untimed)."""
+    import torch
+
+    B, D = x.shape
+    total = 0
+    for blk, eb in zip(blocks, expert_bytes):
+        _, idx, _ = blk.route(x)
+        hit = torch.unique(idx).tolist()
+        total += sum(eb[e] for e in hit) + blk.num_experts * D * 2 + 3 * B * D * 2
+        x = stack_forward([blk], x, one_token)
+    return total
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from robustgemq_b200 import _lib, synth
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    hbm_peak, bf16_peak, bf16_sus, peak_src = peaks()
+    batches = [int(b) for b in args.batches.split(",")]
+    t0 = time.time()
+    blocks = build_stack(args.layers, device, 1000)
+    expert_bytes = [synth.layer_expert_bytes(b) for b in blocks]
+    D = blocks[0].hidden_dim
+    n_sets = 4
+    gen = torch.Generator(device=device).manual_seed(7 + rank)
+    inputs = {B: [torch.randn((B, D), generator=gen, device=device).half() for _ in range(n_sets)] for B in batches}
+    # per-batch algorithmic bytes, averaged over the input sets
+    bytes_per_pass = {}
+    for B in batches:
+        bytes_per_pass[B] = sum(decode_bytes(blocks, expert_bytes, x, B == 1) for x in inputs[B]) / n_sets
+    # warm the workspaces, then capture one graph per batch size
+    static_in = {B: inputs[B][0].clone() for B in batches}
+    graphs, static_out = {}, {}
+    for B in batches:
+        for _ in range(2):
+            stack_forward(blocks, static_in[B], B == 1)
+    torch.cuda.synchronize()
+    for B in batches:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            static_out[B] = stack_forward(blocks, static_in[B], B == 1)
+        graphs[B] = g
+    torch.cuda.synchronize()
+    setup_s = time.time() - t0
+
+    def step(i, per_batch_ms=None):
+        for B in batches:
+            static_in[B].copy_(inputs[B][i % n_sets])
+            graphs[B].replay()
+
+    for i in range(args.warmup):
+        step(i)
+    # per-batch timing (untimed by the driver; for the breakdown)
+    per_b = {}
+    for B in batches:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for i in range(max(3, args.steps // 2)):
+            static_in[B].copy_(inputs[B][i % n_sets])
+            graphs[B].replay()
+        e.record()
+        torch.cuda.synchronize()
+        per_b[B] = s.elapsed_time(e) / max(3, args.steps // 2)
+
+    clocks = Clocks() if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.start()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        step(i)
+    stop.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(stop)
+    clk = clocks.stop([local_rank + r for r in range(world)] if world > 1 else [torch.cuda.current_device()]) if clocks else None
+    ms_t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    step_bytes = sum(bytes_per_pass.values())
+    value = world * step_bytes * args.steps / (ms_max * 1e-3) / 1e9
+
+    # e2e through the block API with pinned host buffers (eager calls, one rank's view)
+    host_in = {B: [t.cpu().pin_memory() for t in inputs[B]] for B in batches}
+    host_out = {B: torch.empty((B, D), dtype=torch.float16).pin_memory() for B in batches}
+    dev_in = {B: torch.empty((B, D), dtype=torch.float16, device=device) for B in batches}
+    for i in range(2):
+        for B in batches:
+            dev_in[B].copy_(host_in[B][i % n_sets], non_blocking=True)
+            host_out[B].copy_(stack_forward(blocks, dev_in[B], B == 1), non_blocking=True)
+    torch.cuda.synchronize()
+    e_steps = max(3, args.steps // 2)
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record()
+    for i in range(e_steps):
+        for B in batches:
+            dev_in[B].copy_(host_in[B][i % n_sets], non_blocking=True)
+            host_out[B].copy_(stack_forward(blocks, dev_in[B], B == 1), non_blocking=True)
+    ee.record()
+    torch.cuda.synchronize()
+    e2e_ms = es.elapsed_time(ee) / e_steps
+    h2d = sum(B * D * 2 for B in batches)
+
+    # stage breakdown + dominant-stage roofline (eager, stage events)
+    stage_ms = {}
+    for B in batches:
+        acc = [0.0] * 6
+        reps = 3
+        for i in range(reps):
+            x = inputs[B][i % n_sets]
+            for blk in blocks:
+                x2 = stack_forward([blk], x, B == 1, time_stages=True)
+                st = stage_times(blk)
+                acc = [a + s for a, s in zip(acc, st)]
+                x = x2
+        stage_ms[B] = [a / reps for a in acc]
+    names = _lib.STAGES
+    dom_b, dom_s = max(((B, s) for B in batches for s in range(6)), key=lambda bs: stage_ms[bs[0]][bs[1]])
+    # algorithmic bytes of the up/down stages for that batch: the hit experts' matrices
+    dom_bytes = None
+    if names[dom_s] in ("up", "down"):
+        share = {"up": 2.0 / 3.0, "down": 1.0 / 3.0}[names[dom_s]]  # w1+w3 vs w2 of each expert (equal shapes)
+        weights = bytes_per_pass[dom_b] - args.layers * (blocks[0].num_experts * D * 2 + 3 * dom_b * D * 2)
+        dom_bytes = weights * share / args.layers
+    dom_ms = stage_ms[dom_b][dom_s] / args.layers
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_bytes else None
+
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill(args, device, bf16_peak, bf16_sus)
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        cpu = cpu_baseline(blocks[0], inputs, args.cpu_seconds)
+    launches = kernel_launches(blocks, batches)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "olmoe-16-layer-moe-stack-decode (BASELINE config 1)",
+                   "batches": batches, "layers": args.layers, "hidden": D, "inter": blocks[0].ffn_dim,
+                   "experts": blocks[0].num_experts, "top_k": blocks[0].top_k, "group_size": 64,
+                   "mean_bits": 2.5, "parallelism": f"replicas x{world}",
+                   "l2": "per-step weight working set 0.3-2.5 GB per batch size > 126 MB L2",
+                   "graph": "one CUDA graph per batch size"},
+        "decode_per_batch": {str(B): {"ms_per_pass": round(per_b[B], 4),
+                                      "gbs": round(bytes_per_pass[B] / (per_b[B] * 1e-3) / 1e9, 1),
+                                      "tokens_per_s": round(B / (per_b[B] * 1e-3), 1),
+                                      "frac_hbm": round(bytes_per_pass[B] / (per_b[B] * 1e-3) / 1e9 / hbm_peak, 3),
+                                      "stage_ms_per_layer": [round(v / args.layers, 5) for v in stage_ms[B]]}
+                             for B in batches},
+        "stages": list(names),
+        "roofline": {"bound": "hbm", "kernel": f"{names[dom_s]} stage at batch {dom_b}",
+                     "achieved": round(achieved, 1) if achieved else None, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 3) if achieved else None, "traffic": None,
+                     "peak_source": peak_src},
+        "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": h2d, "path": "QuantFusedOlmoeMoEBlock._run per layer, eager, pinned host I/O"},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk, "setup_s": round(setup_s, 1),
+    }
+    if prefill:
+        line["prefill"] = prefill
+    if cpu:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+def kernel_launches(blocks, batches):
+    """Kernels of ours per step (counted from the pipeline): one-token path 9 per layer
+    (router, top-k, 2 up partials, 2 reduces, down partial, reduce, combine); n-token
+    path 9 (router, top-k, memset, count, scan, scatter, up, down, combine)."""
+    return sum(len(blocks) * 9 for _ in batches)
+
+
+def run_prefill(args, device, bf16_peak, bf16_sus):
+    import torch
+
+    from robustgemq_b200 import _lib, synth
+    from robustgemq_b200.inference import QuantFusedQwen3MoeMoEBlock
+
+    cfg, shp = synth.qwen3_config()
+    L, T = args.prefill_layers, args.prefill_tokens
+    blocks = [synth.random_block(QuantFusedQwen3MoeMoEBlock, cfg, shp["hidden"], shp["inter"], shp["num_experts"],
+                                 shp["mean_bits"], shp["group_size"], 5000 + l, device) for l in range(L)]
+    logits = [synth.zipf_logits(T, shp["num_experts"], 9000 + l, device) for l in range(L)]
+    x0 = torch.randn((T, shp["hidden"]), device=device).half()
+
+    def fwd(x, time_stages=False):
+        flags = _lib.FWD_RESIDUAL | (_lib.FWD_TIME_STAGES if time_stages else 0)
+        for blk, lg in zip(blocks, logits):
+            x, _ = blk._run(x, flags, want_logits=False, logits_in=lg)
+        return x
+
+    for _ in range(2):
+        fwd(x0)
+    torch.cuda.synchronize()
+    reps = max(2, args.steps // 4)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fwd(x0)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / reps
+    D, F, E, k = shp["hidden"], shp["inter"], shp["num_experts"], cfg.num_experts_per_tok
+    flops = L * T * k * 6 * D * F  # routed experts (router logits are given)
+    # stage times on the first layer
+    x = x0
+    blk = blocks[0]
+    blk._run(x, _lib.FWD_RESIDUAL | _lib.FWD_TIME_STAGES, want_logits=False, logits_in=logits[0])
+    st = stage_times(blk)
+    up_flops = T * k * 4 * D * F
+    dn_flops = T * k * 2 * D * F
+    return {"workload": "qwen3-30b-a3b-shaped prefill, 48 layers, 4096 tokens, Zipf(1.1) router logits (config 2)",
+            "layers": L, "tokens": T, "ms_per_pass": round(ms, 3), "tokens_per_s": round(T / (ms * 1e-3), 1),
+            "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+            "frac_bf16_peak": round(flops / (ms * 1e-3) / 1e12 / bf16_sus, 3),
+            "peak_tflops_used": bf16_sus,
+            "stage_ms_layer0": [round(v, 4) for v in st],
+            "up_tflops": round(up_flops / (st[2] * 1e-3) / 1e12, 1) if st[2] > 0 else None,
+            "down_tflops": round(dn_flops / (st[3] * 1e-3) / 1e12, 1) if st[3] > 0 else None}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_baseline(blk, inputs, seconds):
+    """The reference's CPU fake-quant path (dequantise + torch fp32 matmul) on one OLMoE
+    layer, timed on this host's cores; sample: one layer at each batch size."""
+    import numpy as np
+    import torch
+
+    from oracle import cpu_baseline as cb
+
+    layer = cb.layer_from_block(blk)
+    xs = {B: v[0].float().cpu().numpy() for B, v in inputs.items()}
+    r = cb.time_decode(layer, xs, seconds)
+    r["cores"] = torch.get_num_threads()
+    return r
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    import numpy as np
+    import torch
+
+    from oracle import cpu_baseline as cb
+
+    layer = cb.synthetic_layer(seed=1000)
+    batches = [int(b) for b in args.batches.split(",")]
+    rng = np.random.default_rng(7)
+    xs = {B: rng.standard_normal((B, layer.D)).astype(np.float16) for B in batches}
+    for i in range(args.warmup):
+        B = batches[i % len(batches)]
+        cb.decode_layer(layer, xs[B])
+    t0 = time.perf_counter()
+    total_bytes = 0
+    for i in range(args.steps):
+        B = batches[i % len(batches)]
+        total_bytes += cb.decode_layer(layer, xs[B])
+    dt = time.perf_counter() - t0
+    v = total_bytes / dt / 1e9
+    cores = torch.get_num_threads()
+    sample = (f"{args.steps} single-layer decode passes of the OLMoE-shaped layer cycling batch "
+              f"{batches}, dequantise hit experts to fp32 + torch matmul (the reference's fake-quant path)")
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "olmoe-16-layer-moe-stack-decode (BASELINE config 1), CPU sample"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        import torch
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        print(json.dumps(run_reference(args)))
+        return
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    line = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

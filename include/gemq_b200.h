@@ -1,0 +1,188 @@
+/*
+ * gemq_b200.h -- C ABI of the B200 (sm_100a) real-quant mixed-bit MoE expert path.
+ *
+ * Drop-in for the GPU entry points of RobustGEMQ's quantized-MoE module
+ * (gemq/inference/moe_block.py and gemq/triton_kernels/*.py). The reference binds
+ * these through Python/Triton; here a Python host (robustgemq_b200) binds them with
+ * ctypes, passing tensor.data_ptr() values and torch.cuda.current_stream().cuda_stream.
+ *
+ * Conventions
+ *   - Every pointer argument is device memory unless its comment says "host".
+ *   - fp16 data is passed as uint16_t bit patterns.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t) and returns a status;
+ *     the library never aborts, traps or allocates device memory. Scratch space is
+ *     passed in by the caller (sizes from the *_workspace_size queries).
+ *   - Kernels bound every internal wait; an expired wait is recorded in a device
+ *     error word read by gemq_get_device_error().
+ *   - A layer handle is thread-compatible, not thread-safe.
+ */
+#ifndef GEMQ_B200_H
+#define GEMQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GEMQ_OK 0
+#define GEMQ_ERR_INVALID_ARGUMENT 1 /* the reference raises AssertionError/ValueError here */
+#define GEMQ_ERR_UNSUPPORTED 2
+#define GEMQ_ERR_CUDA 3
+#define GEMQ_ERR_WORKSPACE 4
+
+/* Router flavours (moe_block.py:790 fp16 logits; moe_block.py:549,591 fp32 logits). */
+#define GEMQ_ROUTER_FP16 0
+#define GEMQ_ROUTER_FP32 1
+
+/* gemq_moe_forward flags */
+#define GEMQ_FWD_ONE_TOKEN 1u        /* forward_one_token rounding (moe_block.py:817-853); num_tokens == 1 */
+#define GEMQ_FWD_GIVEN_ROUTING 2u    /* use topk_idx/topk_w instead of routing */
+#define GEMQ_FWD_GIVEN_LOGITS 4u     /* router_logits is an input: skip the gate GEMM */
+#define GEMQ_FWD_FP16_SOFTMAX 8u     /* Mixtral one-token router: fp16 softmax/top-k/renorm (moe_block.py:280-283) */
+#define GEMQ_FWD_FP32_COMBINE 16u    /* one fp32 sum per token instead of per-expert fp16 rounding */
+#define GEMQ_FWD_FORCE_SIMT 32u      /* use the CUDA-core grouped GEMM (cross-checking) */
+#define GEMQ_FWD_RESIDUAL 64u        /* out = fp16(x + block(x)): the decoder layer's residual add, fused */
+#define GEMQ_FWD_TIME_STAGES 128u    /* record CUDA events around each stage (read with gemq_layer_stage_times) */
+
+/* Stage indices reported by gemq_layer_stage_times. */
+#define GEMQ_STAGE_ROUTE 0    /* gate GEMM + softmax/top-k */
+#define GEMQ_STAGE_DISPATCH 1 /* histogram, scan, permute (n-token path) */
+#define GEMQ_STAGE_UP 2       /* gate/up projection with SiLU*mul */
+#define GEMQ_STAGE_DOWN 3     /* down projection with routing weight */
+#define GEMQ_STAGE_SHARED 4   /* DeepSeek shared experts */
+#define GEMQ_STAGE_COMBINE 5  /* per-token combine (+ residual) */
+#define GEMQ_NUM_STAGES 6
+
+/*
+ * One stacked packed projection: the w1/w3/w2 attribute set built by
+ * QuantFused*MoEBlock.from_hf (moe_block.py:725-757, 178-209, 445-474, 955-987).
+ *   wq        int32 [wq_rows, n], expert e's words start at element wq_strides[e];
+ *             code (k, j) of expert e is bits ((k % eps)*b .. +b) of word row k / eps,
+ *             eps = 32 / b (gemq/triton_kernels/utils.py:33-71)
+ *   scales    fp16 [num_experts * k / group_size, n]
+ *   zeros     fp16, additive zero z' = -zero*scale (w = fma(q, s, z'), utils.py:192-212)
+ *   nbits, wq_strides, zs_strides   int32 [num_experts]
+ * The shared experts of DeepSeek (moe_block.py:477-489) are projections with
+ * num_experts == 1.
+ */
+typedef struct gemq_proj {
+  const int32_t* wq;
+  const uint16_t* scales;
+  const uint16_t* zeros;
+  const int32_t* nbits;
+  const int32_t* wq_strides;
+  const int32_t* zs_strides;
+  int64_t wq_rows;
+  int32_t num_experts;
+  int32_t k;
+  int32_t n;
+  int32_t group_size;
+} gemq_proj_t;
+
+/* Block descriptor: the constructor arguments of QuantFused*MoEBlock (moe_block.py:688-713). */
+typedef struct gemq_layer_desc {
+  int32_t hidden;          /* D */
+  int32_t inter;           /* F (per routed expert) */
+  int32_t num_experts;     /* E */
+  int32_t top_k;
+  int32_t group_size;      /* block_group_size (moe_block.py:745-749) */
+  int32_t norm_topk_prob;  /* renormalise the top-k weights (moe_block.py:794-795) */
+  int32_t router;          /* GEMQ_ROUTER_FP16 | GEMQ_ROUTER_FP32 */
+  const uint16_t* gate_weight; /* fp16 [E, D] */
+  gemq_proj_t w1, w3, w2;  /* gate_proj, up_proj, down_proj */
+  int32_t has_shared;      /* DeepSeek shared experts (moe_block.py:575, 617-620) */
+  gemq_proj_t shared_w1, shared_w3, shared_w2;
+} gemq_layer_desc_t;
+
+typedef struct gemq_layer gemq_layer_t;
+
+/* ---------------------------------------------------------------- status */
+const char* gemq_last_error_string(void); /* host string, thread-local */
+int gemq_version(void);
+/* Synchronises the device, returns the device error word (0 = none) and clears it. */
+int gemq_get_device_error(uint32_t* code_out /* host */);
+
+/* ---------------------------------------------------------------- packing */
+/* Replaces pack_weights_over_cols_triton (gemq/triton_kernels/utils.py:74-113).
+ * codes uint8 [rows, cols] -> out int32 [rows, cdiv(cols, 32/nbits)] (the buffer
+ * whose transpose the reference returns). */
+int gemq_pack_weights_over_cols(const uint8_t* codes, int64_t rows, int64_t cols, int32_t nbits,
+                                int32_t* out, void* stream);
+
+/* Replaces unpack_over_cols_triton (gemq/triton_kernels/utils.py:149-189). */
+int gemq_unpack_over_cols(const int32_t* packed, int64_t rows, int64_t packed_cols, int64_t out_cols,
+                          int32_t nbits, uint8_t* out, void* stream);
+
+/* The dequant of gemq/triton_kernels/utils.py:192-212 applied to one whole expert,
+ * addressed as in dequant_group_gemm.py:71-81,118-130: out fp16 [k, n]. */
+int gemq_dequant_expert(const gemq_proj_t* proj /* host struct */, int32_t expert, uint16_t* out,
+                        void* stream);
+
+/* ---------------------------------------------------------------- kernel-level GEMMs */
+/* Replaces dequant_group_gemm_triton (dequant_group_gemm.py:155-202):
+ * out[a] = x[m, k] @ deq(W[indices[a]]) -> fp16 [num_indices, m, n]. */
+size_t gemq_group_gemm_workspace_size(int32_t num_indices);
+int gemq_dequant_group_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t m, const int32_t* indices,
+                            int32_t num_indices, uint16_t* out, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/* Replaces dequant_gemm_triton (dequant_gemm.py:150-193); proj->num_experts == 1. */
+int gemq_dequant_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t m, uint16_t* out, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Replaces dequant_splitk_gemv_triton (dequant_gemv.py:118-156) with a deterministic
+ * reduction (no fp16 atomics); x fp16 [1, k] -> out fp16 [1, n]. */
+size_t gemq_gemv_workspace_size(const gemq_proj_t* proj, int32_t num_rows);
+int gemq_dequant_gemv(const gemq_proj_t* proj, const uint16_t* x, uint16_t* out, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Replaces fused_dequant_up_proj_triton (fused_dequant_bmm.py:122-173):
+ * x fp16 [1, k], idx int32 [num_idx] -> x1, x3 fp16 [1, num_idx * n]. w3 is read
+ * with w1's nbits/strides as the reference does (check_w1_w3_aligned). */
+int gemq_fused_up_proj(const gemq_proj_t* w1, const gemq_proj_t* w3, const uint16_t* x, const int32_t* idx,
+                       int32_t num_idx, uint16_t* x1, uint16_t* x3, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Replaces fused_dequant_down_proj_triton (fused_dequant_bmm.py:264-312):
+ * x1, x3 fp16 [1, num_idx * w2->k] -> x2 fp16 [1, num_idx * n], SiLU*mul in fp32. */
+int gemq_fused_down_proj(const gemq_proj_t* w2, const uint16_t* x1, const uint16_t* x3, const int32_t* idx,
+                         int32_t num_idx, uint16_t* x2, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* ---------------------------------------------------------------- MoE block */
+/* Validates a block (moe_block.py:196-201 single group size, 69-80 w1/w3
+ * alignment, 175-176 packed weights present) and prepares TMA descriptors.
+ * Reads nbits/strides to the host once (synchronous). */
+int gemq_layer_create(const gemq_layer_desc_t* desc /* host */, gemq_layer_t** out /* host */);
+int gemq_layer_destroy(gemq_layer_t* layer);
+
+size_t gemq_moe_workspace_size(const gemq_layer_t* layer, int64_t num_tokens, uint32_t flags);
+
+/* Router of forward_n_tokens / forward_one_token (moe_block.py:790-797, 828-833,
+ * 549-556, 280-283): logits (fp16, or fp32 for GEMQ_ROUTER_FP32) [T, E],
+ * topk_idx int32 [T, k], topk_w fp16 [T, k]. Ties go to the lower expert id. */
+int gemq_moe_route(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, void* logits, int32_t* topk_idx,
+                   uint16_t* topk_w, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The whole block: replaces QuantFused*MoEBlock.forward -> forward_n_tokens /
+ * forward_one_token (moe_block.py:781-858, 234-309, 540-628, 1011-1088).
+ *   x fp16 [T, D] -> out fp16 [T, D]
+ *   router_logits: output [T, E] (fp16 or fp32 per desc->router), may be NULL;
+ *                  an input with GEMQ_FWD_GIVEN_LOGITS (fp32 accepted for both)
+ *   topk_idx/topk_w: inputs with GEMQ_FWD_GIVEN_ROUTING, else NULL */
+int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, uint16_t* out,
+                     void* router_logits, const int32_t* topk_idx, const uint16_t* topk_w, uint32_t flags,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Durations (ms, host array of GEMQ_NUM_STAGES; 0 for stages that did not run) of
+ * the last gemq_moe_forward issued with GEMQ_FWD_TIME_STAGES; waits for it to finish.
+ * No counterpart in the reference (it has no native timing hooks). */
+int gemq_layer_stage_times(gemq_layer_t* layer, float* ms_out /* host */);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GEMQ_B200_H */

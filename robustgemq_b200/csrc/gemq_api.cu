@@ -1,0 +1,750 @@
+// C ABI of gemq-b200: validation, workspace carving and the prefill / one-token
+// pipelines of the quantized MoE block. See include/gemq_b200.h for the contract.
+#include <cuda_fp16.h>
+
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "gemq_common.cuh"
+#include "gemq_internal.h"
+
+namespace gemq {
+
+namespace {
+thread_local std::string t_last_error;
+}
+
+void set_error(const std::string& msg) { t_last_error = msg; }
+
+int device_sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+namespace {
+
+int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  set_error(std::string(where) + ": " + cudaGetErrorString(e));
+  return GEMQ_ERR_CUDA;
+}
+
+#define GEMQ_CUDA(call, where)                                    \
+  do {                                                            \
+    cudaError_t _e = (call);                                      \
+    if (_e != cudaSuccess) return cuda_fail(_e, where);           \
+  } while (0)
+
+ProjDev to_dev(const gemq_proj_t& p) {
+  ProjDev d;
+  d.wq = p.wq;
+  d.scales = p.scales;
+  d.zeros = p.zeros;
+  d.nbits = p.nbits;
+  d.wq_strides = p.wq_strides;
+  d.zs_strides = p.zs_strides;
+  d.wq_rows = p.wq_rows;
+  d.num_experts = p.num_experts;
+  d.k = p.k;
+  d.n = p.n;
+  d.group_size = p.group_size;
+  return d;
+}
+
+// Shape checks every entry point shares (the reference asserts these implicitly).
+int check_proj(const gemq_proj_t* p, const char* name) {
+  if (p == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, std::string(name) + ": null projection");
+  if (p->wq == nullptr || p->scales == nullptr || p->zeros == nullptr || p->nbits == nullptr ||
+      p->wq_strides == nullptr || p->zs_strides == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, std::string(name) + ": null device pointer");
+  if (p->num_experts <= 0 || p->k <= 0 || p->n <= 0 || p->group_size <= 0 || p->wq_rows <= 0)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, std::string(name) + ": non-positive size");
+  if (p->k % p->group_size != 0)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, std::string(name) + ": k must be a multiple of group_size");
+  if (p->n % 4 != 0) return fail(GEMQ_ERR_UNSUPPORTED, std::string(name) + ": n must be a multiple of 4");
+  return GEMQ_OK;
+}
+
+int packed_rows(int k, int nb) {
+  const int eps = 32 / nb;
+  return (k + eps - 1) / eps;
+}
+
+// Reads nbits / strides to the host and checks they describe the from_hf layout
+// (moe_block.py:737-757), so every kernel access stays inside wq / scales / zeros.
+int validate_layout(const gemq_proj_t& p, const char* name, std::vector<int32_t>* nbits_out,
+                    std::vector<int32_t>* wq_strides_out) {
+  std::vector<int32_t> nb(p.num_experts), ws(p.num_experts), zs(p.num_experts);
+  GEMQ_CUDA(cudaMemcpy(nb.data(), p.nbits, sizeof(int32_t) * p.num_experts, cudaMemcpyDeviceToHost), "copy nbits");
+  GEMQ_CUDA(cudaMemcpy(ws.data(), p.wq_strides, sizeof(int32_t) * p.num_experts, cudaMemcpyDeviceToHost),
+            "copy wq_strides");
+  GEMQ_CUDA(cudaMemcpy(zs.data(), p.zs_strides, sizeof(int32_t) * p.num_experts, cudaMemcpyDeviceToHost),
+            "copy zs_strides");
+  int64_t wq_off = 0;
+  const int64_t zs_per = static_cast<int64_t>(p.k / p.group_size) * p.n;
+  for (int e = 0; e < p.num_experts; ++e) {
+    if (nb[e] < 1 || nb[e] > 4)
+      return fail(GEMQ_ERR_UNSUPPORTED, std::string(name) + ": bit-width must be 1, 2, 3 or 4 (utils.py:83)");
+    if (ws[e] != wq_off)
+      return fail(GEMQ_ERR_INVALID_ARGUMENT, std::string(name) + ": wq_strides is not the exclusive cumsum of numel");
+    if (zs[e] != e * zs_per)
+      return fail(GEMQ_ERR_INVALID_ARGUMENT, std::string(name) + ": zs_strides is not the exclusive cumsum of numel");
+    wq_off += static_cast<int64_t>(packed_rows(p.k, nb[e])) * p.n;
+  }
+  if (wq_off > p.wq_rows * p.n)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, std::string(name) + ": wq has fewer rows than its experts need");
+  if (wq_off > INT32_MAX)
+    return fail(GEMQ_ERR_UNSUPPORTED, std::string(name) + ": int32 element offsets overflow (as in the reference)");
+  if (nbits_out) *nbits_out = nb;
+  if (wq_strides_out) *wq_strides_out = ws;
+  return GEMQ_OK;
+}
+
+// Bump allocator over the caller's workspace (256-byte aligned pieces).
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
+  template <typename T>
+  T* take(size_t count) {
+    off = (off + 255) & ~static_cast<size_t>(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += sizeof(T) * count;
+    return p;
+  }
+};
+
+int choose_nt(int64_t rows_per_expert) { return rows_per_expert > 48 ? kNtLarge : kNtSmall; }
+
+// Runs one grouped GEMM, tensor cores when the shape allows, CUDA cores otherwise.
+// The segments must have been built with the nt this returns through `nt_used`.
+bool use_tc(const GemmArgs& a, bool force_simt) { return !force_simt && tc_gemm_supported(a); }
+
+int run_gemm(GemmArgs a, bool force_simt, cudaStream_t s, const char* what) {
+  cudaError_t e = use_tc(a, force_simt) ? launch_tc_gemm(a, s) : launch_simt_gemm(a, s);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return GEMQ_OK;
+}
+
+}  // namespace
+}  // namespace gemq
+
+using namespace gemq;
+
+struct gemq_layer {
+  gemq_layer_desc_t d;
+  ProjDev w1, w3, w2, sw1, sw3, sw2;
+  ProjDev w3_as_w1;  // w3 read with w1's nbits/strides (one-token path, fused_dequant_bmm.py:98)
+  int num_sms;
+  int shared_inter;
+  // optional stage timing (GEMQ_FWD_TIME_STAGES)
+  bool events_ready = false;
+  cudaEvent_t ev[2 * GEMQ_NUM_STAGES];
+  bool stage_ran[GEMQ_NUM_STAGES] = {};
+};
+
+namespace gemq {
+namespace {
+// Records events around pipeline stages when timing is requested.
+struct StageTimer {
+  gemq_layer_t* L;
+  cudaStream_t s;
+  bool on;
+  StageTimer(gemq_layer_t* layer, cudaStream_t stream, uint32_t flags)
+      : L(layer), s(stream), on((flags & GEMQ_FWD_TIME_STAGES) != 0) {
+    if (!on) return;
+    if (!L->events_ready) {
+      for (auto& e : L->ev) cudaEventCreate(&e);
+      L->events_ready = true;
+    }
+    for (bool& r : L->stage_ran) r = false;
+  }
+  void begin(int st) {
+    if (on) cudaEventRecord(L->ev[2 * st], s);
+  }
+  void end(int st) {
+    if (!on) return;
+    cudaEventRecord(L->ev[2 * st + 1], s);
+    L->stage_ran[st] = true;
+  }
+};
+}  // namespace
+}  // namespace gemq
+
+extern "C" {
+
+const char* gemq_last_error_string(void) { return t_last_error.c_str(); }
+
+int gemq_version(void) { return 1; }
+
+int gemq_get_device_error(uint32_t* code_out) {
+  if (code_out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null output");
+  GEMQ_CUDA(cudaDeviceSynchronize(), "synchronize");
+  uint32_t v = 0;
+  GEMQ_CUDA(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)), "read device error");
+  const uint32_t zero = 0;
+  GEMQ_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)), "clear device error");
+  *code_out = v;
+  return GEMQ_OK;
+}
+
+int gemq_pack_weights_over_cols(const uint8_t* codes, int64_t rows, int64_t cols, int32_t nbits, int32_t* out,
+                                void* stream) {
+  if (nbits < 1 || nbits > 4) return fail(GEMQ_ERR_INVALID_ARGUMENT, "Untested quantization bitwidth (utils.py:83)");
+  if (rows < 0 || cols < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative size");
+  if (rows * cols > 0 && (codes == nullptr || out == nullptr)) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
+  GEMQ_CUDA(launch_pack(codes, rows, cols, nbits, out, static_cast<cudaStream_t>(stream)), "pack");
+  return GEMQ_OK;
+}
+
+int gemq_unpack_over_cols(const int32_t* packed, int64_t rows, int64_t packed_cols, int64_t out_cols, int32_t nbits,
+                          uint8_t* out, void* stream) {
+  if (nbits < 1 || nbits > 4) return fail(GEMQ_ERR_INVALID_ARGUMENT, "Untested quantization bitwidth (utils.py:83)");
+  if (rows < 0 || out_cols < 0 || packed_cols < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative size");
+  const int eps = 32 / nbits;
+  if ((out_cols + eps - 1) / eps > packed_cols)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "out_cols needs more packed columns than given");
+  if (rows * out_cols > 0 && (packed == nullptr || out == nullptr)) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
+  GEMQ_CUDA(launch_unpack(packed, rows, packed_cols, out_cols, nbits, out, static_cast<cudaStream_t>(stream)), "unpack");
+  return GEMQ_OK;
+}
+
+int gemq_dequant_expert(const gemq_proj_t* proj, int32_t expert, uint16_t* out, void* stream) {
+  if (int rc = check_proj(proj, "proj")) return rc;
+  if (expert < 0 || expert >= proj->num_experts) return fail(GEMQ_ERR_INVALID_ARGUMENT, "expert out of range");
+  if (out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null output");
+  GEMQ_CUDA(launch_dequant_expert(to_dev(*proj), expert, out, static_cast<cudaStream_t>(stream)), "dequant");
+  return GEMQ_OK;
+}
+
+size_t gemq_group_gemm_workspace_size(int32_t num_indices) {
+  Carver c(nullptr);
+  c.take<Seg>(num_indices > 0 ? num_indices : 1);
+  c.take<int32_t>(num_indices + 1);
+  return c.off + 256;
+}
+
+int gemq_dequant_group_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t m, const int32_t* indices,
+                            int32_t num_indices, uint16_t* out, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (int rc = check_proj(proj, "proj")) return rc;
+  if (num_indices <= 0 || num_indices > 1023) return fail(GEMQ_ERR_INVALID_ARGUMENT, "num_indices must be in [1, 1023]");
+  if (m < 0 || m > INT32_MAX / 2) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad m");
+  if (m == 0) return GEMQ_OK;
+  if (x == nullptr || out == nullptr || indices == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (workspace_bytes < gemq_group_gemm_workspace_size(num_indices) || workspace == nullptr)
+    return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Carver c(workspace);
+  Seg* segs = c.take<Seg>(num_indices);
+  int32_t* tp = c.take<int32_t>(num_indices + 1);
+  GemmArgs a{};
+  a.mode = GemmMode::kStoreF16;
+  a.w0 = to_dev(*proj);
+  a.w1 = a.w0;
+  a.act = x;
+  a.act_rows = m;
+  a.segs = segs;
+  a.tile_prefix = tp;
+  a.num_segs = num_indices;
+  a.out = out;
+  a.out_ld = proj->n;
+  a.out_cols = proj->n;
+  a.num_sms = device_sm_count();
+  a.nt = choose_nt(m);
+  if (!tc_gemm_supported(a)) a.nt = 32;
+  GEMQ_CUDA(launch_build_index_segs(indices, num_indices, m, a.nt, segs, tp, s), "segments");
+  return run_gemm(a, false, s, "dequant_group_gemm");
+}
+
+int gemq_dequant_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t m, uint16_t* out, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if (int rc = check_proj(proj, "proj")) return rc;
+  if (proj->num_experts != 1) return fail(GEMQ_ERR_INVALID_ARGUMENT, "dequant_gemm takes a single weight");
+  if (m <= 0) return m == 0 ? GEMQ_OK : fail(GEMQ_ERR_INVALID_ARGUMENT, "bad m");
+  if (x == nullptr || out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (workspace_bytes < gemq_group_gemm_workspace_size(1) || workspace == nullptr)
+    return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Carver c(workspace);
+  Seg* segs = c.take<Seg>(1);
+  int32_t* tp = c.take<int32_t>(2);
+  GemmArgs a{};
+  a.mode = GemmMode::kStoreF16;
+  a.w0 = to_dev(*proj);
+  a.w1 = a.w0;
+  a.act = x;
+  a.act_rows = m;
+  a.segs = segs;
+  a.tile_prefix = tp;
+  a.num_segs = 1;
+  a.out = out;
+  a.out_ld = proj->n;
+  a.out_cols = proj->n;
+  a.num_sms = device_sm_count();
+  a.nt = choose_nt(m);
+  if (!tc_gemm_supported(a)) a.nt = 32;
+  GEMQ_CUDA(launch_build_index_segs(nullptr, 1, m, a.nt, segs, tp, s), "segments");
+  return run_gemm(a, false, s, "dequant_gemm");
+}
+
+size_t gemq_gemv_workspace_size(const gemq_proj_t* proj, int32_t num_rows) {
+  if (proj == nullptr || num_rows <= 0) return 0;
+  const int splits = gemv_default_splits(proj->k, proj->n, num_rows, device_sm_count());
+  Carver c(nullptr);
+  c.take<float>(static_cast<size_t>(splits) * num_rows * proj->n);
+  c.take<float>(static_cast<size_t>(splits) * num_rows * proj->n);
+  return c.off + 256;
+}
+
+int gemq_dequant_gemv(const gemq_proj_t* proj, const uint16_t* x, uint16_t* out, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if (int rc = check_proj(proj, "proj")) return rc;
+  if (proj->num_experts != 1) return fail(GEMQ_ERR_INVALID_ARGUMENT, "dequant_gemv takes a single weight");
+  if (x == nullptr || out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (workspace == nullptr || workspace_bytes < gemq_gemv_workspace_size(proj, 1))
+    return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int splits = gemv_default_splits(proj->k, proj->n, 1, device_sm_count());
+  Carver c(workspace);
+  float* part = c.take<float>(static_cast<size_t>(splits) * proj->n);
+  GEMQ_CUDA(launch_gemv_partials(to_dev(*proj), nullptr, 1, x, 0, nullptr, part, splits, s), "gemv");
+  GEMQ_CUDA(launch_gemv_reduce(part, splits, 1, proj->n, out, s), "gemv reduce");
+  return GEMQ_OK;
+}
+
+int gemq_fused_up_proj(const gemq_proj_t* w1, const gemq_proj_t* w3, const uint16_t* x, const int32_t* idx,
+                       int32_t num_idx, uint16_t* x1, uint16_t* x3, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  if (int rc = check_proj(w1, "w1")) return rc;
+  if (int rc = check_proj(w3, "w3")) return rc;
+  if (w1->k != w3->k || w1->n != w3->n || w1->num_experts != w3->num_experts || w1->group_size != w3->group_size)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "w1 and w3 shapes differ");
+  if (num_idx <= 0 || x == nullptr || idx == nullptr || x1 == nullptr || x3 == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad arguments");
+  if (workspace == nullptr || workspace_bytes < gemq_gemv_workspace_size(w1, num_idx))
+    return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int splits = gemv_default_splits(w1->k, w1->n, num_idx, device_sm_count());
+  Carver c(workspace);
+  float* p1 = c.take<float>(static_cast<size_t>(splits) * num_idx * w1->n);
+  float* p3 = c.take<float>(static_cast<size_t>(splits) * num_idx * w1->n);
+  ProjDev d1 = to_dev(*w1), d3 = to_dev(*w3);
+  d3.nbits = d1.nbits;            // fused_dequant_bmm.py:55-57: w3 read with w1's nbits
+  d3.wq_strides = d1.wq_strides;  // and w1's word offsets (check_w1_w3_aligned)
+  GEMQ_CUDA(launch_gemv_partials(d1, idx, num_idx, x, 0, nullptr, p1, splits, s), "up w1");
+  GEMQ_CUDA(launch_gemv_partials(d3, idx, num_idx, x, 0, nullptr, p3, splits, s), "up w3");
+  GEMQ_CUDA(launch_gemv_reduce(p1, splits, num_idx, w1->n, x1, s), "reduce x1");
+  GEMQ_CUDA(launch_gemv_reduce(p3, splits, num_idx, w1->n, x3, s), "reduce x3");
+  return GEMQ_OK;
+}
+
+int gemq_fused_down_proj(const gemq_proj_t* w2, const uint16_t* x1, const uint16_t* x3, const int32_t* idx,
+                         int32_t num_idx, uint16_t* x2, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_proj(w2, "w2")) return rc;
+  if (num_idx <= 0 || x1 == nullptr || x3 == nullptr || idx == nullptr || x2 == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad arguments");
+  if (workspace == nullptr || workspace_bytes < gemq_gemv_workspace_size(w2, num_idx))
+    return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int splits = gemv_default_splits(w2->k, w2->n, num_idx, device_sm_count());
+  Carver c(workspace);
+  float* p = c.take<float>(static_cast<size_t>(splits) * num_idx * w2->n);
+  GEMQ_CUDA(launch_gemv_partials(to_dev(*w2), idx, num_idx, x1, w2->k, x3, p, splits, s), "down");
+  GEMQ_CUDA(launch_gemv_reduce(p, splits, num_idx, w2->n, x2, s), "reduce x2");
+  return GEMQ_OK;
+}
+
+// ------------------------------------------------------------------ layer
+int gemq_layer_create(const gemq_layer_desc_t* desc, gemq_layer_t** out) {
+  if (desc == nullptr || out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  const gemq_layer_desc_t& d = *desc;
+  if (d.hidden <= 0 || d.inter <= 0 || d.num_experts <= 0 || d.top_k <= 0 || d.group_size <= 0)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "non-positive block dimension");
+  if (d.top_k > d.num_experts || d.top_k > 16) return fail(GEMQ_ERR_UNSUPPORTED, "top_k must be <= min(E, 16)");
+  if (d.num_experts > 256) return fail(GEMQ_ERR_UNSUPPORTED, "at most 256 experts");
+  if (d.hidden % 8 != 0) return fail(GEMQ_ERR_UNSUPPORTED, "hidden size must be a multiple of 8");
+  if (d.gate_weight == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null gate weight");
+  if (d.router != GEMQ_ROUTER_FP16 && d.router != GEMQ_ROUTER_FP32)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "unknown router flavour");
+  if (int rc = check_proj(&d.w1, "w1")) return rc;
+  if (int rc = check_proj(&d.w3, "w3")) return rc;
+  if (int rc = check_proj(&d.w2, "w2")) return rc;
+  const gemq_proj_t* ps[3] = {&d.w1, &d.w3, &d.w2};
+  for (const gemq_proj_t* p : ps) {
+    if (p->num_experts != d.num_experts) return fail(GEMQ_ERR_INVALID_ARGUMENT, "projection expert count differs");
+    if (p->group_size != d.group_size)
+      return fail(GEMQ_ERR_INVALID_ARGUMENT, "Group sizes must be the same across all experts. (moe_block.py:200)");
+  }
+  if (d.w1.k != d.hidden || d.w1.n != d.inter || d.w3.k != d.hidden || d.w3.n != d.inter || d.w2.k != d.inter ||
+      d.w2.n != d.hidden)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "projection shapes do not match hidden/inter");
+  std::vector<int32_t> nb1, nb3, ws1, ws3;
+  if (int rc = validate_layout(d.w1, "w1", &nb1, &ws1)) return rc;
+  if (int rc = validate_layout(d.w3, "w3", &nb3, &ws3)) return rc;
+  if (int rc = validate_layout(d.w2, "w2", nullptr, nullptr)) return rc;
+  if (nb1 != nb3)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT,
+                "w1 and w3 must share bit-widths: forward_one_token indexes w3 with w1's nbits (moe_block.py:75-77)");
+  if (ws1 != ws3)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT,
+                "w1 and w3 must share packed strides: forward_one_token reads w3 at w1's offsets (moe_block.py:78-80)");
+  int shared_inter = 0;
+  if (d.has_shared) {
+    const gemq_proj_t* ss[3] = {&d.shared_w1, &d.shared_w3, &d.shared_w2};
+    const char* names[3] = {"shared_w1", "shared_w3", "shared_w2"};
+    for (int i = 0; i < 3; ++i) {
+      if (int rc = check_proj(ss[i], names[i])) return rc;
+      if (ss[i]->num_experts != 1) return fail(GEMQ_ERR_INVALID_ARGUMENT, "shared projections hold one weight");
+      if (int rc = validate_layout(*ss[i], names[i], nullptr, nullptr)) return rc;
+    }
+    shared_inter = d.shared_w1.n;
+    if (d.shared_w1.k != d.hidden || d.shared_w3.k != d.hidden || d.shared_w3.n != shared_inter ||
+        d.shared_w2.k != shared_inter || d.shared_w2.n != d.hidden)
+      return fail(GEMQ_ERR_INVALID_ARGUMENT, "shared expert shapes do not match");
+  }
+  gemq_layer_t* L = new gemq_layer();
+  L->d = d;
+  L->w1 = to_dev(d.w1);
+  L->w3 = to_dev(d.w3);
+  L->w2 = to_dev(d.w2);
+  L->w3_as_w1 = L->w3;
+  L->w3_as_w1.nbits = L->w1.nbits;
+  L->w3_as_w1.wq_strides = L->w1.wq_strides;
+  if (d.has_shared) {
+    L->sw1 = to_dev(d.shared_w1);
+    L->sw3 = to_dev(d.shared_w3);
+    L->sw2 = to_dev(d.shared_w2);
+  }
+  L->num_sms = device_sm_count();
+  L->shared_inter = shared_inter;
+  *out = L;
+  return GEMQ_OK;
+}
+
+int gemq_layer_destroy(gemq_layer_t* layer) {
+  if (layer != nullptr && layer->events_ready) {
+    for (auto& e : layer->ev) cudaEventDestroy(e);
+  }
+  delete layer;
+  return GEMQ_OK;
+}
+
+}  // extern "C"
+
+namespace gemq {
+namespace {
+
+struct FwdBufs {
+  void* logits = nullptr;
+  int32_t* topk_idx = nullptr;
+  uint16_t* topk_w = nullptr;
+  int32_t *counts = nullptr, *cursor = nullptr, *tile_prefix = nullptr, *slot_pos = nullptr;
+  Seg* segs = nullptr;
+  Seg* one_seg = nullptr;
+  int32_t* one_tp = nullptr;
+  uint16_t *w_perm = nullptr, *x_perm = nullptr, *h_perm = nullptr, *y_perm = nullptr;
+  uint16_t *s_h = nullptr, *s_out = nullptr;
+  float *part_up = nullptr, *part_dn = nullptr, *part_s = nullptr, *part_s2 = nullptr;
+  uint16_t *x1 = nullptr, *x3 = nullptr, *x2 = nullptr, *s1 = nullptr, *s3 = nullptr, *sh = nullptr, *s2 = nullptr;
+  size_t bytes = 0;
+  int splits_up = 1, splits_dn = 1, splits_s = 1, splits_s2 = 1;
+};
+
+// One carving routine both sizes (base == nullptr) and lays out the workspace.
+FwdBufs carve(const gemq_layer_t* L, int64_t T, uint32_t flags, void* base, const void* given_logits) {
+  const gemq_layer_desc_t& d = L->d;
+  const int E = d.num_experts, k = d.top_k, D = d.hidden, F = d.inter, Fs = L->shared_inter;
+  const int64_t P = T * k;
+  FwdBufs b;
+  Carver c(base);
+  const bool given_routing = (flags & GEMQ_FWD_GIVEN_ROUTING) != 0;
+  (void)given_logits;
+  b.logits = c.take<float>(static_cast<size_t>(T) * E);
+  if (!given_routing) {
+    b.topk_idx = c.take<int32_t>(P);
+    b.topk_w = c.take<uint16_t>(P);
+  }
+  b.one_seg = c.take<Seg>(1);
+  b.one_tp = c.take<int32_t>(2);
+  if (flags & GEMQ_FWD_ONE_TOKEN) {
+    b.splits_up = gemv_default_splits(D, F, k, L->num_sms);
+    b.splits_dn = gemv_default_splits(F, D, k, L->num_sms);
+    b.part_up = c.take<float>(2ull * b.splits_up * k * F);
+    b.x1 = c.take<uint16_t>(static_cast<size_t>(k) * F);
+    b.x3 = c.take<uint16_t>(static_cast<size_t>(k) * F);
+    b.part_dn = c.take<float>(static_cast<size_t>(b.splits_dn) * k * D);
+    b.x2 = c.take<uint16_t>(static_cast<size_t>(k) * D);
+    if (d.has_shared) {
+      b.splits_s = gemv_default_splits(D, Fs, 1, L->num_sms);
+      b.splits_s2 = gemv_default_splits(Fs, D, 1, L->num_sms);
+      b.part_s = c.take<float>(2ull * b.splits_s * Fs);
+      b.s1 = c.take<uint16_t>(Fs);
+      b.s3 = c.take<uint16_t>(Fs);
+      b.sh = c.take<uint16_t>(Fs);
+      b.part_s2 = c.take<float>(static_cast<size_t>(b.splits_s2) * D);
+      b.s2 = c.take<uint16_t>(D);
+    }
+  } else {
+    b.counts = c.take<int32_t>(E);
+    b.cursor = c.take<int32_t>(E);
+    b.segs = c.take<Seg>(E);
+    b.tile_prefix = c.take<int32_t>(E + 1);
+    b.slot_pos = c.take<int32_t>(P);
+    b.w_perm = c.take<uint16_t>(P);
+    b.x_perm = c.take<uint16_t>(static_cast<size_t>(P) * D);
+    b.h_perm = c.take<uint16_t>(static_cast<size_t>(P) * F);
+    b.y_perm = c.take<uint16_t>(static_cast<size_t>(P) * D);
+    if (d.has_shared) {
+      b.s_h = c.take<uint16_t>(static_cast<size_t>(T) * Fs);
+      b.s_out = c.take<uint16_t>(static_cast<size_t>(T) * D);
+    }
+  }
+  b.bytes = c.off + 256;
+  return b;
+}
+
+// logits -> top-k (or nothing when routing is given)
+int run_router(gemq_layer_t* L, const uint16_t* x, int64_t T, void* logits_out, bool logits_given, int32_t* idx,
+               uint16_t* w, uint32_t flags, Seg* one_seg, int32_t* one_tp, cudaStream_t s, StageTimer* tm = nullptr) {
+  if (tm) tm->begin(GEMQ_STAGE_ROUTE);
+  const gemq_layer_desc_t& d = L->d;
+  const bool fp32_logits = logits_given || d.router == GEMQ_ROUTER_FP32;
+  if (!logits_given) {
+    GemmArgs a{};
+    a.mode = d.router == GEMQ_ROUTER_FP32 ? GemmMode::kDenseF32 : GemmMode::kDenseF16;
+    a.w0.k = d.hidden;
+    a.w0.n = d.num_experts;
+    a.w0.num_experts = 1;
+    a.w0.group_size = 64;
+    a.w1 = a.w0;
+    a.dense_a = d.gate_weight;
+    a.act = x;
+    a.act_rows = T;
+    a.num_segs = 1;
+    a.segs = one_seg;
+    a.tile_prefix = one_tp;
+    a.out = logits_out;
+    a.out_ld = d.num_experts;
+    a.out_cols = d.num_experts;
+    a.num_sms = L->num_sms;
+    a.nt = choose_nt(T);
+    const bool tc = T >= 64 && !(flags & GEMQ_FWD_FORCE_SIMT) && tc_gemm_supported(a);
+    if (tc) {
+      GEMQ_CUDA(launch_build_index_segs(nullptr, 1, T, a.nt, one_seg, one_tp, s), "router segments");
+      GEMQ_CUDA(launch_tc_gemm(a, s), "router gemm");
+    } else {
+      GEMQ_CUDA(launch_router_simt(x, T, d.gate_weight, d.num_experts, d.hidden, d.router == GEMQ_ROUTER_FP32,
+                                   logits_out, s),
+                "router");
+    }
+  }
+  GEMQ_CUDA(launch_topk(logits_out, fp32_logits, T, d.num_experts, d.top_k, d.norm_topk_prob != 0,
+                        (flags & GEMQ_FWD_FP16_SOFTMAX) != 0, idx, w, s),
+            "topk");
+  if (tm) tm->end(GEMQ_STAGE_ROUTE);
+  return GEMQ_OK;
+}
+
+int forward_one_token(gemq_layer_t* L, const uint16_t* x, uint16_t* out, const int32_t* idx, const uint16_t* w,
+                      uint32_t flags, FwdBufs& b, cudaStream_t s, StageTimer& tm) {
+  const uint16_t* residual = (flags & GEMQ_FWD_RESIDUAL) ? x : nullptr;
+  const gemq_layer_desc_t& d = L->d;
+  const int k = d.top_k, D = d.hidden, F = d.inter;
+  float* p1 = b.part_up;
+  float* p3 = b.part_up + static_cast<size_t>(b.splits_up) * k * F;
+  tm.begin(GEMQ_STAGE_UP);
+  GEMQ_CUDA(launch_gemv_partials(L->w1, idx, k, x, 0, nullptr, p1, b.splits_up, s), "up w1");
+  GEMQ_CUDA(launch_gemv_partials(L->w3_as_w1, idx, k, x, 0, nullptr, p3, b.splits_up, s), "up w3");
+  GEMQ_CUDA(launch_gemv_reduce(p1, b.splits_up, k, F, b.x1, s), "x1");
+  GEMQ_CUDA(launch_gemv_reduce(p3, b.splits_up, k, F, b.x3, s), "x3");
+  tm.end(GEMQ_STAGE_UP);
+  tm.begin(GEMQ_STAGE_DOWN);
+  GEMQ_CUDA(launch_gemv_partials(L->w2, idx, k, b.x1, F, b.x3, b.part_dn, b.splits_dn, s), "down");
+  GEMQ_CUDA(launch_gemv_reduce(b.part_dn, b.splits_dn, k, D, b.x2, s), "x2");
+  tm.end(GEMQ_STAGE_DOWN);
+  const uint16_t* add = nullptr;
+  if (d.has_shared) {
+    const int Fs = L->shared_inter;
+    tm.begin(GEMQ_STAGE_SHARED);
+    float* q1 = b.part_s;
+    float* q3 = b.part_s + static_cast<size_t>(b.splits_s) * Fs;
+    GEMQ_CUDA(launch_gemv_partials(L->sw1, nullptr, 1, x, 0, nullptr, q1, b.splits_s, s), "shared w1");
+    GEMQ_CUDA(launch_gemv_partials(L->sw3, nullptr, 1, x, 0, nullptr, q3, b.splits_s, s), "shared w3");
+    GEMQ_CUDA(launch_gemv_reduce(q1, b.splits_s, 1, Fs, b.s1, s), "s1");
+    GEMQ_CUDA(launch_gemv_reduce(q3, b.splits_s, 1, Fs, b.s3, s), "s3");
+    GEMQ_CUDA(launch_swiglu_f16(b.s1, b.s3, Fs, b.sh, s), "shared swiglu");
+    GEMQ_CUDA(launch_gemv_partials(L->sw2, nullptr, 1, b.sh, 0, nullptr, b.part_s2, b.splits_s2, s), "shared w2");
+    GEMQ_CUDA(launch_gemv_reduce(b.part_s2, b.splits_s2, 1, D, b.s2, s), "s2");
+    tm.end(GEMQ_STAGE_SHARED);
+    add = b.s2;
+  }
+  tm.begin(GEMQ_STAGE_COMBINE);
+  GEMQ_CUDA(launch_decode_combine(b.x2, w, k, D, add, residual, out, s), "combine");
+  tm.end(GEMQ_STAGE_COMBINE);
+  return GEMQ_OK;
+}
+
+int forward_n_tokens(gemq_layer_t* L, const uint16_t* x, int64_t T, uint16_t* out, const int32_t* idx,
+                     const uint16_t* w, uint32_t flags, FwdBufs& b, cudaStream_t s, StageTimer& tm) {
+  const gemq_layer_desc_t& d = L->d;
+  const int E = d.num_experts, k = d.top_k, D = d.hidden, F = d.inter;
+  const int64_t P = T * k;
+  const bool force_simt = (flags & GEMQ_FWD_FORCE_SIMT) != 0;
+  GemmArgs up{};
+  up.mode = GemmMode::kSwiGLU;
+  up.w0 = L->w1;
+  up.w1 = L->w3;
+  up.act = b.x_perm;
+  up.act_rows = P;
+  up.segs = b.segs;
+  up.tile_prefix = b.tile_prefix;
+  up.num_segs = E;
+  up.out = b.h_perm;
+  up.out_ld = F;
+  up.out_cols = F;
+  up.num_sms = L->num_sms;
+  up.nt = choose_nt(P / E);
+  GemmArgs dn = up;
+  dn.mode = GemmMode::kRouteWeight;
+  dn.w0 = L->w2;
+  dn.w1 = L->w2;
+  dn.act = b.h_perm;
+  dn.out = b.y_perm;
+  dn.out_ld = D;
+  dn.out_cols = D;
+  dn.row_weight = b.w_perm;
+  const bool tc = !force_simt && tc_gemm_supported(up) && tc_gemm_supported(dn);
+  if (!tc) up.nt = dn.nt = 32;
+  tm.begin(GEMQ_STAGE_DISPATCH);
+  GEMQ_CUDA(launch_dispatch(idx, w, x, T, k, E, D, up.nt, b.counts, b.cursor, b.segs, b.tile_prefix, b.slot_pos,
+                            b.w_perm, b.x_perm, s),
+            "dispatch");
+  tm.end(GEMQ_STAGE_DISPATCH);
+  tm.begin(GEMQ_STAGE_UP);
+  if (int rc = run_gemm(up, !tc, s, "up projection")) return rc;
+  tm.end(GEMQ_STAGE_UP);
+  tm.begin(GEMQ_STAGE_DOWN);
+  if (int rc = run_gemm(dn, !tc, s, "down projection")) return rc;
+  tm.end(GEMQ_STAGE_DOWN);
+  const uint16_t* add = nullptr;
+  if (d.has_shared) {
+    const int Fs = L->shared_inter;
+    GemmArgs su{};
+    su.mode = GemmMode::kSwiGLU;
+    su.w0 = L->sw1;
+    su.w1 = L->sw3;
+    su.act = x;
+    su.act_rows = T;
+    su.segs = b.one_seg;
+    su.tile_prefix = b.one_tp;
+    su.num_segs = 1;
+    su.out = b.s_h;
+    su.out_ld = Fs;
+    su.out_cols = Fs;
+    su.num_sms = L->num_sms;
+    su.nt = choose_nt(T);
+    GemmArgs sd = su;
+    sd.mode = GemmMode::kStoreF16;
+    sd.w0 = sd.w1 = L->sw2;
+    sd.act = b.s_h;
+    sd.out = b.s_out;
+    sd.out_ld = D;
+    sd.out_cols = D;
+    const bool stc = !force_simt && tc_gemm_supported(su) && tc_gemm_supported(sd);
+    if (!stc) su.nt = sd.nt = 32;
+    tm.begin(GEMQ_STAGE_SHARED);
+    GEMQ_CUDA(launch_build_index_segs(nullptr, 1, T, su.nt, b.one_seg, b.one_tp, s), "shared segments");
+    if (int rc = run_gemm(su, !stc, s, "shared up")) return rc;
+    if (int rc = run_gemm(sd, !stc, s, "shared down")) return rc;
+    tm.end(GEMQ_STAGE_SHARED);
+    add = b.s_out;
+  }
+  tm.begin(GEMQ_STAGE_COMBINE);
+  GEMQ_CUDA(launch_combine(b.y_perm, b.slot_pos, idx, T, k, D, (flags & GEMQ_FWD_FP32_COMBINE) != 0, add,
+                           (flags & GEMQ_FWD_RESIDUAL) ? x : nullptr, out, s),
+            "combine");
+  tm.end(GEMQ_STAGE_COMBINE);
+  return GEMQ_OK;
+}
+
+}  // namespace
+}  // namespace gemq
+
+extern "C" {
+
+size_t gemq_moe_workspace_size(const gemq_layer_t* layer, int64_t num_tokens, uint32_t flags) {
+  if (layer == nullptr || num_tokens < 0) return 0;
+  return carve(layer, num_tokens, flags, nullptr, nullptr).bytes;
+}
+
+int gemq_moe_route(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, void* logits, int32_t* topk_idx,
+                   uint16_t* topk_w, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
+  if (layer == nullptr || x == nullptr || logits == nullptr || topk_idx == nullptr || topk_w == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  if (num_tokens < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative token count");
+  if (num_tokens == 0) return GEMQ_OK;
+  Carver c(workspace);
+  Seg* seg = c.take<Seg>(1);
+  int32_t* tp = c.take<int32_t>(2);
+  if (workspace == nullptr || workspace_bytes < c.off + 256) return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
+  return run_router(layer, x, num_tokens, logits, (flags & GEMQ_FWD_GIVEN_LOGITS) != 0, topk_idx, topk_w, flags, seg,
+                    tp, static_cast<cudaStream_t>(stream));
+}
+
+int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, uint16_t* out, void* router_logits,
+                     const int32_t* topk_idx, const uint16_t* topk_w, uint32_t flags, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (layer == nullptr || x == nullptr || out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  if (num_tokens < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative token count");
+  if (num_tokens == 0) return GEMQ_OK;
+  const bool one = (flags & GEMQ_FWD_ONE_TOKEN) != 0;
+  if (one && num_tokens != 1)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT,
+                "This function only supports single token forward (moe_block.py:825)");
+  const bool given_routing = (flags & GEMQ_FWD_GIVEN_ROUTING) != 0;
+  const bool given_logits = (flags & GEMQ_FWD_GIVEN_LOGITS) != 0;
+  if (given_routing && (topk_idx == nullptr || topk_w == nullptr))
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "GEMQ_FWD_GIVEN_ROUTING needs topk_idx and topk_w");
+  if (given_logits && router_logits == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "GEMQ_FWD_GIVEN_LOGITS needs router_logits");
+  if (num_tokens * layer->d.top_k > INT32_MAX / 2) return fail(GEMQ_ERR_UNSUPPORTED, "too many tokens");
+  FwdBufs b = carve(layer, num_tokens, flags, workspace, router_logits);
+  if (workspace == nullptr || workspace_bytes < b.bytes) return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  StageTimer tm(layer, s, flags);
+  const int32_t* idx = topk_idx;
+  const uint16_t* w = topk_w;
+  if (!given_routing) {
+    void* logits = (router_logits != nullptr) ? router_logits : b.logits;
+    if (int rc = run_router(layer, x, num_tokens, logits, given_logits, b.topk_idx, b.topk_w, flags, b.one_seg,
+                            b.one_tp, s, &tm))
+      return rc;
+    idx = b.topk_idx;
+    w = b.topk_w;
+  }
+  if (one) return forward_one_token(layer, x, out, idx, w, flags, b, s, tm);
+  return forward_n_tokens(layer, x, num_tokens, out, idx, w, flags, b, s, tm);
+}
+
+int gemq_layer_stage_times(gemq_layer_t* layer, float* ms_out) {
+  if (layer == nullptr || ms_out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  for (int st = 0; st < GEMQ_NUM_STAGES; ++st) ms_out[st] = 0.f;
+  if (!layer->events_ready) return GEMQ_OK;
+  for (int st = 0; st < GEMQ_NUM_STAGES; ++st) {
+    if (!layer->stage_ran[st]) continue;
+    GEMQ_CUDA(cudaEventSynchronize(layer->ev[2 * st + 1]), "stage event");
+    GEMQ_CUDA(cudaEventElapsedTime(&ms_out[st], layer->ev[2 * st], layer->ev[2 * st + 1]), "stage time");
+  }
+  return GEMQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,240 @@
+// Shared device helpers for the gemq-b200 kernels (sm_100a only).
+//
+// * bounded mbarrier waits: every spin gives up after a wall-clock limit, records
+//   where in the device error word and returns false, so no kernel can hang the GPU;
+// * TMA (cp.async.bulk.tensor, no multicast), tcgen05 (MMA, TMEM alloc/ld, commit);
+// * UMMA shared-memory / instruction descriptors for kind::f16 with f32 accumulate;
+// * the packed-code -> fp16 dequant that reproduces the reference exactly:
+//   w = fma.rn.f16(fp16(q), s, z')  (gemq/triton_kernels/utils.py:206-210).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#if !defined(__CUDA_ARCH__) || (__CUDA_ARCH__ >= 1000)
+#else
+#error "gemq-b200 kernels target sm_100a only"
+#endif
+
+namespace gemq {
+
+// ------------------------------------------------------------------ device error word
+// Bit layout of the error word: low 8 bits = error kind, upper bits = site id.
+enum DeviceError : uint32_t {
+  kDevOk = 0,
+  kDevTimeoutTmaFull = 1,
+  kDevTimeoutTmaEmpty = 2,
+  kDevTimeoutAFull = 3,
+  kDevTimeoutAEmpty = 4,
+  kDevTimeoutAccFull = 5,
+  kDevTimeoutAccEmpty = 6,
+  kDevTimeoutDrain = 7,
+  kDevBadExpert = 8,
+  kDevBadBits = 9,
+};
+
+extern __device__ uint32_t g_device_error;
+
+__device__ __forceinline__ void set_device_error(uint32_t code) { atomicCAS(&g_device_error, 0u, code); }
+__device__ __forceinline__ bool device_error_set() {
+  return *((volatile uint32_t*)&g_device_error) != 0u;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wall-clock limit for any single wait inside a kernel (2 s). A healthy wait in
+// these kernels lasts microseconds.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------ mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits until the phase with the given parity has completed. Returns false (and
+// records `code`) if the wait exceeds kWaitLimitNs, or if another thread already
+// recorded an error (so a failed pipeline drains instead of spinning).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(a, parity)) return true;
+    if ((it & 63u) == 0u) {
+      if (device_error_set()) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_device_error(code);
+        return false;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ TMA (no multicast)
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
+                                            int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ------------------------------------------------------------------ tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, one CTA.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives on `bar` once all previously issued tcgen05.mma of this thread completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns; thread i of the warp gets lane (base+i).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, K-major operand in the canonical 128-byte
+// swizzle: rows of 64 fp16 (128 B), 8-row atoms of 1024 B stacked along M/N.
+// Fields per the sm100 UMMA descriptor: start>>4 [0,14), LBO>>4 [16,30) (unused
+// for swizzled K-major), SBO>>4 [32,46), version=1 [46,48), layout [61,64) = 2.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16: A,B fp16 K-major, D fp32, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// ------------------------------------------------------------------ dequant helpers
+// Byte offset of 16-byte chunk `c` (k = 8c..8c+7) of row `r` in a 128B-swizzled
+// K-major tile (row = 128 bytes = 64 fp16).
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t c) {
+  return (r >> 3) * 1024u + (r & 7u) * 128u + ((c ^ (r & 7u)) << 4);
+}
+
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+
+// (1024 + q_lo, 1024 + q_hi) as fp16 pair -> exact (q_lo, q_hi) -> fma.rn.f16x2.
+// fp16(q) for q < 1024 is exact, 1024+q is exact, the subtraction is exact, so the
+// only rounding is the single one of the fused multiply-add, as in the reference.
+__device__ __forceinline__ uint32_t dq_pair(uint32_t magic_pair, __half2 s2, __half2 z2) {
+  const __half2 kMagic = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+  __half2 q = __hsub2(u32_as_h2(magic_pair), kMagic);
+  return h2_as_u32(__hfma2(q, s2, z2));
+}
+
+// Scalar form, the definition the kernels must reproduce bit-exactly.
+__device__ __forceinline__ __half dq_scalar(uint32_t q, __half s, __half z) {
+  return __hfma(__uint2half_rn(q), s, z);
+}
+
+// One 3-bit code pair (ten codes per word, bits 30-31 unused) as the magic pair
+// expected by dq_pair: codes at (word a, slot sa) and (word b, slot sb).
+__device__ __forceinline__ uint32_t magic3(uint32_t wa, int sa, uint32_t wb, int sb) {
+  return ((wa >> (3 * sa)) & 7u) | (((wb >> (3 * sb)) & 7u) << 16) | 0x64006400u;
+}
+
+// Decode the 32/NB codes of one word (NB in {1,2,4}) to fp16 and write them as
+// consecutive-k 16-byte chunks through `emit(chunk_index, uint4)`.
+template <int NB, typename Emit>
+__device__ __forceinline__ void dq_word_pow2(uint32_t w, __half2 s2, __half2 z2, Emit&& emit) {
+  constexpr int kCodes = 32 / NB;   // codes per word
+  constexpr int kPairs = kCodes / 2;  // pairs (j, j + kPairs): half-words are kPairs codes apart
+  constexpr uint32_t kMask = ((1u << NB) - 1u) * 0x00010001u;
+  uint32_t p[kPairs];
+#pragma unroll
+  for (int j = 0; j < kPairs; ++j) p[j] = dq_pair(((w >> (NB * j)) & kMask) | 0x64006400u, s2, z2);
+  // p[j] = (c_j, c_{j+kPairs}); regroup into chunks of 8 consecutive codes. Output
+  // word m of chunk c holds codes (i, i+1), i = 8c + 2m: the low halves of p[i],
+  // p[i+1] when i < kPairs, else the high halves of p[i-kPairs], p[i-kPairs+1].
+#pragma unroll
+  for (int c = 0; c < kCodes / 8; ++c) {
+    uint32_t o[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int i = 8 * c + 2 * m;
+      o[m] = (i < kPairs) ? __byte_perm(p[i], p[i + 1], 0x5410u)
+                          : __byte_perm(p[i - kPairs], p[i - kPairs + 1], 0x7632u);
+    }
+    emit(c, make_uint4(o[0], o[1], o[2], o[3]));
+  }
+}
+
+__host__ __device__ constexpr int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+}  // namespace gemq

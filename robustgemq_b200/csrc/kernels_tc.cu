@@ -1,0 +1,534 @@
+// Persistent grouped dequant GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// Computes, for every work item (segment s -> expert e, a tile of up to NT activation
+// rows, a tile of 128 output features n0..n0+127):
+//     D[n, t] = sum_k deq(W_e)[k, n] * act[row_t, k]          (fp32 in TMEM)
+// i.e. the reference's x @ deq(W) (dequant_group_gemm.py:109-138) with the weight
+// tile as the UMMA A operand (M = 128 features) and the tokens as B (N = NT), so
+// the same kernel serves prefill (NT = 128) and small decode batches (NT = 32).
+//
+// Warp roles (448 threads, one CTA per SM, grid-stride over work items):
+//   warp 0      TMA producer: activation tile (128B swizzle), packed int32 words
+//               (8 word rows x 128 features) and fp16 scale/zero rows, no multicast
+//   warp 1      TMEM allocation + single-thread tcgen05.mma issue + commits
+//   warps 2-5   epilogue: tcgen05.ld -> mode-specific rounding -> global stores
+//   warps 6-13  dequant: packed words -> fp16 via fma.rn.f16 (bit-exact with
+//               utils.py:206-210) written as the 128B-swizzled K-major A tile
+// Dense modes (router gate) load A by TMA and skip the dequant warps.
+// Every wait is bounded (gemq_common.cuh); on expiry all roles drain and return.
+#include <cudaTypedefs.h>
+
+#include "gemq_common.cuh"
+#include "gemq_internal.h"
+
+namespace gemq {
+
+namespace {
+
+constexpr int kBK = 64;        // K per stage: one 128-byte swizzle row of fp16
+constexpr int kBM = 128;       // features per tile (UMMA M)
+constexpr int kWordRows = 8;   // packed word rows per stage (covers 64 k for b in {1,2,3,4})
+constexpr int kThreads = 448;  // 14 warps
+constexpr int kEpiWarp0 = 2;
+constexpr int kDqWarp0 = 6;
+constexpr int kNumDqThreads = 256;
+constexpr int kStages = 4;
+constexpr int kAStages = 2;
+
+__host__ __device__ constexpr int round_up(int v, int m) { return (v + m - 1) / m * m; }
+__host__ __device__ constexpr int tmem_cols_for(int c) { return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512; }
+
+template <int NT, GemmMode MODE>
+struct Cfg {
+  static constexpr bool kDense = (MODE == GemmMode::kDenseF16 || MODE == GemmMode::kDenseF32);
+  static constexpr int kMats = (MODE == GemmMode::kSwiGLU) ? 2 : 1;
+  static constexpr int kActBytes = NT * 128;
+  static constexpr int kWqBytes = kWordRows * kBM * 4;
+  static constexpr int kSzBytes = kBM * 2;
+  static constexpr int kATile = kBM * 128;
+  static constexpr int kWqOff = kActBytes;                              // dequant: packed words
+  static constexpr int kSzOff = kActBytes + kMats * kWqBytes;           // dequant: scales, zeros
+  static constexpr int kStageRaw = kDense ? kActBytes + kATile : kActBytes + kMats * (kWqBytes + 2 * kSzBytes);
+  static constexpr int kStageBytes = round_up(kStageRaw, 1024);
+  static constexpr int kTxBytes = kDense ? kActBytes + kATile : kActBytes + kMats * (kWqBytes + 2 * kSzBytes);
+  static constexpr int kARingOff = kStages * kStageBytes;
+  static constexpr int kARingBytes = kDense ? 0 : kAStages * kMats * kATile;
+  static constexpr int kBarOff = kARingOff + kARingBytes;
+  static constexpr int kNumBars = 2 * kStages + 2 * kAStages + 3;
+  static constexpr int kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;  // + tmem slot + alignment slack
+  static constexpr int kTmemCols = tmem_cols_for(kMats * NT);
+  static constexpr uint32_t kIdesc = idesc_f16_f32(kBM, NT);
+};
+
+struct KArgs {
+  const int32_t* nbits;
+  const int32_t* wq_strides0;
+  const int32_t* zs_strides0;
+  const int32_t* wq_strides1;
+  const int32_t* zs_strides1;
+  const Seg* segs;
+  const int32_t* tile_prefix;
+  int num_segs;
+  int N;           // weight features (rows of A); output columns limit
+  int K;
+  int group_size;
+  int n_tiles;
+  void* out;
+  int64_t out_ld;
+  const __half* row_weight;
+};
+
+struct Work {
+  int e, act_row, out_row, rows, n0, nb, wrow0, srow0, wrow1, srow1;
+};
+
+template <int NT>
+__device__ __forceinline__ Work decode_work(const KArgs& p, int w, bool dense) {
+  Work wk;
+  const int t = w / p.n_tiles;
+  const int i = w - t * p.n_tiles;
+  int lo = 0, hi = p.num_segs;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(p.tile_prefix + mid) <= t) lo = mid; else hi = mid;
+  }
+  const Seg sg = __ldg(p.segs + lo);
+  const int j = t - __ldg(p.tile_prefix + lo);
+  wk.e = sg.x;
+  wk.act_row = sg.y + j * NT;
+  wk.out_row = sg.z + j * NT;
+  wk.rows = min(NT, sg.w - j * NT);
+  wk.n0 = i * kBM;
+  if (dense) {
+    wk.nb = 0;
+    wk.wrow0 = wk.srow0 = wk.wrow1 = wk.srow1 = 0;
+  } else {
+    wk.nb = __ldg(p.nbits + wk.e);
+    wk.wrow0 = __ldg(p.wq_strides0 + wk.e) / p.N;
+    wk.srow0 = __ldg(p.zs_strides0 + wk.e) / p.N;
+    wk.wrow1 = __ldg(p.wq_strides1 + wk.e) / p.N;
+    wk.srow1 = __ldg(p.zs_strides1 + wk.e) / p.N;
+  }
+  return wk;
+}
+
+__device__ __forceinline__ int work_total(const KArgs& p) { return __ldg(p.tile_prefix + p.num_segs) * p.n_tiles; }
+
+// ---------------------------------------------------------------- dequant of one row
+// Thread owns feature row `n` of the 128 x 64 A tile; writes 16-byte chunks
+// [c0, c1) (k = 8c .. 8c+7) of that row. `w` holds the 8 loaded word rows of this
+// feature column; for 3-bit the tile starts at code slot `phase` of word 0.
+template <int NB>
+__device__ __forceinline__ void dq_row_pow2(const uint32_t (&w)[kWordRows], __half2 s2, __half2 z2, uint8_t* row_base,
+                                            uint32_t n, int c0, int c1) {
+  constexpr int kChunksPerWord = (32 / NB) / 8;
+#pragma unroll
+  for (int wi = 0; wi < 8 / kChunksPerWord; ++wi) {
+    const int cw = wi * kChunksPerWord;
+    if (cw >= c0 && cw < c1) {
+      dq_word_pow2<NB>(w[wi], s2, z2, [&](int c, uint4 v) {
+        *reinterpret_cast<uint4*>(row_base + sw128_offset(n, cw + c)) = v;
+      });
+    }
+  }
+}
+
+template <int P>
+__device__ __forceinline__ void dq_row_3bit(const uint32_t (&w)[kWordRows], __half2 s2, __half2 z2, uint8_t* row_base,
+                                            uint32_t n, int c0, int c1) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    if (c >= c0 && c < c1) {
+      uint32_t o[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        constexpr int dummy = 0;
+        (void)dummy;
+        const int j = 8 * c + 2 * m;
+        const int a = (P + j) / 10, sa = (P + j) % 10;
+        const int b = (P + j + 1) / 10, sb = (P + j + 1) % 10;
+        o[m] = dq_pair(magic3(w[a], sa, w[b], sb), s2, z2);
+      }
+      *reinterpret_cast<uint4*>(row_base + sw128_offset(n, c)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+__device__ __forceinline__ void dq_row(int nb, int phase, const uint32_t (&w)[kWordRows], __half2 s2, __half2 z2,
+                                       uint8_t* row_base, uint32_t n, int c0, int c1) {
+  switch (nb) {
+    case 4: dq_row_pow2<4>(w, s2, z2, row_base, n, c0, c1); break;
+    case 2: dq_row_pow2<2>(w, s2, z2, row_base, n, c0, c1); break;
+    case 1: dq_row_pow2<1>(w, s2, z2, row_base, n, c0, c1); break;
+    case 3:
+      switch (phase) {
+        case 0: dq_row_3bit<0>(w, s2, z2, row_base, n, c0, c1); break;
+        case 2: dq_row_3bit<2>(w, s2, z2, row_base, n, c0, c1); break;
+        case 4: dq_row_3bit<4>(w, s2, z2, row_base, n, c0, c1); break;
+        case 6: dq_row_3bit<6>(w, s2, z2, row_base, n, c0, c1); break;
+        default: dq_row_3bit<8>(w, s2, z2, row_base, n, c0, c1); break;
+      }
+      break;
+    default: break;
+  }
+}
+
+// ---------------------------------------------------------------- epilogue math
+__device__ __forceinline__ float silu_ref(float x) { return x / (1.f + expf(-x)); }
+
+template <GemmMode MODE>
+__device__ __forceinline__ void store_one(const KArgs& p, int64_t row, int col, float a0, float a1) {
+  if constexpr (MODE == GemmMode::kSwiGLU) {
+    // x1, x3 stored fp16; F.silu(x1) -> fp16; * x3 -> fp16 (moe_block.py:774-775)
+    const float x1 = __half2float(__float2half_rn(a0));
+    const float x3 = __half2float(__float2half_rn(a1));
+    const float sl = __half2float(__float2half_rn(silu_ref(x1)));
+    static_cast<__half*>(p.out)[row * p.out_ld + col] = __float2half_rn(sl * x3);
+  } else if constexpr (MODE == GemmMode::kRouteWeight) {
+    const float y = __half2float(__float2half_rn(a0));
+    const float wv = __half2float(p.row_weight[row]);
+    static_cast<__half*>(p.out)[row * p.out_ld + col] = __float2half_rn(y * wv);
+  } else if constexpr (MODE == GemmMode::kDenseF32) {
+    static_cast<float*>(p.out)[row * p.out_ld + col] = a0;
+  } else {
+    static_cast<__half*>(p.out)[row * p.out_ld + col] = __float2half_rn(a0);
+  }
+}
+
+// ---------------------------------------------------------------- the kernel
+template <int NT, GemmMode MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_moe_tc(const KArgs p, const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w0,
+             const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ CUtensorMap tm_z0,
+             const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_s1,
+             const __grid_constant__ CUtensorMap tm_z1) {
+  using C = Cfg<NT, MODE>;
+  constexpr bool kDense = C::kDense;
+  constexpr int kMats = C::kMats;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* afull = bars + 2 * kStages;
+  uint64_t* aempty = afull + kAStages;
+  uint64_t* acc_full = aempty + kAStages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* drain = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kDense ? 1 : (kNumDqThreads / 32) + 1);
+    }
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&afull[s], kNumDqThreads);
+      mbar_init(&aempty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_act);
+    tma_prefetch_desc(&tm_w0);
+    if (!kDense) {
+      tma_prefetch_desc(&tm_s0);
+      tma_prefetch_desc(&tm_z0);
+      if (kMats == 2) {
+        tma_prefetch_desc(&tm_w1);
+        tma_prefetch_desc(&tm_s1);
+        tma_prefetch_desc(&tm_z1);
+      }
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = work_total(p);
+  const int KT = p.K / kBK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int armed = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        const Work wk = decode_work<NT>(p, w, kDense);
+        const int eps = kDense ? 1 : 32 / max(wk.nb, 1);
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, kDevTimeoutTmaEmpty)) { ok = false; break; }
+          uint8_t* st = smem + s * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], C::kTxBytes);
+          const int k0 = kt * kBK;
+          tma_load_2d(st, &tm_act, &full[s], k0, wk.act_row);
+          if constexpr (kDense) {
+            tma_load_2d(st + C::kActBytes, &tm_w0, &full[s], k0, wk.n0);
+          } else {
+            const int wr = k0 / eps;
+            const int sr = k0 / p.group_size;
+            tma_load_2d(st + C::kWqOff, &tm_w0, &full[s], wk.n0, wk.wrow0 + wr);
+            tma_load_2d(st + C::kSzOff, &tm_s0, &full[s], wk.n0, wk.srow0 + sr);
+            tma_load_2d(st + C::kSzOff + C::kSzBytes, &tm_z0, &full[s], wk.n0, wk.srow0 + sr);
+            if constexpr (kMats == 2) {
+              tma_load_2d(st + C::kWqOff + C::kWqBytes, &tm_w1, &full[s], wk.n0, wk.wrow1 + wr);
+              tma_load_2d(st + C::kSzOff + 2 * C::kSzBytes, &tm_s1, &full[s], wk.n0, wk.srow1 + sr);
+              tma_load_2d(st + C::kSzOff + 3 * C::kSzBytes, &tm_z1, &full[s], wk.n0, wk.srow1 + sr);
+            }
+          }
+          ++armed;
+          if (++s == kStages) { s = 0; ph ^= 1u; }
+        }
+      }
+      // drain: wait for the last armed phase of every stage (loads still in flight)
+      for (int st = 0; st < kStages && st < armed; ++st) {
+        const int times = (armed - 1 - st) / kStages + 1;
+        mbar_wait(&full[st], static_cast<uint32_t>((times - 1) & 1), kDevTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0, as = 0;
+      uint32_t ph = 0, aph = 0, accph = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        if (!mbar_wait(acc_empty, accph ^ 1u, kDevTimeoutAccEmpty)) break;
+        tc_fence_after();
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&full[s], ph, kDevTimeoutTmaFull)) { ok = false; break; }
+          if constexpr (!kDense) {
+            if (!mbar_wait(&afull[as], aph, kDevTimeoutAFull)) { ok = false; break; }
+          }
+          tc_fence_after();
+          const uint32_t act_addr = smem_u32(smem + s * C::kStageBytes);
+#pragma unroll
+          for (int m = 0; m < kMats; ++m) {
+            const uint32_t a_addr = kDense ? act_addr + C::kActBytes
+                                           : smem_u32(smem + C::kARingOff + (as * kMats + m) * C::kATile);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              umma_f16(tmem + static_cast<uint32_t>(m * NT), sdesc_sw128(a_addr + kk * 32),
+                       sdesc_sw128(act_addr + kk * 32), C::kIdesc, (kt | kk) != 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[s]);
+          if constexpr (!kDense) umma_commit(&aempty[as]);
+          if (++s == kStages) { s = 0; ph ^= 1u; }
+          if constexpr (!kDense) {
+            if (++as == kAStages) { as = 0; aph ^= 1u; }
+          }
+        }
+        if (!ok) break;
+        umma_commit(acc_full);
+        accph ^= 1u;
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, kDevTimeoutDrain);
+    }
+  } else if (warp < kDqWarp0) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * q) << 16);
+    uint32_t accph = 0;
+    for (int w = blockIdx.x; w < total; w += gridDim.x) {
+      const Work wk = decode_work<NT>(p, w, kDense);
+      if (!mbar_wait(acc_full, accph, kDevTimeoutAccFull)) break;
+      tc_fence_after();
+      const int col = wk.n0 + 32 * q + lane;
+      for (int c0 = 0; c0 < NT; c0 += 16) {
+        if (c0 >= wk.rows) break;
+        uint32_t r0[16], r1[16];
+        tmem_ld16(lane_base + c0, r0);
+        if constexpr (kMats == 2) tmem_ld16(lane_base + NT + c0, r1);
+        tmem_ld_wait();
+        if (col < p.N) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (c0 + i < wk.rows) {
+              const float a0 = __uint_as_float(r0[i]);
+              const float a1 = kMats == 2 ? __uint_as_float(r1[i]) : 0.f;
+              store_one<MODE>(p, static_cast<int64_t>(wk.out_row + c0 + i), col, a0, a1);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+      accph ^= 1u;
+    }
+  } else if constexpr (!kDense) {
+    // ------------------------------------------------------------ dequant
+    const int dt = threadIdx.x - kDqWarp0 * 32;
+    const int wg = dt >> 7;
+    const uint32_t n = static_cast<uint32_t>(dt & 127);
+    const int mat = (kMats == 2) ? wg : 0;
+    const int c0 = (kMats == 2) ? 0 : 4 * wg;
+    const int c1 = (kMats == 2) ? 8 : 4 * wg + 4;
+    int s = 0, as = 0;
+    uint32_t ph = 0, aph = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      const Work wk = decode_work<NT>(p, w, false);
+      const int nb = wk.nb;
+      if (nb < 1 || nb > 4) {
+        if (dt == 0) set_device_error(kDevBadBits);
+      }
+      for (int kt = 0; kt < KT; ++kt) {
+        if (!mbar_wait(&full[s], ph, kDevTimeoutTmaFull)) { ok = false; break; }
+        if (!mbar_wait(&aempty[as], aph ^ 1u, kDevTimeoutAEmpty)) { ok = false; break; }
+        const uint8_t* st = smem + s * C::kStageBytes;
+        const uint32_t* wcol = reinterpret_cast<const uint32_t*>(st + C::kWqOff + mat * C::kWqBytes) + n;
+        uint32_t wv[kWordRows];
+#pragma unroll
+        for (int r = 0; r < kWordRows; ++r) wv[r] = wcol[r * kBM];
+        const __half sh = reinterpret_cast<const __half*>(st + C::kSzOff + (2 * mat) * C::kSzBytes)[n];
+        const __half zh = reinterpret_cast<const __half*>(st + C::kSzOff + (2 * mat + 1) * C::kSzBytes)[n];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        const int phase = (nb == 3) ? (kt * kBK) % 10 : 0;
+        uint8_t* a_tile = smem + C::kARingOff + (as * kMats + mat) * C::kATile;
+        dq_row(nb, phase, wv, __halves2half2(sh, sh), __halves2half2(zh, zh), a_tile, n, c0, c1);
+        fence_proxy_async_smem();
+        mbar_arrive(&afull[as]);
+        if (++s == kStages) { s = 0; ph ^= 1u; }
+        if (++as == kAStages) { as = 0; aph ^= 1u; }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+  }
+  return fn;
+}
+
+bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner, uint64_t outer,
+              uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (fn == nullptr || base == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * static_cast<uint64_t>(elem_bytes)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int NT, GemmMode MODE>
+cudaError_t launch_t(const GemmArgs& a, cudaStream_t stream) {
+  using C = Cfg<NT, MODE>;
+  CUtensorMap m_act, m_w0, m_s0, m_z0, m_w1, m_s1, m_z1;
+  const int K = C::kDense ? a.w0.k : a.w0.k;
+  if (!make_map(&m_act, a.act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, static_cast<uint64_t>(a.act_rows), 64, NT,
+                CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if constexpr (C::kDense) {
+    if (!make_map(&m_w0, a.dense_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, a.w0.n, 64, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+    m_s0 = m_z0 = m_w1 = m_s1 = m_z1 = m_w0;
+  } else {
+    const uint64_t srows = static_cast<uint64_t>(a.w0.num_experts) * (a.w0.k / a.w0.group_size);
+    if (!make_map(&m_w0, a.w0.wq, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, a.w0.n, a.w0.wq_rows, kBM, kWordRows,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map(&m_s0, a.w0.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w0.n, srows, kBM, 1,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map(&m_z0, a.w0.zeros, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w0.n, srows, kBM, 1,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+    if constexpr (C::kMats == 2) {
+      const uint64_t srows1 = static_cast<uint64_t>(a.w1.num_experts) * (a.w1.k / a.w1.group_size);
+      if (!make_map(&m_w1, a.w1.wq, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, a.w1.n, a.w1.wq_rows, kBM, kWordRows,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+          !make_map(&m_s1, a.w1.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w1.n, srows1, kBM, 1,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+          !make_map(&m_z1, a.w1.zeros, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w1.n, srows1, kBM, 1,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
+    } else {
+      m_w1 = m_w0;
+      m_s1 = m_s0;
+      m_z1 = m_z0;
+    }
+  }
+  KArgs p;
+  p.nbits = a.w0.nbits;
+  p.wq_strides0 = a.w0.wq_strides;
+  p.zs_strides0 = a.w0.zs_strides;
+  p.wq_strides1 = C::kMats == 2 ? a.w1.wq_strides : a.w0.wq_strides;
+  p.zs_strides1 = C::kMats == 2 ? a.w1.zs_strides : a.w0.zs_strides;
+  p.segs = a.segs;
+  p.tile_prefix = a.tile_prefix;
+  p.num_segs = a.num_segs;
+  p.N = a.w0.n;
+  p.K = K;
+  p.group_size = C::kDense ? 64 : a.w0.group_size;
+  p.n_tiles = (a.w0.n + kBM - 1) / kBM;
+  p.out = a.out;
+  p.out_ld = a.out_ld;
+  p.row_weight = reinterpret_cast<const __half*>(a.row_weight);
+  auto kern = k_moe_tc<NT, MODE>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (err != cudaSuccess) return err;
+  kern<<<a.num_sms, kThreads, C::kSmemBytes, stream>>>(p, m_act, m_w0, m_s0, m_z0, m_w1, m_s1, m_z1);
+  return cudaGetLastError();
+}
+
+template <int NT>
+cudaError_t launch_nt(const GemmArgs& a, cudaStream_t stream) {
+  switch (a.mode) {
+    case GemmMode::kSwiGLU: return launch_t<NT, GemmMode::kSwiGLU>(a, stream);
+    case GemmMode::kRouteWeight: return launch_t<NT, GemmMode::kRouteWeight>(a, stream);
+    case GemmMode::kStoreF16: return launch_t<NT, GemmMode::kStoreF16>(a, stream);
+    case GemmMode::kDenseF16: return launch_t<NT, GemmMode::kDenseF16>(a, stream);
+    case GemmMode::kDenseF32: return launch_t<NT, GemmMode::kDenseF32>(a, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+bool tc_gemm_supported(const GemmArgs& a) {
+  if (encode_fn() == nullptr) return false;
+  if (a.nt != kNtSmall && a.nt != kNtLarge) return false;
+  if (a.w0.k % kBK != 0 || a.w0.k <= 0) return false;
+  const bool dense = (a.mode == GemmMode::kDenseF16 || a.mode == GemmMode::kDenseF32);
+  if (dense) return (reinterpret_cast<uintptr_t>(a.dense_a) & 15u) == 0;
+  if (a.w0.n % kBM != 0 || a.w0.group_size % kBK != 0) return false;
+  if (a.mode == GemmMode::kSwiGLU && (a.w1.n != a.w0.n || a.w1.k != a.w0.k || a.w1.group_size != a.w0.group_size))
+    return false;
+  return (reinterpret_cast<uintptr_t>(a.act) & 15u) == 0;
+}
+
+cudaError_t launch_tc_gemm(const GemmArgs& a, cudaStream_t stream) {
+  if (!tc_gemm_supported(a)) return cudaErrorNotSupported;
+  return a.nt == kNtSmall ? launch_nt<kNtSmall>(a, stream) : launch_nt<kNtLarge>(a, stream);
+}
+
+}  // namespace gemq

@@ -1,0 +1,216 @@
+"""C ABI and host-side logic on the CPU: the library loads without a GPU, exports
+every symbol ``include/gemq_b200.h`` declares, and rejects bad arguments with the
+documented status before touching the device. Block guards mirror the
+reference's truth tables (tests/test_moe_block_equiv.py:255-332 of RobustGEMQ)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def header_functions():
+    text = (ROOT / "include" / "gemq_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*(gemq_[a-z_0-9]+)\s*\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    from robustgemq_b200 import _lib
+
+    lib = _lib.load()
+    declared = header_functions()
+    assert len(declared) >= 18
+    assert sorted(_lib.EXPORTED) == declared
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert lib.gemq_version() == 1
+
+
+def _fake_proj(E=2, K=128, N=128, g=64):
+    from robustgemq_b200._lib import ProjT
+
+    p = ProjT()
+    p.wq = p.scales = p.zeros = p.nbits = p.wq_strides = p.zs_strides = 0x1000
+    p.wq_rows, p.num_experts, p.k, p.n, p.group_size = 64, E, K, N, g
+    return p
+
+
+def _status(rc):
+    from robustgemq_b200 import _lib
+
+    return rc, _lib.load().gemq_last_error_string().decode()
+
+
+def test_argument_errors_are_statuses_not_aborts():
+    from robustgemq_b200 import _lib
+
+    lib = _lib.load()
+    rc, msg = _status(lib.gemq_pack_weights_over_cols(None, 4, 8, 5, None, None))
+    assert rc == _lib.GEMQ_ERR_INVALID_ARGUMENT and "bitwidth" in msg
+    rc, _ = _status(lib.gemq_unpack_over_cols(None, 4, 1, 64, 2, None, None))
+    assert rc == _lib.GEMQ_ERR_INVALID_ARGUMENT  # 64 two-bit codes need 4 words, 1 given
+    p = _fake_proj()
+    p.k = 100  # not a multiple of group_size
+    rc, msg = _status(lib.gemq_dequant_expert(ctypes.byref(p), 0, 0x2000, None))
+    assert rc == _lib.GEMQ_ERR_INVALID_ARGUMENT and "group_size" in msg
+    p = _fake_proj()
+    rc, _ = _status(lib.gemq_dequant_expert(ctypes.byref(p), 5, 0x2000, None))
+    assert rc == _lib.GEMQ_ERR_INVALID_ARGUMENT
+    rc, _ = _status(lib.gemq_dequant_group_gemm(ctypes.byref(p), 0x3000, 4, 0x4000, 0, 0x5000, 0x6000, 1 << 20, None))
+    assert rc == _lib.GEMQ_ERR_INVALID_ARGUMENT  # no indices
+    rc, _ = _status(lib.gemq_dequant_group_gemm(ctypes.byref(p), 0x3000, 4, 0x4000, 1, 0x5000, 0x6000, 8, None))
+    assert rc == _lib.GEMQ_ERR_WORKSPACE
+
+
+def _desc(**kw):
+    from robustgemq_b200._lib import LayerDescT
+
+    d = LayerDescT()
+    d.hidden, d.inter, d.num_experts, d.top_k, d.group_size = 128, 128, 2, 1, 64
+    d.gate_weight = 0x1000
+    d.w1, d.w3, d.w2 = _fake_proj(), _fake_proj(), _fake_proj()
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("field,value,text", [
+    ("top_k", 3, "top_k"),
+    ("num_experts", 300, "256"),
+    ("group_size", 128, "Group sizes"),
+    ("router", 7, "router"),
+    ("gate_weight", None, "gate"),
+])
+def test_layer_create_validates_before_device_access(field, value, text):
+    from robustgemq_b200 import _lib
+
+    lib = _lib.load()
+    d = _desc(**{field: value})
+    h = ctypes.c_void_p()
+    rc, msg = _status(lib.gemq_layer_create(ctypes.byref(d), ctypes.byref(h)))
+    assert rc in (_lib.GEMQ_ERR_INVALID_ARGUMENT, _lib.GEMQ_ERR_UNSUPPORTED)
+    assert text in msg
+
+
+def test_layer_shape_mismatch_rejected():
+    from robustgemq_b200 import _lib
+
+    lib = _lib.load()
+    d = _desc()
+    d.w2.n = 256  # down projection must map F -> D
+    h = ctypes.c_void_p()
+    rc, msg = _status(lib.gemq_layer_create(ctypes.byref(d), ctypes.byref(h)))
+    assert rc == _lib.GEMQ_ERR_INVALID_ARGUMENT and "shapes" in msg
+
+
+def test_workspace_size_queries_grow_with_tokens():
+    from robustgemq_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.gemq_group_gemm_workspace_size(4) >= lib.gemq_group_gemm_workspace_size(1) > 0
+    assert lib.gemq_moe_workspace_size(None, 16, 0) == 0
+
+
+# ----------------------------------------------------------------------------- guards
+def _ds_config(**kw):
+    c = SimpleNamespace(hidden_size=64, moe_intermediate_size=64, n_routed_experts=4, n_shared_experts=2,
+                        num_experts_per_tok=2, norm_topk_prob=False, topk_method="greedy", scoring_func="softmax",
+                        routed_scaling_factor=1.0)
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+class _OfficialBlockStub:
+    pass
+
+
+_OfficialBlockStub.__module__ = "transformers_modules.deepseek.modeling_deepseek"
+
+
+class _BuiltinBlockStub:
+    pass
+
+
+_BuiltinBlockStub.__module__ = "transformers.models.deepseek_v2.modeling_deepseek_v2"
+
+
+@pytest.mark.parametrize("field,value", [("topk_method", "group_limited_greedy"), ("scoring_func", "sigmoid")])
+def test_deepseek_feature_guard(field, value):
+    from robustgemq_b200.inference import check_deepseek_routing_supported
+
+    check_deepseek_routing_supported(_ds_config())
+    with pytest.raises(AssertionError):
+        check_deepseek_routing_supported(_ds_config(**{field: value}))
+
+
+@pytest.mark.parametrize("official,norm,top_k,scaling,ok", [
+    (True, False, 2, 1.0, True), (True, False, 2, 16.0, False), (True, True, 2, 16.0, True),
+    (True, True, 1, 1.0, False), (False, False, 2, 1.0, True), (False, True, 2, 1.0, False),
+    (False, False, 2, 16.0, False),
+])
+def test_deepseek_gate_guard_truth_table(official, norm, top_k, scaling, ok):
+    from robustgemq_b200.inference import check_deepseek_gate_matches
+
+    cfg = _ds_config(norm_topk_prob=norm, num_experts_per_tok=top_k, routed_scaling_factor=scaling)
+    blk = _OfficialBlockStub() if official else _BuiltinBlockStub()
+    if ok:
+        check_deepseek_gate_matches(cfg, blk)
+    else:
+        with pytest.raises(AssertionError):
+            check_deepseek_gate_matches(cfg, blk)
+
+
+def test_from_hf_requires_packed_linears():
+    import torch
+
+    from robustgemq_b200.inference import QuantFusedOlmoeMoEBlock
+
+    cfg = SimpleNamespace(hidden_size=64, intermediate_size=64, num_experts=2, num_experts_per_tok=1,
+                          norm_topk_prob=False)
+    hf = SimpleNamespace(gate=torch.nn.Linear(64, 2, bias=False),
+                         experts=[SimpleNamespace(gate_proj=torch.nn.Linear(64, 64), up_proj=None, down_proj=None)])
+    with pytest.raises(ValueError, match="patch and replace"):
+        QuantFusedOlmoeMoEBlock.from_hf(cfg, hf)
+
+
+def test_stacking_matches_reference_layout():
+    """from_packed stacks like from_hf (moe_block.py:725-757): cat along rows,
+    exclusive-cumsum numel strides, one group size, w1/w3 aligned."""
+    import torch
+
+    from oracle import gemq_oracle as O
+    from robustgemq_b200.inference import QuantFusedOlmoeMoEBlock
+    from robustgemq_b200.quant import PackedLinear
+
+    rng = np.random.default_rng(0)
+    bits, K, N, g = [2, 3, 4], 128, 64, 64
+
+    def lin(b, k, n):
+        codes = rng.integers(0, 2 ** b, size=(n, k), dtype=np.uint8)
+        wq = np.ascontiguousarray(O.pack_weights_over_cols(codes, b))
+        return PackedLinear(torch.from_numpy(wq), torch.zeros((k // g, n), dtype=torch.float16),
+                            torch.zeros((k // g, n), dtype=torch.float16), b, g, k, n)
+
+    cfg = SimpleNamespace(hidden_size=K, intermediate_size=N, num_experts=3, num_experts_per_tok=2,
+                          norm_topk_prob=False)
+    w1 = [lin(b, K, N) for b in bits]
+    w3 = [lin(b, K, N) for b in bits]
+    w2 = [lin(b, N, K) for b in bits]
+    blk = QuantFusedOlmoeMoEBlock.from_packed(cfg, torch.zeros((3, K), dtype=torch.float16), w1, w3, w2)
+    assert blk.block_group_size == g
+    assert blk.w1_wq.shape == (sum(O.packed_rows(K, b) for b in bits), N)
+    assert blk.w1_wq_strides.tolist() == [0, O.packed_rows(K, 2) * N, (O.packed_rows(K, 2) + O.packed_rows(K, 3)) * N]
+    assert blk.w2_zs_strides.tolist() == [0, (N // g) * K, 2 * (N // g) * K]
+    bad = [lin(2, K, N), lin(2, K, N), lin(2, K, N)]
+    bad[1].group_size = 128
+    with pytest.raises(AssertionError, match="Group sizes"):
+        QuantFusedOlmoeMoEBlock.from_packed(cfg, torch.zeros((3, K), dtype=torch.float16), bad, bad, w2)

@@ -1,0 +1,148 @@
+"""Block-level parity of the fused MoE forward with the reference (``-m gpu``).
+
+Mirrors the reference's test_moe_block_equiv.py / test_decode_nan_hunt.py ladder on
+the golden vectors recorded from the reference's own QuantFused*MoEBlock forwards
+(mixed per-expert bits [1,2,3,2,3,1,2,3], D = F = 256, E = 8, top-2, g = 64).
+Tolerance: rel-L2 <= 1e-3 against the reference; the
+reference's two fma semantics alone differ by ~1e-3 on these blocks, so the
+tighter bar against the oracle shows the kernels reproduce the GPU semantics.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_l2
+from gpu_helpers import block_from_golden, cuda
+from oracle import gemq_oracle as O
+from test_oracle_golden import block_weights
+
+pytestmark = pytest.mark.gpu
+
+FAMILIES = ["olmoe", "qwen3", "mixtral", "deepseek"]
+REF_TOL = 1e-3          # against the reference's recorded output
+ORACLE_TOL = 5e-4       # against the CPU restatement with identical routing
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error(cuda_device):
+    from robustgemq_b200 import _lib
+
+    _lib.device_error()
+    yield
+    assert _lib.device_error() == 0, "a kernel recorded a device-side error"
+
+
+def _t(out):
+    return out[0] if isinstance(out, (tuple, list)) else out
+
+
+@pytest.mark.parametrize("family", FAMILIES)
+def test_prefill_given_routing_matches_reference(family):
+    blk, d = block_from_golden(family)
+    x = cuda(d["x"])
+    y = blk.forward_routed(x, cuda(d["route_idx"]), cuda(d["route_w"])).cpu().numpy()
+    err = rel_l2(y, d["y_ntok_gpu"])
+    print(f"\n[{family} prefill] rel-L2 vs reference {err:.3e}")
+    assert err <= REF_TOL
+    ob = block_weights(d, family)
+    yo, _ = O.moe_forward_n_tokens(ob, d["x"], O.Routing(None, d["route_idx"].astype(np.int64), d["route_w"]))
+    assert rel_l2(y, yo) <= ORACLE_TOL
+
+
+@pytest.mark.parametrize("family", FAMILIES)
+def test_prefill_full_forward_matches_reference(family):
+    """Device router + dispatch + grouped GEMMs + combine, through ``forward``."""
+    blk, d = block_from_golden(family)
+    x = cuda(d["x"])[None]  # [1, T, D] -> forward_n_tokens
+    out = blk(x)
+    y = _t(out)[0].cpu().numpy()
+    _, idx, w = blk.route(x)
+    assert np.array_equal(idx.cpu().numpy(), d["route_idx"]), "router picked different experts"
+    assert np.abs(w.float().cpu().numpy() - d["route_w"].astype(np.float32)).max() <= 1e-3
+    assert rel_l2(y, d["y_ntok_gpu"]) <= REF_TOL
+    if family != "deepseek":
+        logits = out[1].float().cpu().numpy()
+        assert rel_l2(logits, d["route_logits"]) <= 2e-3
+
+
+@pytest.mark.parametrize("family", FAMILIES)
+def test_decode_matches_reference(family):
+    blk, d = block_from_golden(family)
+    x = cuda(d["x_one"])[None]  # [1, 1, D] -> forward_one_token
+    y = _t(blk(x)).reshape(1, -1).cpu().numpy()
+    ob = block_weights(d, family)
+    yo, _ = O.moe_forward_one_token(ob, d["x_one"], O.Routing(None, d["route1_idx"].astype(np.int64), d["route1_w"]))
+    err_ref = rel_l2(y, d["y_one_gpu"])
+    err_or = rel_l2(y, yo)
+    print(f"\n[{family} decode] rel-L2 vs reference {err_ref:.3e}, vs oracle {err_or:.3e}")
+    assert err_or <= ORACLE_TOL
+    # DeepSeek's shared experts go through the reference's fp16-atomic split-K GEMV,
+    # whose own run-to-run spread is ~1e-3 (test_decode_nan_hunt.py:241-277)
+    assert err_ref <= (2e-3 if family == "deepseek" else REF_TOL)
+
+
+@pytest.mark.parametrize("family", FAMILIES)
+def test_decode_path_agrees_with_prefill_path(family):
+    blk, d = block_from_golden(family)
+    x = cuda(d["x_one"])[None]
+    y1 = _t(blk.forward_one_token(x)).float()
+    yn = _t(blk.forward_n_tokens(x)).float()
+    assert rel_l2(y1.cpu().numpy(), yn.cpu().numpy()) <= 2e-3
+
+
+@pytest.mark.parametrize("family", FAMILIES)
+def test_tensor_core_and_cuda_core_paths_agree(family):
+    from robustgemq_b200 import _lib
+
+    blk, d = block_from_golden(family)
+    x = cuda(d["x"])
+    idx, w = cuda(d["route_idx"]), cuda(d["route_w"])
+    y_tc = blk.forward_routed(x, idx, w)
+    blk._fwd_flags = _lib.FWD_FORCE_SIMT
+    y_simt = blk.forward_routed(x, idx, w)
+    blk._fwd_flags = 0
+    assert rel_l2(y_tc.cpu().numpy(), y_simt.cpu().numpy()) <= 5e-4
+
+
+def _poison(nbytes=256 * 1024 * 1024):
+    junk = torch.full((nbytes // 2,), float("nan"), dtype=torch.float16, device="cuda")
+    del junk
+
+
+@pytest.mark.parametrize("family", FAMILIES)
+def test_outputs_fully_written_and_deterministic(family):
+    """NaN-poisoned allocator, repeated calls: every element written, bit-identical
+    results on both paths (test_decode_nan_hunt.py:34-98; DeepSeek included, since
+    nothing here accumulates with atomics)."""
+    blk, d = block_from_golden(family)
+    for x in (cuda(d["x_one"])[None], cuda(d["x"])[None]):
+        outs = []
+        for _ in range(3):
+            _poison()
+            blk._workspaces = {}
+            outs.append(_t(blk(x)).clone())
+        assert not torch.isnan(outs[0]).any()
+        assert all(torch.equal(outs[0], o) for o in outs[1:])
+
+
+def test_empty_and_single_token_inputs():
+    blk, d = block_from_golden("olmoe")
+    x0 = torch.empty((1, 0, int(d["D"])), dtype=torch.float16, device="cuda")
+    y0, _ = blk.forward_n_tokens(x0)
+    assert y0.shape == x0.shape
+    x1 = cuda(d["x"][:1])[None]
+    y1, _ = blk.forward_n_tokens(x1)
+    assert torch.isfinite(y1).all()
+
+
+def test_guards_raise_on_gpu_blocks():
+    from robustgemq_b200.inference import check_w1_w3_aligned
+
+    blk, d = block_from_golden("qwen3")
+    check_w1_w3_aligned(blk)
+    blk.w3_nbits = blk.w3_nbits.flip(0)
+    with pytest.raises(AssertionError):
+        check_w1_w3_aligned(blk)
