@@ -261,7 +261,7 @@ int gemq_dequant_group_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t 
   a.num_sms = device_sm_count();
   a.nt = choose_nt(m);
   if (!tc_gemm_supported(a)) a.nt = 32;
-  GEMQ_CUDA(launch_build_index_segs(indices, num_indices, m, a.nt, segs, tp, s), "segments");
+  GEMQ_CUDA(launch_build_index_segs(indices, num_indices, proj->num_experts, m, a.nt, segs, tp, s), "segments");
   return run_gemm(a, false, s, "dequant_group_gemm");
 }
 
@@ -292,7 +292,7 @@ int gemq_dequant_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t m, uin
   a.num_sms = device_sm_count();
   a.nt = choose_nt(m);
   if (!tc_gemm_supported(a)) a.nt = 32;
-  GEMQ_CUDA(launch_build_index_segs(nullptr, 1, m, a.nt, segs, tp, s), "segments");
+  GEMQ_CUDA(launch_build_index_segs(nullptr, 1, 1, m, a.nt, segs, tp, s), "segments");
   return run_gemm(a, false, s, "dequant_gemm");
 }
 
@@ -539,7 +539,7 @@ int run_router(gemq_layer_t* L, const uint16_t* x, int64_t T, void* logits_out, 
     a.nt = choose_nt(T);
     const bool tc = T >= 64 && !(flags & GEMQ_FWD_FORCE_SIMT) && tc_gemm_supported(a);
     if (tc) {
-      GEMQ_CUDA(launch_build_index_segs(nullptr, 1, T, a.nt, one_seg, one_tp, s), "router segments");
+      GEMQ_CUDA(launch_build_index_segs(nullptr, 1, 1, T, a.nt, one_seg, one_tp, s), "router segments");
       GEMQ_CUDA(launch_tc_gemm(a, s), "router gemm");
     } else {
       GEMQ_CUDA(launch_router_simt(x, T, d.gate_weight, d.num_experts, d.hidden, d.router == GEMQ_ROUTER_FP32,
@@ -662,7 +662,7 @@ int forward_n_tokens(gemq_layer_t* L, const uint16_t* x, int64_t T, uint16_t* ou
     const bool stc = !force_simt && tc_gemm_supported(su) && tc_gemm_supported(sd);
     if (!stc) su.nt = sd.nt = 32;
     tm.begin(GEMQ_STAGE_SHARED);
-    GEMQ_CUDA(launch_build_index_segs(nullptr, 1, T, su.nt, b.one_seg, b.one_tp, s), "shared segments");
+    GEMQ_CUDA(launch_build_index_segs(nullptr, 1, 1, T, su.nt, b.one_seg, b.one_tp, s), "shared segments");
     if (int rc = run_gemm(su, !stc, s, "shared up")) return rc;
     if (int rc = run_gemm(sd, !stc, s, "shared down")) return rc;
     tm.end(GEMQ_STAGE_SHARED);
@@ -688,10 +688,11 @@ size_t gemq_moe_workspace_size(const gemq_layer_t* layer, int64_t num_tokens, ui
 
 int gemq_moe_route(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, void* logits, int32_t* topk_idx,
                    uint16_t* topk_w, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
-  if (layer == nullptr || x == nullptr || logits == nullptr || topk_idx == nullptr || topk_w == nullptr)
-    return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  if (layer == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null layer");
   if (num_tokens < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative token count");
   if (num_tokens == 0) return GEMQ_OK;
+  if (x == nullptr || logits == nullptr || topk_idx == nullptr || topk_w == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
   Carver c(workspace);
   Seg* seg = c.take<Seg>(1);
   int32_t* tp = c.take<int32_t>(2);
@@ -703,9 +704,10 @@ int gemq_moe_route(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, v
 int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, uint16_t* out, void* router_logits,
                      const int32_t* topk_idx, const uint16_t* topk_w, uint32_t flags, void* workspace,
                      size_t workspace_bytes, void* stream) {
-  if (layer == nullptr || x == nullptr || out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  if (layer == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null layer");
   if (num_tokens < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative token count");
-  if (num_tokens == 0) return GEMQ_OK;
+  if (num_tokens == 0) return GEMQ_OK;  // empty batch: nothing to read or write (pointers may be null)
+  if (x == nullptr || out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
   const bool one = (flags & GEMQ_FWD_ONE_TOKEN) != 0;
   if (one && num_tokens != 1)
     return fail(GEMQ_ERR_INVALID_ARGUMENT,

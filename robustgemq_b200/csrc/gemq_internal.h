@@ -65,8 +65,8 @@ cudaError_t launch_tc_gemm(const GemmArgs& a, cudaStream_t stream);
 cudaError_t launch_simt_gemm(const GemmArgs& a, cudaStream_t stream);
 
 // Builds segments + tile prefix for a dequant_group_gemm call (one segment per index).
-cudaError_t launch_build_index_segs(const int32_t* indices, int num_indices, int64_t m, int nt, Seg* segs,
-                                    int32_t* tile_prefix, cudaStream_t stream);
+cudaError_t launch_build_index_segs(const int32_t* indices, int num_indices, int num_experts, int64_t m, int nt,
+                                    Seg* segs, int32_t* tile_prefix, cudaStream_t stream);
 
 // Routing / dispatch / combine.
 cudaError_t launch_router_simt(const uint16_t* x, int64_t T, const uint16_t* gate, int E, int D, bool fp32_out,

@@ -181,26 +181,33 @@ __global__ void k_topk(const void* __restrict__ logits, int logits_fp32, int64_t
   float wsel[16];
   int isel[16];
   float wsum = 0.f;
+  // Selection key: NaN ranks above every number (torch.topk's order); taken
+  // entries are -3, so the arg-max is always a valid, untaken expert id.
+  auto key = [](float a) { return (a != a) ? FLT_MAX : a; };
   for (int j = 0; j < k; ++j) {
-    float best = -2.f;
+    float best = -FLT_MAX, bestv = 0.f;
     int bi = 0x7fffffff;
 #pragma unroll
     for (int i = 0; i < kMaxExperts / 32; ++i) {
       const int e = i * 32 + lane;
-      if (e < E && (v[i] > best || (v[i] == best && e < bi))) {
-        best = v[i];
+      if (e < E && v[i] != -3.f && (key(v[i]) > best || (key(v[i]) == best && e < bi))) {
+        best = key(v[i]);
+        bestv = v[i];
         bi = e;
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const float ov = __shfl_xor_sync(0xffffffffu, bestv, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (ob > best || (ob == best && oi < bi)) {
         best = ob;
+        bestv = ov;
         bi = oi;
       }
     }
+    best = bestv;
 #pragma unroll
     for (int i = 0; i < kMaxExperts / 32; ++i)
       if (i * 32 + lane == bi) v[i] = -3.f;
@@ -272,15 +279,22 @@ __global__ void k_scan_segs(const int32_t* __restrict__ counts, int E, int nt, S
 }
 
 // One warp per slot: claim a row, record it, copy the token's activation row.
+// A slot whose expert id is out of range (k_count already recorded kDevBadExpert)
+// gets no row and slot_pos -1, which the combine skips.
 __global__ void k_scatter(const int32_t* __restrict__ topk_idx, const __half* __restrict__ topk_w,
-                          const __half* __restrict__ x, int64_t P, int k, int D, int32_t* __restrict__ cursor,
+                          const __half* __restrict__ x, int64_t P, int k, int E, int D, int32_t* __restrict__ cursor,
                           int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm, __half* __restrict__ x_perm) {
   const int64_t slot = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (slot >= P) return;
+  const int e = topk_idx[slot];
+  if (e < 0 || e >= E) {
+    if (lane == 0) slot_pos[slot] = -1;
+    return;
+  }
   int pos = 0;
   if (lane == 0) {
-    pos = atomicAdd(&cursor[topk_idx[slot]], 1);
+    pos = atomicAdd(&cursor[e], 1);
     slot_pos[slot] = pos;
     w_perm[pos] = topk_w[slot];
   }
@@ -305,7 +319,7 @@ cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, con
   if ((err = cudaGetLastError()) != cudaSuccess) return err;
   if (P > 0) {
     k_scatter<<<static_cast<unsigned>((P * 32 + 255) / 256), 256, 0, stream>>>(
-        topk_idx, reinterpret_cast<const __half*>(topk_w), reinterpret_cast<const __half*>(x), P, k, D, cursor,
+        topk_idx, reinterpret_cast<const __half*>(topk_w), reinterpret_cast<const __half*>(x), P, k, E, D, cursor,
         slot_pos, reinterpret_cast<__half*>(w_perm), reinterpret_cast<__half*>(x_perm));
     err = cudaGetLastError();
   }
@@ -313,17 +327,36 @@ cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, con
 }
 
 // One segment per index of dequant_group_gemm: all `m` rows of x, outputs stacked.
-__global__ void k_index_segs(const int32_t* __restrict__ indices, int A, int64_t m, int nt, Seg* __restrict__ segs,
-                             int32_t* __restrict__ tile_prefix) {
+// An index outside [0, num_experts) gets an empty segment (and kDevBadExpert), so
+// no kernel ever reads that expert's metadata.
+__global__ void k_index_segs(const int32_t* __restrict__ indices, int A, int num_experts, int64_t m, int nt,
+                             Seg* __restrict__ segs, int32_t* __restrict__ tile_prefix) {
+  __shared__ int s_tiles[1024];
   const int a = threadIdx.x;
-  const int tiles = static_cast<int>((m + nt - 1) / nt);
-  if (a < A) segs[a] = make_int4(indices != nullptr ? indices[a] : a, 0, static_cast<int>(a * m), static_cast<int>(m));
-  if (a <= A) tile_prefix[a] = a * tiles;
+  int tiles = 0;
+  if (a < A) {
+    const int e = indices != nullptr ? indices[a] : a;
+    const bool ok = e >= 0 && e < num_experts;
+    if (!ok) set_device_error(kDevBadExpert);
+    segs[a] = make_int4(ok ? e : 0, 0, static_cast<int>(a * m), ok ? static_cast<int>(m) : 0);
+    tiles = ok ? static_cast<int>((m + nt - 1) / nt) : 0;
+  }
+  s_tiles[a] = tiles;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int v = (a >= off) ? s_tiles[a - off] : 0;
+    __syncthreads();
+    s_tiles[a] += v;
+    __syncthreads();
+  }
+  if (a < A) tile_prefix[a] = s_tiles[a] - tiles;
+  if (a == A - 1) tile_prefix[A] = s_tiles[a];
 }
 
-cudaError_t launch_build_index_segs(const int32_t* indices, int num_indices, int64_t m, int nt, Seg* segs,
-                                    int32_t* tile_prefix, cudaStream_t stream) {
-  k_index_segs<<<1, 1024, 0, stream>>>(indices, num_indices, m, nt, segs, tile_prefix);
+cudaError_t launch_build_index_segs(const int32_t* indices, int num_indices, int num_experts, int64_t m, int nt,
+                                    Seg* segs, int32_t* tile_prefix, cudaStream_t stream) {
+  if (num_indices <= 0 || num_indices > 1024) return cudaErrorInvalidValue;
+  k_index_segs<<<1, 1024, 0, stream>>>(indices, num_indices, num_experts, m, nt, segs, tile_prefix);
   return cudaGetLastError();
 }
 
@@ -356,6 +389,7 @@ __global__ void k_combine(const __half* __restrict__ y_perm, const int32_t* __re
   for (int d = threadIdx.x * 2; d < D; d += blockDim.x * 2) {
     float2 acc = make_float2(0.f, 0.f);
     for (int j = 0; j < k; ++j) {
+      if (order[j] < 0) continue;  // slot with an invalid expert id (recorded by k_count)
       const float2 y = __half22float2(*reinterpret_cast<const __half2*>(y_perm + static_cast<int64_t>(order[j]) * D + d));
       if (fp32_sum) {
         acc.x += y.x;

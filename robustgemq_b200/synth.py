@@ -39,9 +39,12 @@ def random_packed_linear(out_features: int, in_features: int, nbits: int, group_
     N, K = out_features, in_features
     codes = torch.randint(0, 2 ** nbits, (N, K), generator=gen, device=device, dtype=torch.int32).to(torch.uint8)
     G = K // group_size
-    rng = 0.1 * (0.75 + 0.5 * torch.rand((G, N), generator=gen, device=device))
+    # codes uniform over a per-group range r with the zero-point mid-range give a
+    # weight std of r/sqrt(12); r ~ 0.07 matches N(0, 0.02) weights
+    rng = 0.07 * (0.75 + 0.5 * torch.rand((G, N), generator=gen, device=device))
     scale = (rng / (2 ** nbits - 1)).half()
-    zero = torch.randint(0, 2 ** nbits, (G, N), generator=gen, device=device).float()
+    qmax = 2 ** nbits - 1
+    zero = (qmax / 2.0 + torch.randint(-1, 2, (G, N), generator=gen, device=device).float() * (qmax // 4)).round()
     zeros = (-(zero * scale.float())).half()
     return PackedLinear(W_q=pack_codes(codes, nbits), scales=scale.contiguous(), zeros=zeros.contiguous(),
                         W_nbits=nbits, group_size=group_size, in_features=K, out_features=N)
