@@ -3,8 +3,10 @@
 
 Headline workload: OLMoE-shaped 16-layer MoE stack, decode at
 batch 1, 8, 32 and 64. One step = one pass of the 16-layer stack at each batch
-size; layers are chained with the decoder's residual add fused into the combine
-(x <- x + moe_l(x)), each batch size replayed as one CUDA graph. ``value`` =
+size, each batch size replayed as one CUDA graph; layer l reads its own seeded
+N(0, 1) input (the normalised hidden state a decoder feeds its MoE; chaining
+un-normalised MoE outputs would overflow fp16), rotated over 4 input sets so the
+routing changes from step to step. ``value`` =
 algorithmic HBM bytes of all passes (packed weights + fp16 scales/zeros of every
 expert the routing hits, the gate weights, activations in/out) / device time, in
 GB/s, summed over ranks (``--gpus N`` runs N independent replicas: weak scaling).
@@ -119,15 +121,20 @@ def build_stack(n_layers, device, seed0):
     return blocks
 
 
-def stack_forward(blocks, x, one_token, time_stages=False):
+def stack_forward(blocks, xs, one_token, time_stages=False, outs=None):
+    """Layer l reads its own input xs[l] (a normalised hidden state stands in for the
+    residual stream after RMSNorm, which an un-normalised MoE chain lacks) and
+    writes outs[l]. Returns the stacked outputs."""
     from robustgemq_b200 import _lib
 
-    flags = _lib.FWD_RESIDUAL | (_lib.FWD_ONE_TOKEN if one_token else 0)
+    flags = _lib.FWD_ONE_TOKEN if one_token else 0
     if time_stages:
         flags |= _lib.FWD_TIME_STAGES
-    for blk in blocks:
-        x, _ = blk._run(x, flags, want_logits=False)
-    return x
+    res = []
+    for l, blk in enumerate(blocks):
+        y, _ = blk._run(xs[l], flags, want_logits=False)
+        res.append(y)
+    return res
 
 
 def stage_times(blk):
@@ -140,17 +147,18 @@ def stage_times(blk):
     return list(arr)
 
 
-def decode_bytes(blocks, expert_bytes, x, one_token):
-    """Algorithmic HBM bytes of one stack pass from its actual routing (untimed)."""
+def decode_bytes(blocks, expert_bytes, xs):
+    """Algorithmic HBM bytes of one stack pass from its actual routing (untimed):
+    hit experts' packed words + scales/zeros, gate weights, activations in/out."""
     import torch
 
-    B, D = x.shape
+    B, D = xs[0].shape
     total = 0
-    for blk, eb in zip(blocks, expert_bytes):
-        _, idx, _ = blk.route(x)
+    for l, (blk, eb) in enumerate(zip(blocks, expert_bytes)):
+        _, idx, _ = blk.route(xs[l])
         hit = torch.unique(idx).tolist()
-        total += sum(eb[e] for e in hit) + blk.num_experts * D * 2 + 3 * B * D * 2
-        x = stack_forward([blk], x, one_token)
+        assert 0 <= min(hit) and max(hit) < blk.num_experts
+        total += sum(eb[e] for e in hit) + blk.num_experts * D * 2 + 2 * B * D * 2
     return total
 
 
@@ -170,11 +178,12 @@ def run_ours(args, rank, world, local_rank):
     D = blocks[0].hidden_dim
     n_sets = 4
     gen = torch.Generator(device=device).manual_seed(7 + rank)
-    inputs = {B: [torch.randn((B, D), generator=gen, device=device).half() for _ in range(n_sets)] for B in batches}
+    L = args.layers
+    # n_sets input sets per batch size, each [L, B, D]: layer l's normalised input
+    inputs = {B: [torch.randn((L, B, D), generator=gen, device=device).half() for _ in range(n_sets)]
+              for B in batches}
     # per-batch algorithmic bytes, averaged over the input sets
-    bytes_per_pass = {}
-    for B in batches:
-        bytes_per_pass[B] = sum(decode_bytes(blocks, expert_bytes, x, B == 1) for x in inputs[B]) / n_sets
+    bytes_per_pass = {B: sum(decode_bytes(blocks, expert_bytes, xs) for xs in inputs[B]) / n_sets for B in batches}
     # warm the workspaces, then capture one graph per batch size
     static_in = {B: inputs[B][0].clone() for B in batches}
     graphs, static_out = {}, {}
@@ -190,25 +199,26 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     setup_s = time.time() - t0
 
-    def step(i, per_batch_ms=None):
+    def step(i):
         for B in batches:
             static_in[B].copy_(inputs[B][i % n_sets])
             graphs[B].replay()
 
     for i in range(args.warmup):
         step(i)
-    # per-batch timing (untimed by the driver; for the breakdown)
+    # per-batch timing (outside the timed region; for the breakdown)
     per_b = {}
     for B in batches:
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(3, args.steps // 2)
         torch.cuda.synchronize()
         s.record()
-        for i in range(max(3, args.steps // 2)):
+        for i in range(reps):
             static_in[B].copy_(inputs[B][i % n_sets])
             graphs[B].replay()
         e.record()
         torch.cuda.synchronize()
-        per_b[B] = s.elapsed_time(e) / max(3, args.steps // 2)
+        per_b[B] = s.elapsed_time(e) / reps
 
     clocks = Clocks() if rank == 0 else None
     if world > 1:
@@ -225,7 +235,7 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(stop)
-    clk = clocks.stop([local_rank + r for r in range(world)] if world > 1 else [torch.cuda.current_device()]) if clocks else None
+    clk = clocks.stop(list(range(world)) if world > 1 else [torch.cuda.current_device()]) if clocks else None
     ms_t = torch.tensor([ms], device=device)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
@@ -233,26 +243,30 @@ def run_ours(args, rank, world, local_rank):
     step_bytes = sum(bytes_per_pass.values())
     value = world * step_bytes * args.steps / (ms_max * 1e-3) / 1e9
 
-    # e2e through the block API with pinned host buffers (eager calls, one rank's view)
+    # e2e through the block API: every step copies its per-layer inputs from pinned
+    # host memory and reads every layer's output back (eager calls)
     host_in = {B: [t.cpu().pin_memory() for t in inputs[B]] for B in batches}
-    host_out = {B: torch.empty((B, D), dtype=torch.float16).pin_memory() for B in batches}
-    dev_in = {B: torch.empty((B, D), dtype=torch.float16, device=device) for B in batches}
-    for i in range(2):
+    host_out = {B: torch.empty((L, B, D), dtype=torch.float16).pin_memory() for B in batches}
+    dev_in = {B: torch.empty((L, B, D), dtype=torch.float16, device=device) for B in batches}
+
+    def e2e_step(i):
         for B in batches:
             dev_in[B].copy_(host_in[B][i % n_sets], non_blocking=True)
-            host_out[B].copy_(stack_forward(blocks, dev_in[B], B == 1), non_blocking=True)
+            outs = stack_forward(blocks, dev_in[B], B == 1)
+            host_out[B].copy_(torch.stack(outs), non_blocking=True)
+
+    for i in range(2):
+        e2e_step(i)
     torch.cuda.synchronize()
     e_steps = max(3, args.steps // 2)
     es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     es.record()
     for i in range(e_steps):
-        for B in batches:
-            dev_in[B].copy_(host_in[B][i % n_sets], non_blocking=True)
-            host_out[B].copy_(stack_forward(blocks, dev_in[B], B == 1), non_blocking=True)
+        e2e_step(i)
     ee.record()
     torch.cuda.synchronize()
     e2e_ms = es.elapsed_time(ee) / e_steps
-    h2d = sum(B * D * 2 for B in batches)
+    h2d = sum(L * B * D * 2 for B in batches)
 
     # stage breakdown + dominant-stage roofline (eager, stage events)
     stage_ms = {}
@@ -260,12 +274,11 @@ def run_ours(args, rank, world, local_rank):
         acc = [0.0] * 6
         reps = 3
         for i in range(reps):
-            x = inputs[B][i % n_sets]
-            for blk in blocks:
-                x2 = stack_forward([blk], x, B == 1, time_stages=True)
+            xs = inputs[B][i % n_sets]
+            for l, blk in enumerate(blocks):
+                stack_forward([blk], xs[l:l + 1], B == 1, time_stages=True)
                 st = stage_times(blk)
                 acc = [a + s for a, s in zip(acc, st)]
-                x = x2
         stage_ms[B] = [a / reps for a in acc]
     names = _lib.STAGES
     dom_b, dom_s = max(((B, s) for B in batches for s in range(6)), key=lambda bs: stage_ms[bs[0]][bs[1]])
@@ -273,7 +286,7 @@ def run_ours(args, rank, world, local_rank):
     dom_bytes = None
     if names[dom_s] in ("up", "down"):
         share = {"up": 2.0 / 3.0, "down": 1.0 / 3.0}[names[dom_s]]  # w1+w3 vs w2 of each expert (equal shapes)
-        weights = bytes_per_pass[dom_b] - args.layers * (blocks[0].num_experts * D * 2 + 3 * dom_b * D * 2)
+        weights = bytes_per_pass[dom_b] - args.layers * (blocks[0].num_experts * D * 2 + 2 * dom_b * D * 2)
         dom_bytes = weights * share / args.layers
     dom_ms = stage_ms[dom_b][dom_s] / args.layers
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_bytes else None
@@ -306,8 +319,9 @@ def run_ours(args, rank, world, local_rank):
                      "achieved": round(achieved, 1) if achieved else None, "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 3) if achieved else None, "traffic": None,
                      "peak_source": peak_src},
-        "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": h2d, "path": "QuantFusedOlmoeMoEBlock._run per layer, eager, pinned host I/O"},
+        "e2e": {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d,
+                "path": "QuantFusedOlmoeMoEBlock per layer (eager C-ABI calls), pinned host in/out every step"},
         "gpu_launches": launches * args.steps,
         "clocks": clk, "setup_s": round(setup_s, 1),
     }
@@ -319,10 +333,11 @@ def run_ours(args, rank, world, local_rank):
 
 
 def kernel_launches(blocks, batches):
-    """Kernels of ours per step (counted from the pipeline): one-token path 9 per layer
+    """Kernels of ours per step, counted from the pipeline: one-token path 9 per layer
     (router, top-k, 2 up partials, 2 reduces, down partial, reduce, combine); n-token
-    path 9 (router, top-k, memset, count, scan, scatter, up, down, combine)."""
-    return sum(len(blocks) * 9 for _ in batches)
+    path 8 (router, top-k, count, scan, scatter, up, down, combine; the counter reset
+    is a memset node)."""
+    return sum(len(blocks) * (9 if B == 1 else 8) for B in batches)
 
 
 def run_prefill(args, device, bf16_peak, bf16_sus):
@@ -339,10 +354,13 @@ def run_prefill(args, device, bf16_peak, bf16_sus):
     x0 = torch.randn((T, shp["hidden"]), device=device).half()
 
     def fwd(x, time_stages=False):
-        flags = _lib.FWD_RESIDUAL | (_lib.FWD_TIME_STAGES if time_stages else 0)
+        # every layer reads the same normalised input (routing comes from the given
+        # per-layer logits); outputs are written and discarded
+        flags = _lib.FWD_TIME_STAGES if time_stages else 0
+        y = None
         for blk, lg in zip(blocks, logits):
-            x, _ = blk._run(x, flags, want_logits=False, logits_in=lg)
-        return x
+            y, _ = blk._run(x, flags, want_logits=False, logits_in=lg)
+        return y
 
     for _ in range(2):
         fwd(x0)
@@ -360,7 +378,7 @@ def run_prefill(args, device, bf16_peak, bf16_sus):
     # stage times on the first layer
     x = x0
     blk = blocks[0]
-    blk._run(x, _lib.FWD_RESIDUAL | _lib.FWD_TIME_STAGES, want_logits=False, logits_in=logits[0])
+    blk._run(x, _lib.FWD_TIME_STAGES, want_logits=False, logits_in=logits[0])
     st = stage_times(blk)
     up_flops = T * k * 4 * D * F
     dn_flops = T * k * 2 * D * F
@@ -384,7 +402,7 @@ def cpu_baseline(blk, inputs, seconds):
     from oracle import cpu_baseline as cb
 
     layer = cb.layer_from_block(blk)
-    xs = {B: v[0].float().cpu().numpy() for B, v in inputs.items()}
+    xs = {B: v[0][0].float().cpu().numpy() for B, v in inputs.items()}
     r = cb.time_decode(layer, xs, seconds)
     r["cores"] = torch.get_num_threads()
     return r

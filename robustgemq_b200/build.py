@@ -20,7 +20,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libgemq_b200.so"
-SOURCES = ["gemq_api.cu", "kernels_misc.cu", "kernels_tc.cu", "kernels_simt.cu"]
+SOURCES = ["gemq_api.cu", "kernels_misc.cu", "kernels_route.cu", "kernels_decode.cu", "kernels_tc.cu",
+           "kernels_simt.cu"]
 HEADERS = ["gemq_common.cuh", "gemq_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -124,6 +124,10 @@ struct Carver {
 
 int choose_nt(int64_t rows_per_expert) { return rows_per_expert > 48 ? kNtLarge : kNtSmall; }
 
+// Up to this many tokens the router runs as one fused gate-GEMV + top-k launch;
+// beyond it, as a tensor-core GEMM followed by the top-k kernel.
+constexpr int64_t kSmallRouteTokens = 256;
+
 // Runs one grouped GEMM, tensor cores when the shape allows, CUDA cores otherwise.
 // The segments must have been built with the nt this returns through `nt_used`.
 bool use_tc(const GemmArgs& a, bool force_simt) { return !force_simt && tc_gemm_supported(a); }
@@ -300,8 +304,7 @@ size_t gemq_gemv_workspace_size(const gemq_proj_t* proj, int32_t num_rows) {
   if (proj == nullptr || num_rows <= 0) return 0;
   const int splits = gemv_default_splits(proj->k, proj->n, num_rows, device_sm_count());
   Carver c(nullptr);
-  c.take<float>(static_cast<size_t>(splits) * num_rows * proj->n);
-  c.take<float>(static_cast<size_t>(splits) * num_rows * proj->n);
+  c.take<float>(2ull * splits * num_rows * proj->n);
   return c.off + 256;
 }
 
@@ -316,7 +319,8 @@ int gemq_dequant_gemv(const gemq_proj_t* proj, const uint16_t* x, uint16_t* out,
   const int splits = gemv_default_splits(proj->k, proj->n, 1, device_sm_count());
   Carver c(workspace);
   float* part = c.take<float>(static_cast<size_t>(splits) * proj->n);
-  GEMQ_CUDA(launch_gemv_partials(to_dev(*proj), nullptr, 1, x, 0, nullptr, part, splits, s), "gemv");
+  GemvSrc src{kGemvX, reinterpret_cast<const __half*>(x), nullptr, 0, nullptr, 0, 0, 0};
+  GEMQ_CUDA(launch_gemv(to_dev(*proj), nullptr, nullptr, 1, src, part, splits, s), "gemv");
   GEMQ_CUDA(launch_gemv_reduce(part, splits, 1, proj->n, out, s), "gemv reduce");
   return GEMQ_OK;
 }
@@ -335,13 +339,13 @@ int gemq_fused_up_proj(const gemq_proj_t* w1, const gemq_proj_t* w3, const uint1
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int splits = gemv_default_splits(w1->k, w1->n, num_idx, device_sm_count());
   Carver c(workspace);
-  float* p1 = c.take<float>(static_cast<size_t>(splits) * num_idx * w1->n);
-  float* p3 = c.take<float>(static_cast<size_t>(splits) * num_idx * w1->n);
+  float* p1 = c.take<float>(2ull * splits * num_idx * w1->n);  // [w1, w3][split][a][n]
+  float* p3 = p1 + static_cast<size_t>(splits) * num_idx * w1->n;
   ProjDev d1 = to_dev(*w1), d3 = to_dev(*w3);
   d3.nbits = d1.nbits;            // fused_dequant_bmm.py:55-57: w3 read with w1's nbits
   d3.wq_strides = d1.wq_strides;  // and w1's word offsets (check_w1_w3_aligned)
-  GEMQ_CUDA(launch_gemv_partials(d1, idx, num_idx, x, 0, nullptr, p1, splits, s), "up w1");
-  GEMQ_CUDA(launch_gemv_partials(d3, idx, num_idx, x, 0, nullptr, p3, splits, s), "up w3");
+  GemvSrc src{kGemvX, reinterpret_cast<const __half*>(x), nullptr, 0, nullptr, 0, 0, 0};
+  GEMQ_CUDA(launch_gemv(d1, &d3, idx, num_idx, src, p1, splits, s), "up projection");
   GEMQ_CUDA(launch_gemv_reduce(p1, splits, num_idx, w1->n, x1, s), "reduce x1");
   GEMQ_CUDA(launch_gemv_reduce(p3, splits, num_idx, w1->n, x3, s), "reduce x3");
   return GEMQ_OK;
@@ -358,7 +362,9 @@ int gemq_fused_down_proj(const gemq_proj_t* w2, const uint16_t* x1, const uint16
   const int splits = gemv_default_splits(w2->k, w2->n, num_idx, device_sm_count());
   Carver c(workspace);
   float* p = c.take<float>(static_cast<size_t>(splits) * num_idx * w2->n);
-  GEMQ_CUDA(launch_gemv_partials(to_dev(*w2), idx, num_idx, x1, w2->k, x3, p, splits, s), "down");
+  GemvSrc src{kGemvSwiGLU, reinterpret_cast<const __half*>(x1), reinterpret_cast<const __half*>(x3), w2->k,
+              nullptr, 0, 0, 0};
+  GEMQ_CUDA(launch_gemv(to_dev(*w2), nullptr, idx, num_idx, src, p, splits, s), "down");
   GEMQ_CUDA(launch_gemv_reduce(p, splits, num_idx, w2->n, x2, s), "reduce x2");
   return GEMQ_OK;
 }
@@ -454,7 +460,6 @@ struct FwdBufs {
   uint16_t *w_perm = nullptr, *x_perm = nullptr, *h_perm = nullptr, *y_perm = nullptr;
   uint16_t *s_h = nullptr, *s_out = nullptr;
   float *part_up = nullptr, *part_dn = nullptr, *part_s = nullptr, *part_s2 = nullptr;
-  uint16_t *x1 = nullptr, *x3 = nullptr, *x2 = nullptr, *s1 = nullptr, *s3 = nullptr, *sh = nullptr, *s2 = nullptr;
   size_t bytes = 0;
   int splits_up = 1, splits_dn = 1, splits_s = 1, splits_s2 = 1;
 };
@@ -478,20 +483,13 @@ FwdBufs carve(const gemq_layer_t* L, int64_t T, uint32_t flags, void* base, cons
   if (flags & GEMQ_FWD_ONE_TOKEN) {
     b.splits_up = gemv_default_splits(D, F, k, L->num_sms);
     b.splits_dn = gemv_default_splits(F, D, k, L->num_sms);
-    b.part_up = c.take<float>(2ull * b.splits_up * k * F);
-    b.x1 = c.take<uint16_t>(static_cast<size_t>(k) * F);
-    b.x3 = c.take<uint16_t>(static_cast<size_t>(k) * F);
+    b.part_up = c.take<float>(2ull * b.splits_up * k * F);  // [w1, w3][split][a][F]
     b.part_dn = c.take<float>(static_cast<size_t>(b.splits_dn) * k * D);
-    b.x2 = c.take<uint16_t>(static_cast<size_t>(k) * D);
     if (d.has_shared) {
       b.splits_s = gemv_default_splits(D, Fs, 1, L->num_sms);
       b.splits_s2 = gemv_default_splits(Fs, D, 1, L->num_sms);
       b.part_s = c.take<float>(2ull * b.splits_s * Fs);
-      b.s1 = c.take<uint16_t>(Fs);
-      b.s3 = c.take<uint16_t>(Fs);
-      b.sh = c.take<uint16_t>(Fs);
       b.part_s2 = c.take<float>(static_cast<size_t>(b.splits_s2) * D);
-      b.s2 = c.take<uint16_t>(D);
     }
   } else {
     b.counts = c.take<int32_t>(E);
@@ -518,6 +516,16 @@ int run_router(gemq_layer_t* L, const uint16_t* x, int64_t T, void* logits_out, 
   if (tm) tm->begin(GEMQ_STAGE_ROUTE);
   const gemq_layer_desc_t& d = L->d;
   const bool fp32_logits = logits_given || d.router == GEMQ_ROUTER_FP32;
+  const bool norm = d.norm_topk_prob != 0;
+  const bool fp16_softmax = (flags & GEMQ_FWD_FP16_SOFTMAX) != 0;
+  if (!logits_given && T <= kSmallRouteTokens) {
+    // small batches: gate dot products + top-k in one launch
+    GEMQ_CUDA(launch_route_small(x, T, d.hidden, d.gate_weight, d.num_experts, d.router == GEMQ_ROUTER_FP32,
+                                 logits_out, d.top_k, norm, fp16_softmax, idx, w, s),
+              "router");
+    if (tm) tm->end(GEMQ_STAGE_ROUTE);
+    return GEMQ_OK;
+  }
   if (!logits_given) {
     GemmArgs a{};
     a.mode = d.router == GEMQ_ROUTER_FP32 ? GemmMode::kDenseF32 : GemmMode::kDenseF16;
@@ -537,19 +545,17 @@ int run_router(gemq_layer_t* L, const uint16_t* x, int64_t T, void* logits_out, 
     a.out_cols = d.num_experts;
     a.num_sms = L->num_sms;
     a.nt = choose_nt(T);
-    const bool tc = T >= 64 && !(flags & GEMQ_FWD_FORCE_SIMT) && tc_gemm_supported(a);
+    const bool tc = !(flags & GEMQ_FWD_FORCE_SIMT) && tc_gemm_supported(a);
     if (tc) {
       GEMQ_CUDA(launch_build_index_segs(nullptr, 1, 1, T, a.nt, one_seg, one_tp, s), "router segments");
       GEMQ_CUDA(launch_tc_gemm(a, s), "router gemm");
     } else {
-      GEMQ_CUDA(launch_router_simt(x, T, d.gate_weight, d.num_experts, d.hidden, d.router == GEMQ_ROUTER_FP32,
-                                   logits_out, s),
-                "router");
+      a.nt = 32;
+      GEMQ_CUDA(launch_build_index_segs(nullptr, 1, 1, T, a.nt, one_seg, one_tp, s), "router segments");
+      GEMQ_CUDA(launch_simt_gemm(a, s), "router gemm");
     }
   }
-  GEMQ_CUDA(launch_topk(logits_out, fp32_logits, T, d.num_experts, d.top_k, d.norm_topk_prob != 0,
-                        (flags & GEMQ_FWD_FP16_SOFTMAX) != 0, idx, w, s),
-            "topk");
+  GEMQ_CUDA(launch_topk(logits_out, fp32_logits, T, d.num_experts, d.top_k, norm, fp16_softmax, idx, w, s), "topk");
   if (tm) tm->end(GEMQ_STAGE_ROUTE);
   return GEMQ_OK;
 }
@@ -559,36 +565,29 @@ int forward_one_token(gemq_layer_t* L, const uint16_t* x, uint16_t* out, const i
   const uint16_t* residual = (flags & GEMQ_FWD_RESIDUAL) ? x : nullptr;
   const gemq_layer_desc_t& d = L->d;
   const int k = d.top_k, D = d.hidden, F = d.inter;
-  float* p1 = b.part_up;
-  float* p3 = b.part_up + static_cast<size_t>(b.splits_up) * k * F;
+  // up: w1 and w3 (read with w1's nbits/offsets, fused_dequant_bmm.py:98) in one launch
   tm.begin(GEMQ_STAGE_UP);
-  GEMQ_CUDA(launch_gemv_partials(L->w1, idx, k, x, 0, nullptr, p1, b.splits_up, s), "up w1");
-  GEMQ_CUDA(launch_gemv_partials(L->w3_as_w1, idx, k, x, 0, nullptr, p3, b.splits_up, s), "up w3");
-  GEMQ_CUDA(launch_gemv_reduce(p1, b.splits_up, k, F, b.x1, s), "x1");
-  GEMQ_CUDA(launch_gemv_reduce(p3, b.splits_up, k, F, b.x3, s), "x3");
+  const GemvSrc xs{kGemvX, reinterpret_cast<const __half*>(x), nullptr, 0, nullptr, 0, 0, 0};
+  GEMQ_CUDA(launch_gemv(L->w1, &L->w3_as_w1, idx, k, xs, b.part_up, b.splits_up, s), "up projection");
   tm.end(GEMQ_STAGE_UP);
+  // down: reduces the up partials to fp16 x1/x3 and forms fp32 silu(x1)*x3 itself
   tm.begin(GEMQ_STAGE_DOWN);
-  GEMQ_CUDA(launch_gemv_partials(L->w2, idx, k, b.x1, F, b.x3, b.part_dn, b.splits_dn, s), "down");
-  GEMQ_CUDA(launch_gemv_reduce(b.part_dn, b.splits_dn, k, D, b.x2, s), "x2");
+  const GemvSrc hs{kGemvPartF32, nullptr, nullptr, 0, b.part_up, b.splits_up, k, F};
+  GEMQ_CUDA(launch_gemv(L->w2, nullptr, idx, k, hs, b.part_dn, b.splits_dn, s), "down projection");
   tm.end(GEMQ_STAGE_DOWN);
-  const uint16_t* add = nullptr;
+  const float* shared_part = nullptr;
   if (d.has_shared) {
     const int Fs = L->shared_inter;
     tm.begin(GEMQ_STAGE_SHARED);
-    float* q1 = b.part_s;
-    float* q3 = b.part_s + static_cast<size_t>(b.splits_s) * Fs;
-    GEMQ_CUDA(launch_gemv_partials(L->sw1, nullptr, 1, x, 0, nullptr, q1, b.splits_s, s), "shared w1");
-    GEMQ_CUDA(launch_gemv_partials(L->sw3, nullptr, 1, x, 0, nullptr, q3, b.splits_s, s), "shared w3");
-    GEMQ_CUDA(launch_gemv_reduce(q1, b.splits_s, 1, Fs, b.s1, s), "s1");
-    GEMQ_CUDA(launch_gemv_reduce(q3, b.splits_s, 1, Fs, b.s3, s), "s3");
-    GEMQ_CUDA(launch_swiglu_f16(b.s1, b.s3, Fs, b.sh, s), "shared swiglu");
-    GEMQ_CUDA(launch_gemv_partials(L->sw2, nullptr, 1, b.sh, 0, nullptr, b.part_s2, b.splits_s2, s), "shared w2");
-    GEMQ_CUDA(launch_gemv_reduce(b.part_s2, b.splits_s2, 1, D, b.s2, s), "s2");
+    GEMQ_CUDA(launch_gemv(L->sw1, &L->sw3, nullptr, 1, xs, b.part_s, b.splits_s, s), "shared up");
+    const GemvSrc ss{kGemvPartF16, nullptr, nullptr, 0, b.part_s, b.splits_s, 1, Fs};
+    GEMQ_CUDA(launch_gemv(L->sw2, nullptr, nullptr, 1, ss, b.part_s2, b.splits_s2, s), "shared down");
     tm.end(GEMQ_STAGE_SHARED);
-    add = b.s2;
+    shared_part = b.part_s2;
   }
   tm.begin(GEMQ_STAGE_COMBINE);
-  GEMQ_CUDA(launch_decode_combine(b.x2, w, k, D, add, residual, out, s), "combine");
+  GEMQ_CUDA(launch_decode_combine(b.part_dn, b.splits_dn, k, D, w, shared_part, b.splits_s2, residual, out, s),
+            "combine");
   tm.end(GEMQ_STAGE_COMBINE);
   return GEMQ_OK;
 }

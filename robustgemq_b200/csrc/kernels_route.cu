@@ -1,0 +1,439 @@
+// Routing, dispatch and combine of the quantized MoE block.
+//
+// Reference behaviour restated (paths relative to the RobustGEMQ root):
+//   router     gemq/inference/moe_block.py:790-797 (fp16 logits), 549-556 (fp32 logits),
+//              280-283 (Mixtral one-token: fp16 softmax / top-k / renorm)
+//   dispatch   gemq/inference/moe_block.py:804-810 (one_hot / nonzero / where / gather)
+//   combine    gemq/inference/moe_block.py:799-812 (fp16 index_add_ in ascending expert order)
+#include <cuda_fp16.h>
+
+#include <cfloat>
+
+#include "gemq_common.cuh"
+#include "gemq_internal.h"
+
+namespace gemq {
+
+namespace {
+
+constexpr int kMaxExperts = 256;
+
+// Softmax + top-k + optional renormalisation of one token's logits by one warp.
+// Softmax in fp32 with expf; selection takes the larger probability first and the
+// lower expert id on ties; NaN ranks above every number (torch.topk's order), so
+// the selected ids are always valid. fp16_softmax rounds the probabilities, their
+// sum and the quotients to fp16 as the fp16 tensors of moe_block.py:280-283 do.
+template <typename GetLogit>
+__device__ __forceinline__ void topk_warp(GetLogit get, int E, int k, int norm, int fp16_softmax,
+                                          int32_t* __restrict__ idx_out, __half* __restrict__ w_out) {
+  const int lane = threadIdx.x & 31;
+  float v[kMaxExperts / 32];
+  float mx = -FLT_MAX;
+#pragma unroll
+  for (int i = 0; i < kMaxExperts / 32; ++i) {
+    const int e = i * 32 + lane;
+    const float l = (e < E) ? get(e) : -FLT_MAX;
+    v[i] = l;
+    mx = fmaxf(mx, l);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxExperts / 32; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = (e < E) ? expf(v[i] - mx) : 0.f;
+    sum += v[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+  for (int i = 0; i < kMaxExperts / 32; ++i) {
+    const int e = i * 32 + lane;
+    float pr = (e < E) ? v[i] / sum : -1.f;
+    if (fp16_softmax && e < E) pr = __half2float(__float2half_rn(pr));
+    v[i] = pr;
+  }
+  auto key = [](float a) { return (a != a) ? FLT_MAX : a; };
+  float wsel[16];
+  int isel[16];
+  float wsum = 0.f;
+  for (int j = 0; j < k; ++j) {
+    float best = -FLT_MAX, bestv = 0.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kMaxExperts / 32; ++i) {
+      const int e = i * 32 + lane;
+      if (e < E && v[i] != -3.f && (key(v[i]) > best || (key(v[i]) == best && e < bi))) {
+        best = key(v[i]);
+        bestv = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const float ov = __shfl_xor_sync(0xffffffffu, bestv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bestv = ov;
+        bi = oi;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxExperts / 32; ++i)
+      if (i * 32 + lane == bi) v[i] = -3.f;
+    wsel[j] = bestv;
+    isel[j] = bi;
+    wsum += bestv;
+  }
+  if (lane == 0) {
+    if (fp16_softmax) wsum = __half2float(__float2half_rn(wsum));
+    for (int j = 0; j < k; ++j) {
+      float w = wsel[j];
+      if (norm) w = w / wsum;
+      idx_out[j] = isel[j];
+      w_out[j] = __float2half_rn(w);
+    }
+  }
+}
+
+// One warp per token, logits from global memory (the tensor-core router's output
+// or given logits).
+__global__ void k_topk(const void* __restrict__ logits, int logits_fp32, int64_t T, int E, int k, int norm,
+                       int fp16_softmax, int32_t* __restrict__ topk_idx, __half* __restrict__ topk_w) {
+  const int64_t t = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  if (t >= T) return;
+  auto get = [&](int e) {
+    return logits_fp32 ? static_cast<const float*>(logits)[t * E + e]
+                       : __half2float(static_cast<const __half*>(logits)[t * E + e]);
+  };
+  topk_warp(get, E, k, norm, fp16_softmax, topk_idx + t * k, topk_w + t * k);
+}
+
+// Small-batch router: one CTA per token computes the E gate dot products (fp32
+// accumulation; the fp16 router rounds each logit to fp16 as F.linear's fp16 output
+// does) and the top-k in one launch.
+constexpr int kRouteThreads = 256;
+
+__global__ void __launch_bounds__(kRouteThreads) k_route_small(const __half* __restrict__ x, int D,
+                                                               const __half* __restrict__ gate, int E, int fp32_logits,
+                                                               void* __restrict__ logits_out, int k, int norm,
+                                                               int fp16_softmax, int32_t* __restrict__ topk_idx,
+                                                               __half* __restrict__ topk_w) {
+  extern __shared__ uint4 s_x4[];
+  __shared__ float s_logit[kMaxExperts];
+  const int64_t t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + t * D);
+  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) s_x4[i] = xr[i];
+  __syncthreads();
+  for (int e = warp; e < E; e += kRouteThreads / 32) {
+    const uint4* gr = reinterpret_cast<const uint4*>(gate + static_cast<int64_t>(e) * D);
+    float acc = 0.f;
+    for (int i = lane; i < D / 8; i += 32) {
+      const uint4 gv = __ldg(gr + i);
+      const uint4 xv = s_x4[i];
+      const __half2* gh = reinterpret_cast<const __half2*>(&gv);
+      const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = __half22float2(xh[j]);
+        const float2 b = __half22float2(gh[j]);
+        acc = fmaf(a.x, b.x, acc);
+        acc = fmaf(a.y, b.y, acc);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      if (fp32_logits) {
+        s_logit[e] = acc;
+        if (logits_out) static_cast<float*>(logits_out)[t * E + e] = acc;
+      } else {
+        const __half h = __float2half_rn(acc);
+        s_logit[e] = __half2float(h);
+        if (logits_out) static_cast<__half*>(logits_out)[t * E + e] = h;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 0) topk_warp([&](int e) { return s_logit[e]; }, E, k, norm, fp16_softmax, topk_idx + t * k, topk_w + t * k);
+}
+
+// ------------------------------------------------------------------ dispatch (large batches)
+__global__ void k_count(const int32_t* __restrict__ topk_idx, int64_t P, int E, int32_t* __restrict__ counts) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= P) return;
+  const int e = topk_idx[i];
+  if (e < 0 || e >= E) {
+    set_device_error(kDevBadExpert);
+    return;
+  }
+  atomicAdd(&counts[e], 1);
+}
+
+// Single block: exclusive scans over experts (E <= 1024).
+__global__ void k_scan_segs(const int32_t* __restrict__ counts, int E, int nt, Seg* __restrict__ segs,
+                            int32_t* __restrict__ tile_prefix, int32_t* __restrict__ cursor) {
+  __shared__ int s_rows[1024];
+  __shared__ int s_tiles[1024];
+  const int e = threadIdx.x;
+  const int c = (e < E) ? counts[e] : 0;
+  s_rows[e] = c;
+  s_tiles[e] = (c + nt - 1) / nt;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int a = (e >= off) ? s_rows[e - off] : 0;
+    const int b = (e >= off) ? s_tiles[e - off] : 0;
+    __syncthreads();
+    s_rows[e] += a;
+    s_tiles[e] += b;
+    __syncthreads();
+  }
+  if (e < E) {
+    const int start = s_rows[e] - c;
+    segs[e] = make_int4(e, start, start, c);
+    tile_prefix[e] = s_tiles[e] - (c + nt - 1) / nt;
+    cursor[e] = start;
+    if (e == E - 1) tile_prefix[E] = s_tiles[e];
+  }
+}
+
+// One warp per slot: claim a row, record it, copy the token's activation row. Rows
+// within a segment are in arrival order, which changes no result: each row is
+// computed alone and the combine visits a token's experts in ascending id. A slot
+// whose expert id is out of range (k_count recorded kDevBadExpert) gets no row and
+// slot_pos -1, which the combine skips.
+__global__ void k_scatter(const int32_t* __restrict__ topk_idx, const __half* __restrict__ topk_w,
+                          const __half* __restrict__ x, int64_t P, int k, int E, int D, int32_t* __restrict__ cursor,
+                          int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm, __half* __restrict__ x_perm) {
+  const int64_t slot = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (slot >= P) return;
+  const int e = topk_idx[slot];
+  if (e < 0 || e >= E) {
+    if (lane == 0) slot_pos[slot] = -1;
+    return;
+  }
+  int pos = 0;
+  if (lane == 0) {
+    pos = atomicAdd(&cursor[e], 1);
+    slot_pos[slot] = pos;
+    w_perm[pos] = topk_w[slot];
+  }
+  pos = __shfl_sync(0xffffffffu, pos, 0);
+  const int64_t t = slot / k;
+  const uint4* src = reinterpret_cast<const uint4*>(x + t * D);
+  uint4* dst = reinterpret_cast<uint4*>(x_perm + static_cast<int64_t>(pos) * D);
+  for (int i = lane; i < D / 8; i += 32) dst[i] = src[i];
+}
+
+// ------------------------------------------------------------------ dispatch (small batches)
+// One launch: every CTA recounts the (small) slot list in shared memory, scans it,
+// and places its own 8 slots at deterministic positions (rank among earlier slots
+// of the same expert); CTA 0 also publishes counts, segments and the tile prefix.
+constexpr int kSmallDispatchMaxSlots = 4096;
+
+__device__ __forceinline__ void warp_exclusive_scan_256(const int* in, int* out, int E, int lane) {
+  // E <= 256: each lane owns 8 consecutive entries
+  int vals[8];
+  int local = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane * 8 + i;
+    vals[i] = (e < E) ? in[e] : 0;
+    local += vals[i];
+  }
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  int run = incl - local;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane * 8 + i;
+    if (e < E) out[e] = run;
+    run += vals[i];
+  }
+  if (lane == 31) out[E] = incl;
+}
+
+__global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restrict__ topk_idx,
+                                                        const __half* __restrict__ topk_w, const __half* __restrict__ x,
+                                                        int P, int k, int E, int D, int nt, int32_t* __restrict__ counts,
+                                                        Seg* __restrict__ segs, int32_t* __restrict__ tile_prefix,
+                                                        int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm,
+                                                        __half* __restrict__ x_perm) {
+  __shared__ int s_idx[kSmallDispatchMaxSlots];
+  __shared__ int s_cnt[kMaxExperts];
+  __shared__ int s_tiles[kMaxExperts];
+  __shared__ int s_start[kMaxExperts + 1];
+  __shared__ int s_tstart[kMaxExperts + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    const int e = topk_idx[i];
+    s_idx[i] = e;
+    if (e >= 0 && e < E) atomicAdd(&s_cnt[e], 1);
+    else if (blockIdx.x == 0) set_device_error(kDevBadExpert);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_tiles[e] = (s_cnt[e] + nt - 1) / nt;
+  __syncthreads();
+  if (warp == 0) warp_exclusive_scan_256(s_cnt, s_start, E, lane);
+  if (warp == 1) warp_exclusive_scan_256(s_tiles, s_tstart, E, lane);
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      counts[e] = s_cnt[e];
+      segs[e] = make_int4(e, s_start[e], s_start[e], s_cnt[e]);
+      tile_prefix[e] = s_tstart[e];
+    }
+    if (threadIdx.x == 0) tile_prefix[E] = s_tstart[E];
+  }
+  const int slot = blockIdx.x * 8 + warp;
+  if (slot >= P) return;
+  const int e = s_idx[slot];
+  if (e < 0 || e >= E) {
+    if (lane == 0) slot_pos[slot] = -1;
+    return;
+  }
+  int rank = 0;
+  for (int s = lane; s < slot; s += 32) rank += (s_idx[s] == e) ? 1 : 0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+  const int pos = s_start[e] + rank;
+  if (lane == 0) {
+    slot_pos[slot] = pos;
+    w_perm[pos] = topk_w[slot];
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(slot / k) * D);
+  uint4* dst = reinterpret_cast<uint4*>(x_perm + static_cast<int64_t>(pos) * D);
+  for (int i = lane; i < D / 8; i += 32) dst[i] = src[i];
+}
+
+// ------------------------------------------------------------------ combine
+// out[t] = ((0 + y_{e1}) + y_{e2}) + ... over the token's experts in ascending id,
+// every partial sum rounded to fp16: the fp16 index_add_ of forward_n_tokens
+// (moe_block.py:799-812). fp32_sum: one fp32 sum, one rounding. `add` (DeepSeek
+// shared experts) is added in fp16 afterwards (moe_block.py:575), then `residual`.
+__global__ void k_combine(const __half* __restrict__ y_perm, const int32_t* __restrict__ slot_pos,
+                          const int32_t* __restrict__ topk_idx, int64_t T, int k, int D, int fp32_sum,
+                          const __half* __restrict__ add, const __half* __restrict__ residual,
+                          __half* __restrict__ out) {
+  const int64_t t = blockIdx.x;
+  int order[16];
+  int eid[16];
+  for (int j = 0; j < k; ++j) {
+    order[j] = slot_pos[t * k + j];
+    eid[j] = topk_idx[t * k + j];
+  }
+  for (int a = 1; a < k; ++a) {  // insertion sort by expert id
+    int e = eid[a], o = order[a], b = a - 1;
+    while (b >= 0 && eid[b] > e) {
+      eid[b + 1] = eid[b];
+      order[b + 1] = order[b];
+      --b;
+    }
+    eid[b + 1] = e;
+    order[b + 1] = o;
+  }
+  for (int d = threadIdx.x * 2; d < D; d += blockDim.x * 2) {
+    float2 acc = make_float2(0.f, 0.f);
+    for (int j = 0; j < k; ++j) {
+      if (order[j] < 0) continue;  // slot with an invalid expert id
+      const float2 y =
+          __half22float2(*reinterpret_cast<const __half2*>(y_perm + static_cast<int64_t>(order[j]) * D + d));
+      if (fp32_sum) {
+        acc.x += y.x;
+        acc.y += y.y;
+      } else {
+        acc.x = __half2float(__float2half_rn(acc.x + y.x));
+        acc.y = __half2float(__float2half_rn(acc.y + y.y));
+      }
+    }
+    __half2 r = __floats2half2_rn(acc.x, acc.y);
+    if (add != nullptr) {
+      const float2 a2 = __half22float2(*reinterpret_cast<const __half2*>(add + t * D + d));
+      const float2 r2 = __half22float2(r);
+      r = __floats2half2_rn(r2.x + a2.x, r2.y + a2.y);
+    }
+    if (residual != nullptr) {
+      const float2 a2 = __half22float2(*reinterpret_cast<const __half2*>(residual + t * D + d));
+      const float2 r2 = __half22float2(r);
+      r = __floats2half2_rn(r2.x + a2.x, r2.y + a2.y);
+    }
+    *reinterpret_cast<__half2*>(out + t * D + d) = r;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_topk(const void* logits, bool logits_fp32, int64_t T, int E, int k, bool norm, bool fp16_softmax,
+                        int32_t* topk_idx, uint16_t* topk_w, cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  k_topk<<<static_cast<unsigned>((T * 32 + 255) / 256), 256, 0, stream>>>(
+      logits, logits_fp32 ? 1 : 0, T, E, k, norm ? 1 : 0, fp16_softmax ? 1 : 0, topk_idx,
+      reinterpret_cast<__half*>(topk_w));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route_small(const uint16_t* x, int64_t T, int D, const uint16_t* gate, int E, bool fp32_logits,
+                               void* logits_out, int k, bool norm, bool fp16_softmax, int32_t* topk_idx,
+                               uint16_t* topk_w, cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const size_t smem = static_cast<size_t>(D) * 2;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_route_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  k_route_small<<<static_cast<unsigned>(T), kRouteThreads, smem, stream>>>(
+      reinterpret_cast<const __half*>(x), D, reinterpret_cast<const __half*>(gate), E, fp32_logits ? 1 : 0,
+      logits_out, k, norm ? 1 : 0, fp16_softmax ? 1 : 0, topk_idx, reinterpret_cast<__half*>(topk_w));
+  return cudaGetLastError();
+}
+
+bool small_dispatch_ok(int64_t P, int E) { return P <= kSmallDispatchMaxSlots && E <= kMaxExperts; }
+
+cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t T, int k,
+                            int E, int D, int nt, int32_t* counts, int32_t* cursor, Seg* segs, int32_t* tile_prefix,
+                            int32_t* slot_pos, uint16_t* w_perm, uint16_t* x_perm, cudaStream_t stream) {
+  const int64_t P = T * k;
+  cudaError_t err;
+  if (small_dispatch_ok(P, E)) {
+    const unsigned grid = static_cast<unsigned>(P > 0 ? (P + 7) / 8 : 1);
+    k_dispatch_small<<<grid, 256, 0, stream>>>(topk_idx, reinterpret_cast<const __half*>(topk_w),
+                                                reinterpret_cast<const __half*>(x), static_cast<int>(P), k, E, D, nt,
+                                                counts, segs, tile_prefix, slot_pos, reinterpret_cast<__half*>(w_perm),
+                                                reinterpret_cast<__half*>(x_perm));
+    return cudaGetLastError();
+  }
+  err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, stream);
+  if (err != cudaSuccess) return err;
+  k_count<<<static_cast<unsigned>((P + 255) / 256), 256, 0, stream>>>(topk_idx, P, E, counts);
+  if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  k_scan_segs<<<1, 1024, 0, stream>>>(counts, E, nt, segs, tile_prefix, cursor);
+  if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  k_scatter<<<static_cast<unsigned>((P * 32 + 255) / 256), 256, 0, stream>>>(
+      topk_idx, reinterpret_cast<const __half*>(topk_w), reinterpret_cast<const __half*>(x), P, k, E, D, cursor,
+      slot_pos, reinterpret_cast<__half*>(w_perm), reinterpret_cast<__half*>(x_perm));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const uint16_t* y_perm, const int32_t* slot_pos, const int32_t* topk_idx, int64_t T, int k,
+                           int D, bool fp32_sum, const uint16_t* add, const uint16_t* residual, uint16_t* out,
+                           cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  k_combine<<<static_cast<unsigned>(T), 256, 0, stream>>>(
+      reinterpret_cast<const __half*>(y_perm), slot_pos, topk_idx, T, k, D, fp32_sum ? 1 : 0,
+      reinterpret_cast<const __half*>(add), reinterpret_cast<const __half*>(residual), reinterpret_cast<__half*>(out));
+  return cudaGetLastError();
+}
+
+}  // namespace gemq

@@ -9,13 +9,16 @@
 //
 // Warp roles (448 threads, one CTA per SM, grid-stride over work items):
 //   warp 0      TMA producer: activation tile (128B swizzle), packed int32 words
-//               (8 word rows x 128 features) and fp16 scale/zero rows, no multicast
+//               (2/4/8 word rows x 128 features, by bit-width) and fp16 scale/zero
+//               rows; no multicast
 //   warp 1      TMEM allocation + single-thread tcgen05.mma issue + commits
 //   warps 2-5   epilogue: tcgen05.ld -> mode-specific rounding -> global stores
 //   warps 6-13  dequant: packed words -> fp16 via fma.rn.f16 (bit-exact with
 //               utils.py:206-210) written as the 128B-swizzled K-major A tile
-// Dense modes (router gate) load A by TMA and skip the dequant warps.
-// Every wait is bounded (gemq_common.cuh); on expiry all roles drain and return.
+// Accumulators are double-buffered in TMEM so the epilogue of one item overlaps the
+// MMAs of the next. Dense modes (router gate) load A by TMA and skip the dequant
+// warps. Every wait is bounded (gemq_common.cuh); on expiry all roles drain and
+// return.
 #include <cudaTypedefs.h>
 
 #include "gemq_common.cuh"
@@ -27,16 +30,20 @@ namespace {
 
 constexpr int kBK = 64;        // K per stage: one 128-byte swizzle row of fp16
 constexpr int kBM = 128;       // features per tile (UMMA M)
-constexpr int kWordRows = 8;   // packed word rows per stage (covers 64 k for b in {1,2,3,4})
+constexpr int kWordRows = 8;   // word-row slots per stage (covers 64 k for b in {1,2,3,4})
 constexpr int kThreads = 448;  // 14 warps
-constexpr int kEpiWarp0 = 2;
 constexpr int kDqWarp0 = 6;
 constexpr int kNumDqThreads = 256;
-constexpr int kStages = 4;
 constexpr int kAStages = 2;
+constexpr int kSmemBudget = 225 * 1024;
 
 __host__ __device__ constexpr int round_up(int v, int m) { return (v + m - 1) / m * m; }
 __host__ __device__ constexpr int tmem_cols_for(int c) { return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512; }
+__host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
+
+// Word rows a 64-wide K tile needs: 64 / (32 / b) for b in {1, 2, 4}; 3-bit tiles
+// straddle words (ten codes per word) and need up to 8.
+__host__ __device__ constexpr int word_rows_for(int nb) { return nb == 1 ? 2 : nb == 2 ? 4 : 8; }
 
 template <int NT, GemmMode MODE>
 struct Cfg {
@@ -50,14 +57,21 @@ struct Cfg {
   static constexpr int kSzOff = kActBytes + kMats * kWqBytes;           // dequant: scales, zeros
   static constexpr int kStageRaw = kDense ? kActBytes + kATile : kActBytes + kMats * (kWqBytes + 2 * kSzBytes);
   static constexpr int kStageBytes = round_up(kStageRaw, 1024);
-  static constexpr int kTxBytes = kDense ? kActBytes + kATile : kActBytes + kMats * (kWqBytes + 2 * kSzBytes);
-  static constexpr int kARingOff = kStages * kStageBytes;
   static constexpr int kARingBytes = kDense ? 0 : kAStages * kMats * kATile;
+  static constexpr int kStages = cmin(8, (kSmemBudget - kARingBytes - 2048) / kStageBytes);
+  static constexpr int kARingOff = kStages * kStageBytes;
   static constexpr int kBarOff = kARingOff + kARingBytes;
-  static constexpr int kNumBars = 2 * kStages + 2 * kAStages + 3;
+  static constexpr int kNumBars = 2 * kStages + 2 * kAStages + 5;
   static constexpr int kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;  // + tmem slot + alignment slack
-  static constexpr int kTmemCols = tmem_cols_for(kMats * NT);
+  static constexpr int kAccCols = kMats * NT;                             // one accumulator buffer
+  static constexpr int kTmemCols = tmem_cols_for(2 * kAccCols);
   static constexpr uint32_t kIdesc = idesc_f16_f32(kBM, NT);
+  static_assert(kStages >= 2, "shared memory budget too small");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget exceeded");
+  // bytes one stage delivers for a given bit-width (dense: fixed)
+  __host__ __device__ static constexpr uint32_t tx_bytes(int nb) {
+    return kDense ? kActBytes + kATile : kActBytes + kMats * (word_rows_for(nb) * kBM * 4 + 2 * kSzBytes);
+  }
 };
 
 struct KArgs {
@@ -76,6 +90,11 @@ struct KArgs {
   void* out;
   int64_t out_ld;
   const __half* row_weight;
+};
+
+// Packed-word maps, one per box height (2, 4, 8 word rows) and matrix.
+struct WordMaps {
+  CUtensorMap m[2][3];
 };
 
 struct Work {
@@ -116,7 +135,7 @@ __device__ __forceinline__ int work_total(const KArgs& p) { return __ldg(p.tile_
 
 // ---------------------------------------------------------------- dequant of one row
 // Thread owns feature row `n` of the 128 x 64 A tile; writes 16-byte chunks
-// [c0, c1) (k = 8c .. 8c+7) of that row. `w` holds the 8 loaded word rows of this
+// [c0, c1) (k = 8c .. 8c+7) of that row. `w` holds the loaded word rows of this
 // feature column; for 3-bit the tile starts at code slot `phase` of word 0.
 template <int NB>
 __device__ __forceinline__ void dq_row_pow2(const uint32_t (&w)[kWordRows], __half2 s2, __half2 z2, uint8_t* row_base,
@@ -142,8 +161,6 @@ __device__ __forceinline__ void dq_row_3bit(const uint32_t (&w)[kWordRows], __ha
       uint32_t o[4];
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        constexpr int dummy = 0;
-        (void)dummy;
         const int j = 8 * c + 2 * m;
         const int a = (P + j) / 10, sa = (P + j) % 10;
         const int b = (P + j + 1) / 10, sb = (P + j + 1) % 10;
@@ -198,13 +215,13 @@ __device__ __forceinline__ void store_one(const KArgs& p, int64_t row, int col, 
 // ---------------------------------------------------------------- the kernel
 template <int NT, GemmMode MODE>
 __global__ void __launch_bounds__(kThreads, 1)
-    k_moe_tc(const KArgs p, const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w0,
+    k_moe_tc(const KArgs p, const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ WordMaps tm_words,
              const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ CUtensorMap tm_z0,
-             const __grid_constant__ CUtensorMap tm_w1, const __grid_constant__ CUtensorMap tm_s1,
-             const __grid_constant__ CUtensorMap tm_z1) {
+             const __grid_constant__ CUtensorMap tm_s1, const __grid_constant__ CUtensorMap tm_z1) {
   using C = Cfg<NT, MODE>;
   constexpr bool kDense = C::kDense;
   constexpr int kMats = C::kMats;
+  constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
@@ -212,9 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = bars + kStages;
   uint64_t* afull = bars + 2 * kStages;
   uint64_t* aempty = afull + kAStages;
-  uint64_t* acc_full = aempty + kAStages;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* drain = acc_full + 2;
+  uint64_t* acc_full = aempty + kAStages;   // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint64_t* drain = acc_full + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
 
   const int warp = threadIdx.x >> 5;
@@ -229,22 +246,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&afull[s], kNumDqThreads);
       mbar_init(&aempty[s], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
     mbar_init(drain, 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_act);
-    tma_prefetch_desc(&tm_w0);
+    tma_prefetch_desc(&tm_words.m[0][2]);
     if (!kDense) {
       tma_prefetch_desc(&tm_s0);
       tma_prefetch_desc(&tm_z0);
-      if (kMats == 2) {
-        tma_prefetch_desc(&tm_w1);
-        tma_prefetch_desc(&tm_s1);
-        tma_prefetch_desc(&tm_z1);
-      }
     }
   }
   if (warp == 1) {
@@ -266,23 +280,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
         const Work wk = decode_work<NT>(p, w, kDense);
-        const int eps = kDense ? 1 : 32 / max(wk.nb, 1);
+        const int nb = kDense ? 4 : min(max(wk.nb, 1), 4);
+        const int eps = 32 / nb;
+        const int box = nb == 1 ? 0 : nb == 2 ? 1 : 2;  // word-row map index
+        const uint32_t tx = C::tx_bytes(nb);
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&empty[s], ph ^ 1u, kDevTimeoutTmaEmpty)) { ok = false; break; }
           uint8_t* st = smem + s * C::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], C::kTxBytes);
+          mbar_arrive_expect_tx(&full[s], tx);
           const int k0 = kt * kBK;
           tma_load_2d(st, &tm_act, &full[s], k0, wk.act_row);
           if constexpr (kDense) {
-            tma_load_2d(st + C::kActBytes, &tm_w0, &full[s], k0, wk.n0);
+            tma_load_2d(st + C::kActBytes, &tm_words.m[0][2], &full[s], k0, wk.n0);
           } else {
             const int wr = k0 / eps;
             const int sr = k0 / p.group_size;
-            tma_load_2d(st + C::kWqOff, &tm_w0, &full[s], wk.n0, wk.wrow0 + wr);
+            tma_load_2d(st + C::kWqOff, &tm_words.m[0][box], &full[s], wk.n0, wk.wrow0 + wr);
             tma_load_2d(st + C::kSzOff, &tm_s0, &full[s], wk.n0, wk.srow0 + sr);
             tma_load_2d(st + C::kSzOff + C::kSzBytes, &tm_z0, &full[s], wk.n0, wk.srow0 + sr);
             if constexpr (kMats == 2) {
-              tma_load_2d(st + C::kWqOff + C::kWqBytes, &tm_w1, &full[s], wk.n0, wk.wrow1 + wr);
+              tma_load_2d(st + C::kWqOff + C::kWqBytes, &tm_words.m[1][box], &full[s], wk.n0, wk.wrow1 + wr);
               tma_load_2d(st + C::kSzOff + 2 * C::kSzBytes, &tm_s1, &full[s], wk.n0, wk.srow1 + sr);
               tma_load_2d(st + C::kSzOff + 3 * C::kSzBytes, &tm_z1, &full[s], wk.n0, wk.srow1 + sr);
             }
@@ -301,10 +318,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int s = 0, as = 0;
-      uint32_t ph = 0, aph = 0, accph = 0;
+      uint32_t ph = 0, aph = 0;
+      int it = 0;
       bool ok = true;
-      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
-        if (!mbar_wait(acc_empty, accph ^ 1u, kDevTimeoutAccEmpty)) break;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t d_base = tmem + static_cast<uint32_t>(buf * C::kAccCols);
+        if (!mbar_wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1u, kDevTimeoutAccEmpty)) break;
         tc_fence_after();
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&full[s], ph, kDevTimeoutTmaFull)) { ok = false; break; }
@@ -319,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                            : smem_u32(smem + C::kARingOff + (as * kMats + m) * C::kATile);
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk) {
-              umma_f16(tmem + static_cast<uint32_t>(m * NT), sdesc_sw128(a_addr + kk * 32),
+              umma_f16(d_base + static_cast<uint32_t>(m * NT), sdesc_sw128(a_addr + kk * 32),
                        sdesc_sw128(act_addr + kk * 32), C::kIdesc, (kt | kk) != 0 ? 1u : 0u);
             }
           }
@@ -331,8 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
-        umma_commit(acc_full);
-        accph ^= 1u;
+        umma_commit(&acc_full[buf]);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, kDevTimeoutDrain);
@@ -340,11 +359,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < kDqWarp0) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * q) << 16);
-    uint32_t accph = 0;
-    for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    int it = 0;
+    for (int w = blockIdx.x; w < total; w += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * C::kAccCols);
       const Work wk = decode_work<NT>(p, w, kDense);
-      if (!mbar_wait(acc_full, accph, kDevTimeoutAccFull)) break;
+      if (!mbar_wait(&acc_full[buf], (it >> 1) & 1, kDevTimeoutAccFull)) break;
       tc_fence_after();
       const int col = wk.n0 + 32 * q + lane;
       for (int c0 = 0; c0 < NT; c0 += 16) {
@@ -365,8 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(acc_empty);
-      accph ^= 1u;
+      mbar_arrive(&acc_empty[buf]);
     }
   } else if constexpr (!kDense) {
     // ------------------------------------------------------------ dequant
@@ -385,6 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (nb < 1 || nb > 4) {
         if (dt == 0) set_device_error(kDevBadBits);
       }
+      const int rows_needed = word_rows_for(nb);
       for (int kt = 0; kt < KT; ++kt) {
         if (!mbar_wait(&full[s], ph, kDevTimeoutTmaFull)) { ok = false; break; }
         if (!mbar_wait(&aempty[as], aph ^ 1u, kDevTimeoutAEmpty)) { ok = false; break; }
@@ -392,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t* wcol = reinterpret_cast<const uint32_t*>(st + C::kWqOff + mat * C::kWqBytes) + n;
         uint32_t wv[kWordRows];
 #pragma unroll
-        for (int r = 0; r < kWordRows; ++r) wv[r] = wcol[r * kBM];
+        for (int r = 0; r < kWordRows; ++r) wv[r] = (r < rows_needed) ? wcol[r * kBM] : 0u;
         const __half sh = reinterpret_cast<const __half*>(st + C::kSzOff + (2 * mat) * C::kSzBytes)[n];
         const __half zh = reinterpret_cast<const __half*>(st + C::kSzOff + (2 * mat + 1) * C::kSzBytes)[n];
         __syncwarp();
@@ -441,22 +461,34 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_word_maps(CUtensorMap (&maps)[3], const ProjDev& w) {
+  const uint32_t heights[3] = {2, 4, 8};
+  for (int i = 0; i < 3; ++i) {
+    if (!make_map(&maps[i], w.wq, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, w.n, w.wq_rows, kBM, heights[i],
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
+      return false;
+  }
+  return true;
+}
+
 template <int NT, GemmMode MODE>
 cudaError_t launch_t(const GemmArgs& a, cudaStream_t stream) {
   using C = Cfg<NT, MODE>;
-  CUtensorMap m_act, m_w0, m_s0, m_z0, m_w1, m_s1, m_z1;
-  const int K = C::kDense ? a.w0.k : a.w0.k;
+  CUtensorMap m_act, m_s0, m_z0, m_s1, m_z1;
+  WordMaps words;
+  const int K = a.w0.k;
   if (!make_map(&m_act, a.act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, static_cast<uint64_t>(a.act_rows), 64, NT,
                 CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   if constexpr (C::kDense) {
-    if (!make_map(&m_w0, a.dense_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, a.w0.n, 64, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!make_map(&words.m[0][2], a.dense_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, a.w0.n, 64, kBM,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
-    m_s0 = m_z0 = m_w1 = m_s1 = m_z1 = m_w0;
+    for (int i = 0; i < 3; ++i) words.m[0][i] = words.m[1][i] = words.m[0][2];
+    m_s0 = m_z0 = m_s1 = m_z1 = m_act;
   } else {
     const uint64_t srows = static_cast<uint64_t>(a.w0.num_experts) * (a.w0.k / a.w0.group_size);
-    if (!make_map(&m_w0, a.w0.wq, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, a.w0.n, a.w0.wq_rows, kBM, kWordRows,
-                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+    if (!make_word_maps(words.m[0], a.w0) ||
         !make_map(&m_s0, a.w0.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w0.n, srows, kBM, 1,
                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !make_map(&m_z0, a.w0.zeros, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w0.n, srows, kBM, 1,
@@ -464,15 +496,14 @@ cudaError_t launch_t(const GemmArgs& a, cudaStream_t stream) {
       return cudaErrorInvalidValue;
     if constexpr (C::kMats == 2) {
       const uint64_t srows1 = static_cast<uint64_t>(a.w1.num_experts) * (a.w1.k / a.w1.group_size);
-      if (!make_map(&m_w1, a.w1.wq, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, a.w1.n, a.w1.wq_rows, kBM, kWordRows,
-                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      if (!make_word_maps(words.m[1], a.w1) ||
           !make_map(&m_s1, a.w1.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w1.n, srows1, kBM, 1,
                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
           !make_map(&m_z1, a.w1.zeros, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w1.n, srows1, kBM, 1,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     } else {
-      m_w1 = m_w0;
+      for (int i = 0; i < 3; ++i) words.m[1][i] = words.m[0][i];
       m_s1 = m_s0;
       m_z1 = m_z0;
     }
@@ -494,9 +525,13 @@ cudaError_t launch_t(const GemmArgs& a, cudaStream_t stream) {
   p.out_ld = a.out_ld;
   p.row_weight = reinterpret_cast<const __half*>(a.row_weight);
   auto kern = k_moe_tc<NT, MODE>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-  if (err != cudaSuccess) return err;
-  kern<<<a.num_sms, kThreads, C::kSmemBytes, stream>>>(p, m_act, m_w0, m_s0, m_z0, m_w1, m_s1, m_z1);
+  static bool attr_set = false;  // set once per instantiation (outside any graph capture)
+  if (!attr_set) {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    attr_set = true;
+  }
+  kern<<<a.num_sms, kThreads, C::kSmemBytes, stream>>>(p, m_act, words, m_s0, m_z0, m_s1, m_z1);
   return cudaGetLastError();
 }
 

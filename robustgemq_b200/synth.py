@@ -2,10 +2,9 @@
 
 Bit mixes use exact counts that hit the mean bit-width, permuted per layer by a
 seeded generator (mean 2.5 -> {2: 5/8, 3: 1/4, 4: 1/8} of E; 2.75 -> {2: 1/2,
-3: 1/4, 4: 1/4}; 3.0 -> {2: 1/4, 3: 1/2, 4: 1/4}). Codes are uniform in
-[0, 2^b); scales and zero-points follow what min-max RTN of N(0, 0.02) weights
-produces (scale ~ range / (2^b - 1), zero ~ mid-range), stored in the packed
-layout of ``quant.PackedLinear`` / ``QuantFused*.from_hf``.
+3: 1/4, 4: 1/4}; 3.0 -> {2: 1/4, 3: 1/2, 4: 1/4}). Weights are N(0, 0.02) in
+fp16, quantised per group with the reference's min-max RTN and stored in the
+packed layout of ``quant.PackedLinear`` / ``QuantFused*.from_hf``.
 """
 
 from __future__ import annotations
@@ -15,7 +14,7 @@ from typing import Dict, List, Optional
 
 import torch
 
-from .quant import PackedLinear, pack_codes
+from .quant import PackedLinear, pack_linear, rtn_quantize
 
 BIT_MIX = {
     2.5: {2: 5 / 8, 3: 1 / 4, 4: 1 / 8},
@@ -36,18 +35,10 @@ def bit_mix(num_experts: int, mean_bits: float, seed: int) -> List[int]:
 
 def random_packed_linear(out_features: int, in_features: int, nbits: int, group_size: int, gen: torch.Generator,
                          device) -> PackedLinear:
-    N, K = out_features, in_features
-    codes = torch.randint(0, 2 ** nbits, (N, K), generator=gen, device=device, dtype=torch.int32).to(torch.uint8)
-    G = K // group_size
-    # codes uniform over a per-group range r with the zero-point mid-range give a
-    # weight std of r/sqrt(12); r ~ 0.07 matches N(0, 0.02) weights
-    rng = 0.07 * (0.75 + 0.5 * torch.rand((G, N), generator=gen, device=device))
-    scale = (rng / (2 ** nbits - 1)).half()
-    qmax = 2 ** nbits - 1
-    zero = (qmax / 2.0 + torch.randint(-1, 2, (G, N), generator=gen, device=device).float() * (qmax // 4)).round()
-    zeros = (-(zero * scale.float())).half()
-    return PackedLinear(W_q=pack_codes(codes, nbits), scales=scale.contiguous(), zeros=zeros.contiguous(),
-                        W_nbits=nbits, group_size=group_size, in_features=K, out_features=N)
+    """N(0, 0.02) fp16 weights, min-max RTN per group along the input dim, packed."""
+    W = (torch.randn((out_features, in_features), generator=gen, device=device) * 0.02).half()
+    Q, s, z = rtn_quantize(W, nbits, group_size)
+    return pack_linear(Q, s, z, nbits, group_size)
 
 
 def random_block(family_cls, config, hidden: int, inter: int, num_experts: int, mean_bits: float, group_size: int,

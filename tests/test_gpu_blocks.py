@@ -138,6 +138,28 @@ def test_empty_and_single_token_inputs():
     assert torch.isfinite(y1).all()
 
 
+def test_out_of_range_expert_ids_are_recorded_not_followed():
+    """A routing table with an expert id outside [0, E) never reaches memory: the slot
+    is dropped, the device error word records it (code 8), the other slots combine."""
+    from robustgemq_b200 import _lib
+
+    blk, d = block_from_golden("olmoe")
+    x = cuda(d["x"])
+    idx = cuda(d["route_idx"]).clone()
+    w = cuda(d["route_w"])
+    ref = blk.forward_routed(x, idx, w)
+    assert _lib.device_error() == 0
+    bad = idx.clone()
+    bad[0, 1] = 1000  # token 0 loses its second expert
+    y = blk.forward_routed(x, bad, w)
+    assert _lib.device_error() == 8
+    assert torch.equal(y[1:], ref[1:])
+    w0 = w.clone()
+    w0[0, 1] = 0.0
+    y0 = blk.forward_routed(x, idx, w0)
+    assert rel_l2(y[0].cpu().numpy(), y0[0].cpu().numpy()) <= 1e-3
+
+
 def test_guards_raise_on_gpu_blocks():
     from robustgemq_b200.inference import check_w1_w3_aligned
 
