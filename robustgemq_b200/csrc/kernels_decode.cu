@@ -3,10 +3,16 @@
 // dequant_gemv.py:118-156.
 //
 // part[mat][s][a][n] = split s of sum_k xin_a[k] * deq(W_{mat, idx[a]})[k, n] in fp32.
-// A block covers 128 output features (4 per lane, 16-byte word loads) of one
-// (matrix, row a) and one K split; its word rows are cut into 8 contiguous runs,
-// one per warp, reduced through shared memory in a fixed order, so every result is
-// bit-reproducible (the reference's fp16 atomics are not, dequant_gemv.py:115).
+// A block covers 128 output features (4 per lane, one 16-byte load = the same word
+// row of 4 features) of one (matrix, row a) and one K split; its word rows are cut
+// into 8 contiguous runs, one per warp, reduced through shared memory in a fixed
+// order, so every result is bit-reproducible (the reference's fp16 atomics are not,
+// dequant_gemv.py:115).
+//
+// Inner loop: two codes per magic-number pair, dequantised with one fma.rn.f16x2
+// (bit-exact with utils.py:206-210); fp16 inputs accumulate with the mixed-precision
+// fma.rn.f32.f16 (exact product, one rounding: identical to converting and using an
+// fp32 fma), fp32 inputs (the one-token path's fp32 SiLU*mul) with fma.rn.f32x2.
 //
 // Input modes (xin):
 //   kGemvX        fp16 rows x[a * x_stride + k]
@@ -29,9 +35,147 @@ constexpr int kGemvCols = 128;
 
 __device__ __forceinline__ float silu_f32(float x) { return x / (1.f + expf(-x)); }
 
-__global__ void __launch_bounds__(kGemvThreads) k_gemv(ProjDev w0, ProjDev w1, const int32_t* __restrict__ idx,
+// acc + a * b with a, b fp16 and one rounding to fp32
+__device__ __forceinline__ float fma_f32_f16(__half a, __half b, float c) {
+  float d;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(__half_as_ushort(a)), "h"(__half_as_ushort(b)), "f"(c));
+  return d;
+}
+
+// (d0, d1) += (a0, a1) * (b0, b1), each lane one rounding
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 A, B, C;\n\t"
+      "mov.b64 A, {%2, %3};\n\t"
+      "mov.b64 B, {%4, %5};\n\t"
+      "mov.b64 C, {%0, %1};\n\t"
+      "fma.rn.f32x2 C, A, B, C;\n\t"
+      "mov.b64 {%0, %1}, C;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// Accumulates one word (codes j = 0..eps-1 at k0 + j) of one feature column.
+// Pair p holds codes (p, p + eps/2): 16 bits apart, so one shift + mask per pair.
+template <int NB, bool XF16>
+__device__ __forceinline__ void word_pow2(uint32_t w, __half2 s2, __half2 z2, const void* xr, float& acc0,
+                                          float& acc1) {
+  constexpr int kEps = 32 / NB, kHalf = kEps / 2;
+  constexpr uint32_t kMask = ((1u << NB) - 1u) * 0x00010001u;
+#pragma unroll
+  for (int j = 0; j < kHalf; ++j) {
+    const __half2 wq = u32_as_h2(dq_pair(((w >> (NB * j)) & kMask) | 0x64006400u, s2, z2));
+    if constexpr (XF16) {
+      const __half* x = static_cast<const __half*>(xr);
+      acc0 = fma_f32_f16(__low2half(wq), x[j], acc0);
+      acc1 = fma_f32_f16(__high2half(wq), x[j + kHalf], acc1);
+    } else {
+      const float* x = static_cast<const float*>(xr);
+      const float2 wf = __half22float2(wq);
+      ffma2(acc0, acc1, x[j], x[j + kHalf], wf.x, wf.y);
+    }
+  }
+}
+
+// 3-bit: ten codes per word (bits 30-31 unused); pair p holds codes (p, p + 5).
+// A word may straddle a scale-group boundary: codes j < b use (sa, za), codes
+// j >= b the next group's (sb, zb) (b = 10 when the word lies in one group).
+template <bool XF16>
+__device__ __forceinline__ void word_3bit(uint32_t w, __half sa, __half za, __half sb, __half zb, int b,
+                                          const void* xr, float& acc0, float& acc1) {
+#pragma unroll
+  for (int j = 0; j < 5; ++j) {
+    const uint32_t t = w >> (3 * j);        // code j at bits 0..2
+    const uint32_t u = w >> (3 * j + 15);   // code j + 5 at bits 0..2
+    const uint32_t m = (t & 7u) | ((u & 7u) << 16) | 0x64006400u;
+    const __half2 s2 = __halves2half2(j >= b ? sb : sa, j + 5 >= b ? sb : sa);
+    const __half2 z2 = __halves2half2(j >= b ? zb : za, j + 5 >= b ? zb : za);
+    const __half2 wq = u32_as_h2(dq_pair(m, s2, z2));
+    if constexpr (XF16) {
+      const __half* x = static_cast<const __half*>(xr);
+      acc0 = fma_f32_f16(__low2half(wq), x[j], acc0);
+      acc1 = fma_f32_f16(__high2half(wq), x[j + 5], acc1);
+    } else {
+      const float* x = static_cast<const float*>(xr);
+      const float2 wf = __half22float2(wq);
+      ffma2(acc0, acc1, x[j], x[j + 5], wf.x, wf.y);
+    }
+  }
+}
+
+template <bool XF16>
+__device__ __forceinline__ void gemv_rows(const ProjDev& w, int e, int nb, int n, int wr0, int wr1, int k0,
+                                          const void* s_x, float (&acc)[4][2]) {
+  const int K = w.k, N = w.n, g = w.group_size;
+  const int32_t* wbase = w.wq + static_cast<int64_t>(w.wq_strides[e]);
+  const int64_t zbase = static_cast<int64_t>(w.zs_strides[e]);
+  const int eps = 32 / nb;
+  int cur_g = -1;
+  __half2 s_c[4], z_c[4];       // scale / zero of the current group, per column
+  auto load_group = [&](int gi, __half2 (&sd)[4], __half2 (&zd)[4]) {
+    const uint2 sv = __ldg(reinterpret_cast<const uint2*>(w.scales + zbase + static_cast<int64_t>(gi) * N + n));
+    const uint2 zv = __ldg(reinterpret_cast<const uint2*>(w.zeros + zbase + static_cast<int64_t>(gi) * N + n));
+    const __half* sp = reinterpret_cast<const __half*>(&sv);
+    const __half* zp = reinterpret_cast<const __half*>(&zv);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      sd[c] = __halves2half2(sp[c], sp[c]);
+      zd[c] = __halves2half2(zp[c], zp[c]);
+    }
+  };
+  constexpr int kXBytes = XF16 ? 2 : 4;
+  const char* xbase = static_cast<const char*>(s_x);
+#pragma unroll 2
+  for (int r = wr0; r < wr1; ++r) {
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wbase + static_cast<int64_t>(r) * N + n));
+    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+    const int kr = r * eps;
+    const int ga = kr / g;
+    if (ga != cur_g) {
+      cur_g = ga;
+      load_group(ga, s_c, z_c);
+    }
+    const void* xr = xbase + static_cast<size_t>(kr - k0) * kXBytes;
+    if (nb == 3) {
+      const int gb = min(kr + 9, K - 1) / g;
+      if (gb == ga) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_c[c]), __low2half(z_c[c]),
+                          10, xr, acc[c][0], acc[c][1]);
+      } else {
+        // codes at k >= gb * g use the next group's scale and zero
+        __half2 s_n[4], z_n[4];
+        load_group(gb, s_n, z_n);
+        const int b = gb * g - kr;  // first code index in the next group (1..9)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_n[c]), __low2half(z_n[c]), b,
+                          xr, acc[c][0], acc[c][1]);
+        cur_g = gb;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          s_c[c] = s_n[c];
+          z_c[c] = z_n[c];
+        }
+      }
+      // codes past K in a ragged last word are zero-padded and their x staged as 0
+    } else if (nb == 2) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) word_pow2<2, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
+    } else if (nb == 4) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) word_pow2<4, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) word_pow2<1, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
+    }
+  }
+}
+
+template <bool XF16>
+__global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1, const int32_t* __restrict__ idx,
                                                        int rows_a, GemvSrc src, float* __restrict__ part, int splits) {
-  extern __shared__ float s_x[];  // inputs of this split's k range
+  extern __shared__ __align__(16) unsigned char s_raw[];  // inputs of this split's k range
   __shared__ float s_red[8][kGemvCols];
   const int slab = blockIdx.x, s = blockIdx.y;
   const int mat = blockIdx.z / rows_a, a = blockIdx.z - mat * rows_a;
@@ -48,78 +192,47 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(ProjDev w0, ProjDev w1, c
     return;
   }
   const int eps = 32 / nb;
-  const int K = w.k, N = w.n, g = w.group_size;
+  const int K = w.k, N = w.n;
   const int rows = (K + eps - 1) / eps;
   const int r0 = static_cast<int>((static_cast<int64_t>(rows) * s) / splits);
   const int r1 = static_cast<int>((static_cast<int64_t>(rows) * (s + 1)) / splits);
   const int k0 = r0 * eps;
-  const int k1 = min(r1 * eps, K);
-  for (int kk = k0 + threadIdx.x; kk < k1; kk += blockDim.x) {
-    float v;
-    if (src.mode == kGemvX) {
-      v = __half2float(src.x[a * src.x_stride + kk]);
-    } else if (src.mode == kGemvSwiGLU) {
-      v = silu_f32(__half2float(src.x[a * src.x_stride + kk])) * __half2float(src.x3[a * src.x_stride + kk]);
-    } else {
-      const int64_t mstride = static_cast<int64_t>(src.part_splits) * src.part_rows * src.part_n;
-      float g1 = 0.f, g3 = 0.f;
-      for (int q = 0; q < src.part_splits; ++q) {
-        const int64_t off = (static_cast<int64_t>(q) * src.part_rows + a) * src.part_n + kk;
-        g1 += src.part[off];
-        g3 += src.part[mstride + off];
-      }
-      const float x1 = __half2float(__float2half_rn(g1));
-      const float x3 = __half2float(__float2half_rn(g3));
-      if (src.mode == kGemvPartF32) {
-        v = silu_f32(x1) * x3;
+  const int kspan = (r1 - r0) * eps;  // padded to whole words; entries past K are 0
+  for (int i = threadIdx.x; i < kspan; i += blockDim.x) {
+    const int kk = k0 + i;
+    float v = 0.f;
+    if (kk < K) {
+      if (src.mode == kGemvX) {
+        v = __half2float(src.x[a * src.x_stride + kk]);
+      } else if (src.mode == kGemvSwiGLU) {
+        v = silu_f32(__half2float(src.x[a * src.x_stride + kk])) * __half2float(src.x3[a * src.x_stride + kk]);
       } else {
-        v = __half2float(__float2half_rn(__half2float(__float2half_rn(silu_f32(x1))) * x3));
+        const int64_t mstride = static_cast<int64_t>(src.part_splits) * src.part_rows * src.part_n;
+        float g1 = 0.f, g3 = 0.f;
+        for (int q = 0; q < src.part_splits; ++q) {
+          const int64_t off = (static_cast<int64_t>(q) * src.part_rows + a) * src.part_n + kk;
+          g1 += src.part[off];
+          g3 += src.part[mstride + off];
+        }
+        const float x1 = __half2float(__float2half_rn(g1));
+        const float x3 = __half2float(__float2half_rn(g3));
+        v = (src.mode == kGemvPartF32) ? silu_f32(x1) * x3
+                                       : __half2float(__float2half_rn(__half2float(__float2half_rn(silu_f32(x1))) * x3));
       }
     }
-    s_x[kk - k0] = v;
+    if constexpr (XF16)
+      reinterpret_cast<__half*>(s_raw)[i] = __float2half_rn(v);  // exact: kGemvX inputs are fp16
+    else
+      reinterpret_cast<float*>(s_raw)[i] = v;
   }
   __syncthreads();
   const int n = slab * kGemvCols + lane * 4;
-  const bool col_ok = n < N;  // N % 4 == 0 is required by the host
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc[4][2] = {};
   const int per = (r1 - r0 + 7) / 8;
   const int wr0 = r0 + warp * per, wr1 = min(r1, wr0 + per);
-  const int32_t* wbase = w.wq + static_cast<int64_t>(w.wq_strides[e]);
-  const int64_t zbase = static_cast<int64_t>(w.zs_strides[e]);
-  const uint32_t mask = (1u << nb) - 1u;
-  int cur_g = -1;
-  __half sh[4], zh[4];
-  if (col_ok) {
-    for (int r = wr0; r < wr1; ++r) {
-      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wbase + static_cast<int64_t>(r) * N + n));
-      const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-      for (int j = 0; j < eps; ++j) {
-        const int kk = r * eps + j;
-        if (kk >= K) break;
-        const int gi = kk / g;
-        if (gi != cur_g) {
-          cur_g = gi;
-          const uint2 sv = __ldg(reinterpret_cast<const uint2*>(w.scales + zbase + static_cast<int64_t>(gi) * N + n));
-          const uint2 zv = __ldg(reinterpret_cast<const uint2*>(w.zeros + zbase + static_cast<int64_t>(gi) * N + n));
-          const __half* sp = reinterpret_cast<const __half*>(&sv);
-          const __half* zp = reinterpret_cast<const __half*>(&zv);
+  if (n < N) gemv_rows<XF16>(w, e, nb, n, wr0, wr1, k0, s_raw, acc);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            sh[c] = sp[c];
-            zh[c] = zp[c];
-          }
-        }
-        const float xv = s_x[kk - k0];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t q = (words[c] >> (j * nb)) & mask;
-          acc[c] = fmaf(xv, __half2float(dq_scalar(q, sh[c], zh[c])), acc[c]);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < 4; ++c) s_red[warp][lane * 4 + c] = acc[c];
+  for (int c = 0; c < 4; ++c) s_red[warp][lane * 4 + c] = acc[c][0] + acc[c][1];
   __syncthreads();
   if (threadIdx.x < kGemvCols) {
     const int nn = slab * kGemvCols + threadIdx.x;
@@ -164,6 +277,24 @@ __global__ void k_decode_combine(const float* __restrict__ part, int splits, int
   out[i] = r;
 }
 
+template <bool XF16>
+cudaError_t launch_gemv_t(const ProjDev& w0, const ProjDev* w1, const int32_t* idx, int rows_a, const GemvSrc& src,
+                          float* part, int splits, cudaStream_t s) {
+  const int nmat = (w1 != nullptr) ? 2 : 1;
+  // a split covers at most cdiv(rows, splits) word rows of <= 32 codes: < k/splits + 64
+  const size_t smem = (XF16 ? 2 : 4) * static_cast<size_t>((w0.k + splits - 1) / splits + 128);
+  static int smem_set = 48 * 1024;
+  if (static_cast<int>(smem) > smem_set) {
+    cudaError_t e =
+        cudaFuncSetAttribute(k_gemv<XF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    smem_set = static_cast<int>(smem);
+  }
+  dim3 grid((w0.n + kGemvCols - 1) / kGemvCols, splits, nmat * rows_a);
+  k_gemv<XF16><<<grid, kGemvThreads, smem, s>>>(w0, w1 != nullptr ? *w1 : w0, idx, rows_a, src, part, splits);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 int gemv_default_splits(int k, int n, int rows_a, int num_sms) {
@@ -176,18 +307,10 @@ int gemv_default_splits(int k, int n, int rows_a, int num_sms) {
 cudaError_t launch_gemv(const ProjDev& w0, const ProjDev* w1, const int32_t* idx, int rows_a, const GemvSrc& src,
                         float* part, int splits, cudaStream_t s) {
   if (rows_a == 0) return cudaSuccess;
-  const int nmat = (w1 != nullptr) ? 2 : 1;
-  // a split covers at most cdiv(rows, splits) + 1 word rows of <= 32 codes each
-  const size_t smem = sizeof(float) * static_cast<size_t>((w0.k + splits - 1) / splits + 64);
-  static int smem_set = 48 * 1024;
-  if (static_cast<int>(smem) > smem_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    smem_set = static_cast<int>(smem);
-  }
-  dim3 grid((w0.n + kGemvCols - 1) / kGemvCols, splits, nmat * rows_a);
-  k_gemv<<<grid, kGemvThreads, smem, s>>>(w0, w1 != nullptr ? *w1 : w0, idx, rows_a, src, part, splits);
-  return cudaGetLastError();
+  // the fast inner loop needs whole words inside one scale group for b in {1, 2, 4}
+  if (w0.group_size % 32 != 0 || (w1 != nullptr && w1->group_size % 32 != 0)) return cudaErrorNotSupported;
+  return src.mode == kGemvX ? launch_gemv_t<true>(w0, w1, idx, rows_a, src, part, splits, s)
+                            : launch_gemv_t<false>(w0, w1, idx, rows_a, src, part, splits, s);
 }
 
 cudaError_t launch_gemv_reduce(const float* part, int splits, int rows_a, int n, uint16_t* out, cudaStream_t s) {

@@ -115,7 +115,7 @@ __global__ void k_topk(const void* __restrict__ logits, int logits_fp32, int64_t
 // Small-batch router: one CTA per token computes the E gate dot products (fp32
 // accumulation; the fp16 router rounds each logit to fp16 as F.linear's fp16 output
 // does) and the top-k in one launch.
-constexpr int kRouteThreads = 256;
+constexpr int kRouteThreads = 1024;  // upper bound; small batches use all of it
 
 __global__ void __launch_bounds__(kRouteThreads) k_route_small(const __half* __restrict__ x, int D,
                                                                const __half* __restrict__ gate, int E, int fp32_logits,
@@ -129,9 +129,11 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_small(const __half* __r
   const uint4* xr = reinterpret_cast<const uint4*>(x + t * D);
   for (int i = threadIdx.x; i < D / 8; i += blockDim.x) s_x4[i] = xr[i];
   __syncthreads();
-  for (int e = warp; e < E; e += kRouteThreads / 32) {
+  const int nwarps = blockDim.x >> 5;
+  for (int e = warp; e < E; e += nwarps) {
     const uint4* gr = reinterpret_cast<const uint4*>(gate + static_cast<int64_t>(e) * D);
     float acc = 0.f;
+#pragma unroll 8
     for (int i = lane; i < D / 8; i += 32) {
       const uint4 gv = __ldg(gr + i);
       const uint4 xv = s_x4[i];
@@ -393,7 +395,8 @@ cudaError_t launch_route_small(const uint16_t* x, int64_t T, int D, const uint16
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  k_route_small<<<static_cast<unsigned>(T), kRouteThreads, smem, stream>>>(
+  const int threads = T <= 16 ? 1024 : 256;  // one CTA per token: fewer tokens, wider CTAs
+  k_route_small<<<static_cast<unsigned>(T), threads, smem, stream>>>(
       reinterpret_cast<const __half*>(x), D, reinterpret_cast<const __half*>(gate), E, fp32_logits ? 1 : 0,
       logits_out, k, norm ? 1 : 0, fp16_softmax ? 1 : 0, topk_idx, reinterpret_cast<__half*>(topk_w));
   return cudaGetLastError();
