@@ -82,21 +82,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may sleep up to `hint_ns` for the phase to
+// complete (it wakes as soon as it does), so waiting warps do not re-issue polls
+// that would steal issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Each sleeping poll lasts at most this long (the bound of every wait is checked
+// between polls).
+constexpr uint32_t kPollSleepNs = 100000;
+
 // Waits until the phase with the given parity has completed. Returns false (and
 // records `code`) if the wait exceeds kWaitLimitNs, or if another thread already
 // recorded an error (so a failed pipeline drains instead of spinning).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(a, parity)) return true;
-    if ((it & 63u) == 0u) {
-      if (device_error_set()) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        set_device_error(code);
-        return false;
-      }
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(a, parity, kPollSleepNs)) return true;
+    if (device_error_set()) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_device_error(code);
+      return false;
     }
   }
 }

@@ -102,18 +102,26 @@ __device__ __forceinline__ void word_3bit(uint32_t w, __half sa, __half za, __ha
   }
 }
 
+// Scale/zero rows of the groups a block's K range touches, staged in shared memory
+// ([group][128 features] fp16 each) so that a group change costs a shared load.
+struct GroupStage {
+  const __half* s;
+  const __half* z;
+  int g0;  // first staged group
+};
+
 template <bool XF16>
-__device__ __forceinline__ void gemv_rows(const ProjDev& w, int e, int nb, int n, int wr0, int wr1, int k0,
-                                          const void* s_x, float (&acc)[4][2]) {
+__device__ __forceinline__ void gemv_rows(const ProjDev& w, int e, int nb, int lane, int n, int wr0, int wr1, int k0,
+                                          const void* s_x, const GroupStage& gs, float (&acc)[4][2]) {
   const int K = w.k, N = w.n, g = w.group_size;
   const int32_t* wbase = w.wq + static_cast<int64_t>(w.wq_strides[e]);
-  const int64_t zbase = static_cast<int64_t>(w.zs_strides[e]);
   const int eps = 32 / nb;
   int cur_g = -1;
-  __half2 s_c[4], z_c[4];       // scale / zero of the current group, per column
+  __half2 s_c[4], z_c[4];  // scale / zero of the current group, per column
   auto load_group = [&](int gi, __half2 (&sd)[4], __half2 (&zd)[4]) {
-    const uint2 sv = __ldg(reinterpret_cast<const uint2*>(w.scales + zbase + static_cast<int64_t>(gi) * N + n));
-    const uint2 zv = __ldg(reinterpret_cast<const uint2*>(w.zeros + zbase + static_cast<int64_t>(gi) * N + n));
+    const int off = (gi - gs.g0) * 128 + lane * 4;
+    const uint2 sv = *reinterpret_cast<const uint2*>(gs.s + off);
+    const uint2 zv = *reinterpret_cast<const uint2*>(gs.z + off);
     const __half* sp = reinterpret_cast<const __half*>(&sv);
     const __half* zp = reinterpret_cast<const __half*>(&zv);
 #pragma unroll
@@ -123,59 +131,74 @@ __device__ __forceinline__ void gemv_rows(const ProjDev& w, int e, int nb, int n
     }
   };
   constexpr int kXBytes = XF16 ? 2 : 4;
+  constexpr int kBatch = 8;  // word rows whose loads are issued before any is used
   const char* xbase = static_cast<const char*>(s_x);
-#pragma unroll 2
-  for (int r = wr0; r < wr1; ++r) {
-    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wbase + static_cast<int64_t>(r) * N + n));
-    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-    const int kr = r * eps;
-    const int ga = kr / g;
-    if (ga != cur_g) {
-      cur_g = ga;
-      load_group(ga, s_c, z_c);
-    }
-    const void* xr = xbase + static_cast<size_t>(kr - k0) * kXBytes;
-    if (nb == 3) {
-      const int gb = min(kr + 9, K - 1) / g;
-      if (gb == ga) {
+  for (int rb = wr0; rb < wr1; rb += kBatch) {
+    uint4 wv[kBatch];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_c[c]), __low2half(z_c[c]),
-                          10, xr, acc[c][0], acc[c][1]);
-      } else {
-        // codes at k >= gb * g use the next group's scale and zero
-        __half2 s_n[4], z_n[4];
-        load_group(gb, s_n, z_n);
-        const int b = gb * g - kr;  // first code index in the next group (1..9)
+    for (int i = 0; i < kBatch; ++i)
+      wv[i] = (rb + i < wr1) ? __ldg(reinterpret_cast<const uint4*>(wbase + static_cast<int64_t>(rb + i) * N + n))
+                             : make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_n[c]), __low2half(z_n[c]), b,
-                          xr, acc[c][0], acc[c][1]);
-        cur_g = gb;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          s_c[c] = s_n[c];
-          z_c[c] = z_n[c];
-        }
+    for (int i = 0; i < kBatch; ++i) {
+      const int r = rb + i;
+      if (r >= wr1) break;
+      const uint32_t words[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+      const int kr = r * eps;
+      const int ga = kr / g;
+      if (ga != cur_g) {
+        cur_g = ga;
+        load_group(ga, s_c, z_c);
       }
-      // codes past K in a ragged last word are zero-padded and their x staged as 0
-    } else if (nb == 2) {
+      const void* xr = xbase + static_cast<size_t>(kr - k0) * kXBytes;
+      if (nb == 3) {
+        const int gb = min(kr + 9, K - 1) / g;
+        if (gb == ga) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) word_pow2<2, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
-    } else if (nb == 4) {
+          for (int c = 0; c < 4; ++c)
+            word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_c[c]), __low2half(z_c[c]),
+                            10, xr, acc[c][0], acc[c][1]);
+        } else {
+          // codes at k >= gb * g use the next group's scale and zero
+          __half2 s_n[4], z_n[4];
+          load_group(gb, s_n, z_n);
+          const int b = gb * g - kr;  // first code index in the next group (1..9)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) word_pow2<4, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
-    } else {
+          for (int c = 0; c < 4; ++c)
+            word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_n[c]), __low2half(z_n[c]),
+                            b, xr, acc[c][0], acc[c][1]);
+          cur_g = gb;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) word_pow2<1, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
+          for (int c = 0; c < 4; ++c) {
+            s_c[c] = s_n[c];
+            z_c[c] = z_n[c];
+          }
+        }
+        // codes past K in a ragged last word are zero-padded and their x staged as 0
+      } else if (nb == 2) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) word_pow2<2, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
+      } else if (nb == 4) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) word_pow2<4, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) word_pow2<1, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
+      }
     }
   }
 }
 
+// Shared memory of one block: x of its K range (padded to whole words), then the
+// staged scale and zero rows.
+__host__ __device__ inline int gemv_x_elems(int k, int splits) { return (k + splits - 1) / splits + 128; }
+__host__ __device__ inline int gemv_groups(int k, int splits, int g) { return gemv_x_elems(k, splits) / g + 2; }
+
 template <bool XF16>
 __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1, const int32_t* __restrict__ idx,
-                                                       int rows_a, GemvSrc src, float* __restrict__ part, int splits) {
-  extern __shared__ __align__(16) unsigned char s_raw[];  // inputs of this split's k range
+                                                          int rows_a, GemvSrc src, float* __restrict__ part,
+                                                          int splits) {
+  extern __shared__ __align__(16) unsigned char s_raw[];
   __shared__ float s_red[8][kGemvCols];
   const int slab = blockIdx.x, s = blockIdx.y;
   const int mat = blockIdx.z / rows_a, a = blockIdx.z - mat * rows_a;
@@ -192,12 +215,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
     return;
   }
   const int eps = 32 / nb;
-  const int K = w.k, N = w.n;
+  const int K = w.k, N = w.n, g = w.group_size;
   const int rows = (K + eps - 1) / eps;
   const int r0 = static_cast<int>((static_cast<int64_t>(rows) * s) / splits);
   const int r1 = static_cast<int>((static_cast<int64_t>(rows) * (s + 1)) / splits);
   const int k0 = r0 * eps;
   const int kspan = (r1 - r0) * eps;  // padded to whole words; entries past K are 0
+  // stage x
   for (int i = threadIdx.x; i < kspan; i += blockDim.x) {
     const int kk = k0 + i;
     float v = 0.f;
@@ -225,12 +249,30 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
     else
       reinterpret_cast<float*>(s_raw)[i] = v;
   }
+  // stage the scale / zero rows of the groups [g0, g1] this block's K range touches
+  const int xbytes = (XF16 ? 2 : 4) * gemv_x_elems(K, splits);
+  __half* s_s = reinterpret_cast<__half*>(s_raw + ((xbytes + 15) & ~15));
+  const int ng_max = gemv_groups(K, splits, g);
+  __half* s_z = s_s + ng_max * 128;
+  const int g0 = k0 / g;
+  const int g1 = (min(k0 + max(kspan, 1), K) - 1) / g;
+  const int64_t zbase = static_cast<int64_t>(w.zs_strides[e]);
+  for (int i = threadIdx.x; i < (g1 - g0 + 1) * 128; i += blockDim.x) {
+    const int gl = i >> 7, c = i & 127;
+    const int nn = slab * kGemvCols + c;
+    if (nn < N) {
+      const int64_t off = zbase + static_cast<int64_t>(g0 + gl) * N + nn;
+      s_s[i] = __ushort_as_half(__ldg(w.scales + off));
+      s_z[i] = __ushort_as_half(__ldg(w.zeros + off));
+    }
+  }
   __syncthreads();
   const int n = slab * kGemvCols + lane * 4;
   float acc[4][2] = {};
   const int per = (r1 - r0 + 7) / 8;
   const int wr0 = r0 + warp * per, wr1 = min(r1, wr0 + per);
-  if (n < N) gemv_rows<XF16>(w, e, nb, n, wr0, wr1, k0, s_raw, acc);
+  const GroupStage gs{s_s, s_z, g0};
+  if (n < N) gemv_rows<XF16>(w, e, nb, lane, n, wr0, wr1, k0, s_raw, gs, acc);
 #pragma unroll
   for (int c = 0; c < 4; ++c) s_red[warp][lane * 4 + c] = acc[c][0] + acc[c][1];
   __syncthreads();
@@ -281,8 +323,10 @@ template <bool XF16>
 cudaError_t launch_gemv_t(const ProjDev& w0, const ProjDev* w1, const int32_t* idx, int rows_a, const GemvSrc& src,
                           float* part, int splits, cudaStream_t s) {
   const int nmat = (w1 != nullptr) ? 2 : 1;
-  // a split covers at most cdiv(rows, splits) word rows of <= 32 codes: < k/splits + 64
-  const size_t smem = (XF16 ? 2 : 4) * static_cast<size_t>((w0.k + splits - 1) / splits + 128);
+  // x of a split (at most cdiv(rows, splits) word rows of <= 32 codes: < k/splits + 64)
+  // plus the scale and zero rows of the groups it touches
+  const int xbytes = (XF16 ? 2 : 4) * gemv_x_elems(w0.k, splits);
+  const size_t smem = ((xbytes + 15) & ~15) + 2 * 2 * 128 * static_cast<size_t>(gemv_groups(w0.k, splits, w0.group_size));
   static int smem_set = 48 * 1024;
   if (static_cast<int>(smem) > smem_set) {
     cudaError_t e =
