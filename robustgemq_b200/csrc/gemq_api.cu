@@ -196,6 +196,7 @@ int gemq_get_device_error(uint32_t* code_out) {
   GEMQ_CUDA(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)), "read device error");
   const uint32_t zero = 0;
   GEMQ_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)), "clear device error");
+  GEMQ_CUDA(cudaMemcpyToSymbol(g_device_abort, &zero, sizeof(zero)), "clear device abort");
   *code_out = v;
   return GEMQ_OK;
 }

@@ -35,11 +35,20 @@ enum DeviceError : uint32_t {
   kDevBadBits = 9,
 };
 
+// g_device_error: first error recorded (any kind), reported by gemq_get_device_error.
+// g_device_abort: set only when a wait expired; every other pending wait then gives
+// up at once so a broken pipeline drains quickly. Input errors (an out-of-range
+// expert id, a bad bit-width) are recorded without aborting other kernels.
 extern __device__ uint32_t g_device_error;
+extern __device__ uint32_t g_device_abort;
 
 __device__ __forceinline__ void set_device_error(uint32_t code) { atomicCAS(&g_device_error, 0u, code); }
+__device__ __forceinline__ void set_device_abort(uint32_t code) {
+  set_device_error(code);
+  atomicExch(&g_device_abort, 1u);
+}
 __device__ __forceinline__ bool device_error_set() {
-  return *((volatile uint32_t*)&g_device_error) != 0u;
+  return *((volatile uint32_t*)&g_device_abort) != 0u;
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -112,7 +121,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     if (mbar_try_wait_sleep(a, parity, kPollSleepNs)) return true;
     if (device_error_set()) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      set_device_error(code);
+      set_device_abort(code);
       return false;
     }
   }

@@ -11,6 +11,7 @@
 namespace gemq {
 
 __device__ uint32_t g_device_error = 0;
+__device__ uint32_t g_device_abort = 0;
 
 // ------------------------------------------------------------------ pack / unpack
 // One thread per output word. Codes are OR-ed in without masking, as the reference

@@ -34,7 +34,6 @@ constexpr int kWordRows = 8;   // word-row slots per stage (covers 64 k for b in
 constexpr int kThreads = 448;  // 14 warps
 constexpr int kDqWarp0 = 6;
 constexpr int kNumDqThreads = 256;
-constexpr int kAStages = 2;
 constexpr int kMaxSegs = 256;  // segments whose metadata every CTA stages in shared memory
 constexpr int kMetaBytes = kMaxSegs * 16 + (kMaxSegs + 1) * 4 + kMaxSegs * 4 * 5 + 16;
 constexpr int kSmemBudget = 225 * 1024 - kMetaBytes;
@@ -59,6 +58,10 @@ struct Cfg {
   static constexpr int kSzOff = kActBytes + kMats * kWqBytes;           // dequant: scales, zeros
   static constexpr int kStageRaw = kDense ? kActBytes + kATile : kActBytes + kMats * (kWqBytes + 2 * kSzBytes);
   static constexpr int kStageBytes = round_up(kStageRaw, 1024);
+  // dequantised-A ring depth: a buffer returns only when the MMAs that read it
+  // commit, so the ring must cover that round trip (deeper for short K tiles of
+  // few tokens, where the round trip dominates)
+  static constexpr int kAStages = kDense ? 1 : (NT <= 32 ? (kMats == 2 ? 4 : 6) : (kMats == 2 ? 3 : 4));
   static constexpr int kARingBytes = kDense ? 0 : kAStages * kMats * kATile;
   static constexpr int kStages = cmin(8, (kSmemBudget - kARingBytes - 2048) / kStageBytes);
   static constexpr int kARingOff = kStages * kStageBytes;
@@ -252,6 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + kStages;
   uint64_t* afull = bars + 2 * kStages;
+  constexpr int kAStages = C::kAStages;
   uint64_t* aempty = afull + kAStages;
   uint64_t* acc_full = aempty + kAStages;   // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
@@ -267,12 +271,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], kDense ? 1 : (kNumDqThreads / 32) + 1);
     }
     for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&afull[s], kNumDqThreads);
+      mbar_init(&afull[s], kNumDqThreads / 32);  // one arrival per dequant warp
       mbar_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -411,7 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   } else if constexpr (!kDense) {
     // ------------------------------------------------------------ dequant
@@ -446,8 +451,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int phase = (nb == 3) ? (kt * kBK) % 10 : 0;
         uint8_t* a_tile = smem + C::kARingOff + (as * kMats + mat) * C::kATile;
         dq_row(nb, phase, wv, __halves2half2(sh, sh), __halves2half2(zh, zh), a_tile, n, c0, c1);
+        // every writer makes its A-tile stores visible to the tensor core's async
+        // proxy, the warp converges, and one lane releases the warp's part
         fence_proxy_async_smem();
-        mbar_arrive(&afull[as]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[as]);
         if (++s == kStages) { s = 0; ph ^= 1u; }
         if (++as == kAStages) { as = 0; aph ^= 1u; }
       }
