@@ -128,6 +128,23 @@ int gemq_dequant_group_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t 
                             int32_t num_indices, uint16_t* out, void* workspace, size_t workspace_bytes,
                             void* stream);
 
+/* gemq_dequant_group_gemm for callers that cannot allocate device memory: no
+ * counterpart in the reference (its Triton launchers allocate through torch).
+ * Meant for hosts whose device memory is fixed or owned by someone else, e.g. a
+ * serving process that reserves its memory pool at start-up, or a plugin that must
+ * not call its host's allocator: it takes no workspace and calls no cudaMalloc,
+ * cudaFree or other allocating routine. The segment table lives in a 20 KiB array
+ * in the library's device image, which every GPU that loads the library holds
+ * until the process exits; num_indices above GEMQ_NOALLOC_MAX_INDICES is rejected
+ * with GEMQ_ERR_INVALID_ARGUMENT. The first call on each device looks up that
+ * array's address (cudaGetSymbolAddress), so make it before any stream capture.
+ * Every call shares the one array: calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller. Each call
+ * rewrites the entries it reads, so no clearing is needed between calls. */
+#define GEMQ_NOALLOC_MAX_INDICES 1023
+int gemq_dequant_group_gemm_noalloc(const gemq_proj_t* proj, const uint16_t* x, int64_t m, const int32_t* indices,
+                                    int32_t num_indices, uint16_t* out, void* stream);
+
 /* Replaces dequant_gemm_triton (dequant_gemm.py:150-193); proj->num_experts == 1. */
 int gemq_dequant_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t m, uint16_t* out, void* workspace,
                       size_t workspace_bytes, void* stream);

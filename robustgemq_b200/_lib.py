@@ -38,7 +38,8 @@ STAGES = ("route", "dispatch", "up", "down", "shared", "combine")
 EXPORTED = [
     "gemq_last_error_string", "gemq_version", "gemq_get_device_error",
     "gemq_pack_weights_over_cols", "gemq_unpack_over_cols", "gemq_dequant_expert",
-    "gemq_group_gemm_workspace_size", "gemq_dequant_group_gemm", "gemq_dequant_gemm",
+    "gemq_group_gemm_workspace_size", "gemq_dequant_group_gemm", "gemq_dequant_group_gemm_noalloc",
+    "gemq_dequant_gemm",
     "gemq_gemv_workspace_size", "gemq_dequant_gemv", "gemq_fused_up_proj", "gemq_fused_down_proj",
     "gemq_layer_create", "gemq_layer_destroy", "gemq_moe_workspace_size", "gemq_moe_route",
     "gemq_moe_forward", "gemq_layer_stage_times",
@@ -94,6 +95,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "gemq_dequant_expert": (ctypes.c_int, [P(ProjT), i32, vp, vp]),
         "gemq_group_gemm_workspace_size": (sz, [i32]),
         "gemq_dequant_group_gemm": (ctypes.c_int, [P(ProjT), vp, i64, vp, i32, vp, vp, sz, vp]),
+        "gemq_dequant_group_gemm_noalloc": (ctypes.c_int, [P(ProjT), vp, i64, vp, i32, vp, vp]),
         "gemq_dequant_gemm": (ctypes.c_int, [P(ProjT), vp, i64, vp, vp, sz, vp]),
         "gemq_gemv_workspace_size": (sz, [P(ProjT), i32]),
         "gemq_dequant_gemv": (ctypes.c_int, [P(ProjT), vp, vp, vp, sz, vp]),

@@ -4,6 +4,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -750,3 +751,82 @@ int gemq_layer_stage_times(gemq_layer_t* layer, float* ms_out) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ allocation-free group GEMM
+// gemq_dequant_group_gemm keeps its segment table and tile prefix in caller
+// workspace. Hosts that cannot allocate device memory of their own (an
+// inference server whose memory pool is fixed when it starts, a plugin running
+// inside a host whose allocator it must not call, a caller with no cudaMalloc
+// binding) use gemq_dequant_group_gemm_noalloc instead: the same table lives in
+// the file-scope array below, part of the library's device image.
+namespace gemq {
+namespace {
+
+constexpr int kNoallocMaxDevices = 64;
+constexpr size_t kNoallocSegBytes = sizeof(Seg) * 1024;                    // segments [0, 1023)
+constexpr size_t kNoallocScratchBytes = kNoallocSegBytes + sizeof(int32_t) * 1024;  // + tile prefix [0, 1023]
+static_assert(GEMQ_NOALLOC_MAX_INDICES < 1024, "static scratch sized for 1023 indices");
+
+// Every GPU that loads the library holds these 20 KiB until the process exits.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoallocMaxDevices] = {};
+
+// The device address of g_noalloc_scratch on the current device, looked up once
+// per device (host code cannot use the symbol itself as a pointer).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  GEMQ_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= kNoallocMaxDevices) return fail(GEMQ_ERR_UNSUPPORTED, "device ordinal above 63");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    GEMQ_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(static scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return GEMQ_OK;
+}
+
+}  // namespace
+}  // namespace gemq
+
+extern "C" int gemq_dequant_group_gemm_noalloc(const gemq_proj_t* proj, const uint16_t* x, int64_t m,
+                                               const int32_t* indices, int32_t num_indices, uint16_t* out,
+                                               void* stream) {
+  if (int rc = check_proj(proj, "proj")) return rc;
+  if (num_indices > GEMQ_NOALLOC_MAX_INDICES)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "num_indices " + std::to_string(num_indices) +
+                                               " exceeds GEMQ_NOALLOC_MAX_INDICES (" +
+                                               std::to_string(GEMQ_NOALLOC_MAX_INDICES) +
+                                               "), the capacity of the library's static segment table");
+  if (num_indices <= 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "num_indices must be positive");
+  if (m < 0 || m > INT32_MAX / 2) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad m");
+  if (m == 0) return GEMQ_OK;
+  if (x == nullptr || out == nullptr || indices == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The segment kernel rewrites every entry the GEMM reads (segments [0, A) and
+  // tile prefix [0, A]), so the previous call's contents need no clearing.
+  Seg* segs = static_cast<Seg*>(scratch);
+  int32_t* tp = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(scratch) + kNoallocSegBytes);
+  GemmArgs a{};
+  a.mode = GemmMode::kStoreF16;
+  a.w0 = to_dev(*proj);
+  a.w1 = a.w0;
+  a.act = x;
+  a.act_rows = m;
+  a.segs = segs;
+  a.tile_prefix = tp;
+  a.num_segs = num_indices;
+  a.out = out;
+  a.out_ld = proj->n;
+  a.out_cols = proj->n;
+  a.num_sms = device_sm_count();
+  a.nt = choose_nt(m);
+  if (!tc_gemm_supported(a)) a.nt = 32;
+  GEMQ_CUDA(launch_build_index_segs(indices, num_indices, proj->num_experts, m, a.nt, segs, tp, s), "segments");
+  return run_gemm(a, false, s, "dequant_group_gemm_noalloc");
+}
