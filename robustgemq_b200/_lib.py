@@ -32,6 +32,7 @@ FWD_FP32_COMBINE = 16
 FWD_FORCE_SIMT = 32
 FWD_RESIDUAL = 64
 FWD_TIME_STAGES = 128
+FWD_SMEM_DEQUANT = 256
 STAGES = ("route", "dispatch", "up", "down", "shared", "combine")
 
 # every symbol include/gemq_b200.h declares

@@ -625,16 +625,27 @@ int forward_n_tokens(gemq_layer_t* L, const uint16_t* x, int64_t T, uint16_t* ou
   dn.row_weight = b.w_perm;
   const bool tc = !force_simt && tc_gemm_supported(up) && tc_gemm_supported(dn);
   if (!tc) up.nt = dn.nt = 32;
+  // decode batches: the tensor-memory dequant GEMM, with activations in its K order
+  const bool dec = tc && (flags & GEMQ_FWD_SMEM_DEQUANT) == 0 && tcd_gemm_supported(up) && tcd_gemm_supported(dn);
+  if (dec) up.perm_out_nbits = L->w2.nbits;
   tm.begin(GEMQ_STAGE_DISPATCH);
   GEMQ_CUDA(launch_dispatch(idx, w, x, T, k, E, D, up.nt, b.counts, b.cursor, b.segs, b.tile_prefix, b.slot_pos,
-                            b.w_perm, b.x_perm, s),
+                            b.w_perm, b.x_perm, dec ? L->w1.nbits : nullptr, s),
             "dispatch");
   tm.end(GEMQ_STAGE_DISPATCH);
   tm.begin(GEMQ_STAGE_UP);
-  if (int rc = run_gemm(up, !tc, s, "up projection")) return rc;
+  if (dec) {
+    GEMQ_CUDA(launch_tcd_gemm(up, s), "up projection");
+  } else if (int rc = run_gemm(up, !tc, s, "up projection")) {
+    return rc;
+  }
   tm.end(GEMQ_STAGE_UP);
   tm.begin(GEMQ_STAGE_DOWN);
-  if (int rc = run_gemm(dn, !tc, s, "down projection")) return rc;
+  if (dec) {
+    GEMQ_CUDA(launch_tcd_gemm(dn, s), "down projection");
+  } else if (int rc = run_gemm(dn, !tc, s, "down projection")) {
+    return rc;
+  }
   tm.end(GEMQ_STAGE_DOWN);
   const uint16_t* add = nullptr;
   if (d.has_shared) {

@@ -57,6 +57,7 @@ struct GemmArgs {
   int out_cols;                // valid output columns (n)
   const uint16_t* row_weight;  // kRouteWeight: fp16 per output row
   int num_sms;
+  const int32_t* perm_out_nbits;  // decode GEMM, kSwiGLU: store h in the slot order of these bit-widths
 };
 
 // Tensor-core (tcgen05) grouped GEMM; cudaErrorNotSupported for shapes it does not
@@ -64,6 +65,14 @@ struct GemmArgs {
 bool tc_gemm_supported(const GemmArgs& a);
 cudaError_t launch_tc_gemm(const GemmArgs& a, cudaStream_t stream);
 cudaError_t launch_simt_gemm(const GemmArgs& a, cudaStream_t stream);
+
+// Decode-batch tensor-core GEMM (token tiles of 32, dequantised weights in tensor
+// memory; kernels_tcd.cu). Its activations are stored in the slot order of
+// kperm.cuh for the expert's bit-width: dispatch with perm_nbits, and the gate/up
+// launch's perm_out_nbits for the down projection.
+bool tcd_gemm_supported(const GemmArgs& a);
+cudaError_t launch_tcd_gemm(const GemmArgs& a, cudaStream_t stream);
+int kperm_source_column(int nb, int k);
 
 // One segment per index of dequant_group_gemm (invalid indices -> empty segments).
 cudaError_t launch_build_index_segs(const int32_t* indices, int num_indices, int num_experts, int64_t m, int nt,
@@ -79,7 +88,8 @@ cudaError_t launch_route_small(const uint16_t* x, int64_t T, int D, const uint16
 bool small_dispatch_ok(int64_t P, int E);
 cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t T, int k,
                             int E, int D, int nt, int32_t* counts, int32_t* cursor, Seg* segs, int32_t* tile_prefix,
-                            int32_t* slot_pos, uint16_t* w_perm, uint16_t* x_perm, cudaStream_t stream);
+                            int32_t* slot_pos, uint16_t* w_perm, uint16_t* x_perm, const int32_t* perm_nbits,
+                            cudaStream_t stream);
 cudaError_t launch_combine(const uint16_t* y_perm, const int32_t* slot_pos, const int32_t* topk_idx, int64_t T, int k,
                            int D, bool fp32_sum, const uint16_t* add, const uint16_t* residual, uint16_t* out,
                            cudaStream_t stream);

@@ -11,8 +11,13 @@
 
 #include "gemq_common.cuh"
 #include "gemq_internal.h"
+#include "kperm.cuh"
 
 namespace gemq {
+
+namespace {
+__constant__ kperm::Perm3 c_perm3_route = kperm::make_perm3();
+}  // namespace
 
 namespace {
 
@@ -164,6 +169,37 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_small(const __half* __r
   if (warp == 0) topk_warp([&](int e) { return s_logit[e]; }, E, k, norm, fp16_softmax, topk_idx + t * k, topk_w + t * k);
 }
 
+// Copies token row `src` to `dst` (D fp16, D % 8 == 0) by one warp: as is, or in
+// the decode GEMM's K slot order for bit-width nb (kperm.cuh; D % 128 == 0 then),
+// gathering through the warp's staging buffer `sbuf` (D halves of shared memory).
+__device__ __forceinline__ void copy_row(const __half* __restrict__ src, __half* __restrict__ dst, int D, int nb,
+                                         int lane, __half* sbuf) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+  if (nb == 0) {
+    for (int i = lane; i < D / 8; i += 32) d4[i] = s4[i];
+    return;
+  }
+  uint4* b4 = reinterpret_cast<uint4*>(sbuf);
+  for (int i = lane; i < D / 8; i += 32) b4[i] = s4[i];
+  __syncwarp();
+  const unsigned short* b16 = reinterpret_cast<const unsigned short*>(sbuf);
+  for (int i = lane; i < D / 8; i += 32) {
+    const int k0 = 8 * i, st = k0 >> 7;
+    const int ph = kperm::phase3(st);
+    uint32_t v[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int sa = (k0 + 2 * m) & 127, sb = sa + 1;
+      const int a = (nb == 3) ? c_perm3_route.fwd[ph][sa] : kperm::perm_pow2(nb, sa);
+      const int b = (nb == 3) ? c_perm3_route.fwd[ph][sb] : kperm::perm_pow2(nb, sb);
+      v[m] = static_cast<uint32_t>(b16[(st << 7) + a]) | (static_cast<uint32_t>(b16[(st << 7) + b]) << 16);
+    }
+    d4[i] = make_uint4(v[0], v[1], v[2], v[3]);
+  }
+  __syncwarp();
+}
+
 // ------------------------------------------------------------------ dispatch (large batches)
 __global__ void k_count(const int32_t* __restrict__ topk_idx, int64_t P, int E, int32_t* __restrict__ counts) {
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -210,7 +246,8 @@ __global__ void k_scan_segs(const int32_t* __restrict__ counts, int E, int nt, S
 // slot_pos -1, which the combine skips.
 __global__ void k_scatter(const int32_t* __restrict__ topk_idx, const __half* __restrict__ topk_w,
                           const __half* __restrict__ x, int64_t P, int k, int E, int D, int32_t* __restrict__ cursor,
-                          int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm, __half* __restrict__ x_perm) {
+                          int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm, __half* __restrict__ x_perm,
+                          const int32_t* __restrict__ perm_nbits) {
   const int64_t slot = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (slot >= P) return;
@@ -227,9 +264,10 @@ __global__ void k_scatter(const int32_t* __restrict__ topk_idx, const __half* __
   }
   pos = __shfl_sync(0xffffffffu, pos, 0);
   const int64_t t = slot / k;
-  const uint4* src = reinterpret_cast<const uint4*>(x + t * D);
-  uint4* dst = reinterpret_cast<uint4*>(x_perm + static_cast<int64_t>(pos) * D);
-  for (int i = lane; i < D / 8; i += 32) dst[i] = src[i];
+  const int nb = perm_nbits != nullptr ? min(max(__ldg(perm_nbits + e), 1), 4) : 0;
+  extern __shared__ __align__(16) __half s_stage_rows[];
+  copy_row(x + t * D, x_perm + static_cast<int64_t>(pos) * D, D, nb, lane,
+           s_stage_rows + static_cast<size_t>(threadIdx.x >> 5) * D);
 }
 
 // ------------------------------------------------------------------ dispatch (small batches)
@@ -269,7 +307,8 @@ __global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restric
                                                         int P, int k, int E, int D, int nt, int32_t* __restrict__ counts,
                                                         Seg* __restrict__ segs, int32_t* __restrict__ tile_prefix,
                                                         int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm,
-                                                        __half* __restrict__ x_perm) {
+                                                        __half* __restrict__ x_perm,
+                                                        const int32_t* __restrict__ perm_nbits) {
   __shared__ int s_idx[kSmallDispatchMaxSlots];
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_tiles[kMaxExperts];
@@ -314,9 +353,10 @@ __global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restric
     slot_pos[slot] = pos;
     w_perm[pos] = topk_w[slot];
   }
-  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(slot / k) * D);
-  uint4* dst = reinterpret_cast<uint4*>(x_perm + static_cast<int64_t>(pos) * D);
-  for (int i = lane; i < D / 8; i += 32) dst[i] = src[i];
+  const int nb = perm_nbits != nullptr ? min(max(__ldg(perm_nbits + e), 1), 4) : 0;
+  extern __shared__ __align__(16) __half s_stage_rows[];
+  copy_row(x + static_cast<int64_t>(slot / k) * D, x_perm + static_cast<int64_t>(pos) * D, D, nb, lane,
+           s_stage_rows + static_cast<size_t>(warp) * D);
 }
 
 // ------------------------------------------------------------------ combine
@@ -406,15 +446,30 @@ bool small_dispatch_ok(int64_t P, int E) { return P <= kSmallDispatchMaxSlots &&
 
 cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t T, int k,
                             int E, int D, int nt, int32_t* counts, int32_t* cursor, Seg* segs, int32_t* tile_prefix,
-                            int32_t* slot_pos, uint16_t* w_perm, uint16_t* x_perm, cudaStream_t stream) {
+                            int32_t* slot_pos, uint16_t* w_perm, uint16_t* x_perm, const int32_t* perm_nbits,
+                            cudaStream_t stream) {
   const int64_t P = T * k;
+  if (perm_nbits != nullptr && D % kperm::kStageK != 0) return cudaErrorInvalidValue;
+  // permuted copies stage each warp's row in shared memory (8 warps per block)
+  const size_t row_smem = perm_nbits != nullptr ? static_cast<size_t>(8) * D * sizeof(__half) : 0;
+  if (row_smem > 0) {
+    static size_t attr_set = 0;  // raised once per larger row size (outside graph capture)
+    if (row_smem > attr_set) {
+      cudaError_t e = cudaFuncSetAttribute(k_dispatch_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(row_smem));
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(row_smem));
+      if (e != cudaSuccess) return e;
+      attr_set = row_smem;
+    }
+  }
   cudaError_t err;
   if (small_dispatch_ok(P, E)) {
     const unsigned grid = static_cast<unsigned>(P > 0 ? (P + 7) / 8 : 1);
-    k_dispatch_small<<<grid, 256, 0, stream>>>(topk_idx, reinterpret_cast<const __half*>(topk_w),
+    k_dispatch_small<<<grid, 256, row_smem, stream>>>(topk_idx, reinterpret_cast<const __half*>(topk_w),
                                                 reinterpret_cast<const __half*>(x), static_cast<int>(P), k, E, D, nt,
                                                 counts, segs, tile_prefix, slot_pos, reinterpret_cast<__half*>(w_perm),
-                                                reinterpret_cast<__half*>(x_perm));
+                                                reinterpret_cast<__half*>(x_perm), perm_nbits);
     return cudaGetLastError();
   }
   err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, stream);
@@ -423,9 +478,9 @@ cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, con
   if ((err = cudaGetLastError()) != cudaSuccess) return err;
   k_scan_segs<<<1, 1024, 0, stream>>>(counts, E, nt, segs, tile_prefix, cursor);
   if ((err = cudaGetLastError()) != cudaSuccess) return err;
-  k_scatter<<<static_cast<unsigned>((P * 32 + 255) / 256), 256, 0, stream>>>(
+  k_scatter<<<static_cast<unsigned>((P * 32 + 255) / 256), 256, row_smem, stream>>>(
       topk_idx, reinterpret_cast<const __half*>(topk_w), reinterpret_cast<const __half*>(x), P, k, E, D, cursor,
-      slot_pos, reinterpret_cast<__half*>(w_perm), reinterpret_cast<__half*>(x_perm));
+      slot_pos, reinterpret_cast<__half*>(w_perm), reinterpret_cast<__half*>(x_perm), perm_nbits);
   return cudaGetLastError();
 }
 

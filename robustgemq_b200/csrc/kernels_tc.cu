@@ -23,6 +23,7 @@
 
 #include "gemq_common.cuh"
 #include "gemq_internal.h"
+#include "tc_work.cuh"
 
 namespace gemq {
 
@@ -34,8 +35,10 @@ constexpr int kWordRows = 8;   // word-row slots per stage (covers 64 k for b in
 constexpr int kThreads = 448;  // 14 warps
 constexpr int kDqWarp0 = 6;
 constexpr int kNumDqThreads = 256;
-constexpr int kMaxSegs = 256;  // segments whose metadata every CTA stages in shared memory
-constexpr int kMetaBytes = kMaxSegs * 16 + (kMaxSegs + 1) * 4 + kMaxSegs * 4 * 5 + 16;
+using tcw::kMaxSegs;
+using tcw::kMetaBytes;
+using tcw::Meta;
+using tcw::Work;
 constexpr int kSmemBudget = 225 * 1024 - kMetaBytes;
 
 __host__ __device__ constexpr int round_up(int v, int m) { return (v + m - 1) / m * m; }
@@ -102,63 +105,6 @@ struct KArgs {
 struct WordMaps {
   CUtensorMap m[2][3];
 };
-
-struct Work {
-  int e, act_row, out_row, rows, n0, nb, wrow0, srow0, wrow1, srow1;
-};
-
-// Segment table and per-segment expert metadata, staged once per CTA so that work
-// decoding on the producer's critical path costs shared-memory reads only.
-struct Meta {
-  Seg seg[kMaxSegs];
-  int tp[kMaxSegs + 1];
-  int nb[kMaxSegs], wrow0[kMaxSegs], srow0[kMaxSegs], wrow1[kMaxSegs], srow1[kMaxSegs];
-};
-static_assert(sizeof(Meta) <= kMetaBytes, "metadata layout");
-
-__device__ __forceinline__ void stage_meta(Meta& m, const KArgs& p, bool dense) {
-  for (int i = threadIdx.x; i <= p.num_segs; i += blockDim.x) m.tp[i] = __ldg(p.tile_prefix + i);
-  for (int i = threadIdx.x; i < p.num_segs; i += blockDim.x) {
-    const Seg sg = __ldg(p.segs + i);
-    m.seg[i] = sg;
-    if (dense) {
-      m.nb[i] = 4;
-      m.wrow0[i] = m.srow0[i] = m.wrow1[i] = m.srow1[i] = 0;
-    } else {
-      const int e = sg.x;
-      m.nb[i] = __ldg(p.nbits + e);
-      m.wrow0[i] = __ldg(p.wq_strides0 + e) / p.N;
-      m.srow0[i] = __ldg(p.zs_strides0 + e) / p.N;
-      m.wrow1[i] = __ldg(p.wq_strides1 + e) / p.N;
-      m.srow1[i] = __ldg(p.zs_strides1 + e) / p.N;
-    }
-  }
-}
-
-template <int NT>
-__device__ __forceinline__ Work decode_work(const Meta& m, const KArgs& p, int w) {
-  Work wk;
-  const int t = w / p.n_tiles;
-  const int i = w - t * p.n_tiles;
-  int lo = 0, hi = p.num_segs;
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (m.tp[mid] <= t) lo = mid; else hi = mid;
-  }
-  const Seg sg = m.seg[lo];
-  const int j = t - m.tp[lo];
-  wk.e = sg.x;
-  wk.act_row = sg.y + j * NT;
-  wk.out_row = sg.z + j * NT;
-  wk.rows = min(NT, sg.w - j * NT);
-  wk.n0 = i * kBM;
-  wk.nb = m.nb[lo];
-  wk.wrow0 = m.wrow0[lo];
-  wk.srow0 = m.srow0[lo];
-  wk.wrow1 = m.wrow1[lo];
-  wk.srow1 = m.srow1[lo];
-  return wk;
-}
 
 // ---------------------------------------------------------------- dequant of one row
 // Thread owns feature row `n` of the 128 x 64 A tile; writes 16-byte chunks
@@ -294,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
   Meta& meta = *reinterpret_cast<Meta*>(smem + C::kMetaOff);
-  stage_meta(meta, p, kDense);
+  tcw::stage_meta(meta, p, kDense);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -309,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int armed = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
-        const Work wk = decode_work<NT>(meta, p, w);
+        const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
         const int nb = kDense ? 4 : min(max(wk.nb, 1), 4);
         const int eps = 32 / nb;
         const int box = nb == 1 ? 0 : nb == 2 ? 1 : 2;  // word-row map index
@@ -393,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++it) {
       const int buf = it & 1;
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * C::kAccCols);
-      const Work wk = decode_work<NT>(meta, p, w);
+      const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
       if (!mbar_wait(&acc_full[buf], (it >> 1) & 1, kDevTimeoutAccFull)) break;
       tc_fence_after();
       const int col = wk.n0 + 32 * q + lane;
@@ -430,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t ph = 0, aph = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
-      const Work wk = decode_work<NT>(meta, p, w);
+      const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
       const int nb = wk.nb;
       if (nb < 1 || nb > 4) {
         if (dt == 0) set_device_error(kDevBadBits);

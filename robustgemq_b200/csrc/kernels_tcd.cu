@@ -1,0 +1,712 @@
+// Decode-batch grouped dequant GEMM on tcgen05 with the dequantised weights in
+// tensor memory (sm_100a).
+//
+// Same product as k_moe_tc (D[n, t] = sum_k deq(W_e)[k, n] * act[row_t, k], fp32 in
+// TMEM; the reference's x @ deq(W), dequant_group_gemm.py:109-138) for token tiles
+// of NT <= 32 rows, where each expert sees a handful of tokens and the kernel must
+// stream packed weights at HBM speed. Differences from k_moe_tc:
+//   * the dequant warps write the A tile (128 features x 128 k per stage and
+//     matrix) straight into tensor memory with tcgen05.st, and the MMA reads A from
+//     there: the tile never round-trips through shared memory;
+//   * K advances in stages of 128 and the activations arrive in the slot order of
+//     kperm.cuh (written so by dispatch / the gate-up epilogue), so every column of
+//     the A tile is one shift + one mask of a packed word, then the exact
+//     fma.rn.f16 dequant (utils.py:206-210);
+//   * scale / zero rows are fetched 16 groups at a time into their own ring, and
+//     the per-stage copies are issued by two producer warps (a single thread issues
+//     one bulk tensor copy every ~100+ cycles).
+//
+// Warps (512 threads, one CTA per SM, grid-stride over work items):
+//   0      producer: activation sub-tile 0 (k0..k0+63) and packed words of matrix 0
+//   1      TMEM allocation, single-thread tcgen05.mma issue and commits
+//   2      producer: activation sub-tile 1 (k0+64..k0+127) and words of matrix 1
+//   3      producer: scale / zero chunks
+//   4-7    epilogue: tcgen05.ld -> rounding -> global stores (lane quarter = warp % 4)
+//   8-15   dequant: warp w owns features 32*(w%4) .. +31 (its TMEM lane quarter);
+//          two matrices: warps 8-11 matrix 0, 12-15 matrix 1, all 128 k of a stage;
+//          one matrix: warps 8-11 k 0..63, 12-15 k 64..127
+// Every wait is bounded (gemq_common.cuh); on expiry all roles drain and return.
+#include <cudaTypedefs.h>
+
+#include <utility>
+
+#include "gemq_common.cuh"
+#include "gemq_internal.h"
+#include "kperm.cuh"
+#include "tc_work.cuh"
+
+namespace gemq {
+
+namespace {
+
+using tcw::Meta;
+using tcw::Work;
+
+constexpr int kThreadsD = 768;
+constexpr int kDqWarp0 = 8;
+constexpr int kNumDqWarps = 16;
+constexpr int kSK = kperm::kStageK;  // 128
+constexpr int kScRows = 16;          // scale rows (groups) per chunk
+constexpr int kMaxWordRows = 16;
+constexpr uint32_t kIdleSleepNs = 256;  // pause between polls of waiters off the critical path
+// Pause between polls of the dequant warps and the MMA issuer: a spinning warp takes
+// issue slots and integer-pipe cycles from the dequant warps of its sub-partition.
+constexpr uint32_t kBusySleepNs = 64;
+
+__constant__ kperm::Perm3 c_perm3 = kperm::make_perm3();
+
+__host__ __device__ constexpr int cmin_d(int a, int b) { return a < b ? a : b; }
+__host__ __device__ constexpr int round_up_d(int v, int m) { return (v + m - 1) / m * m; }
+
+template <int NT, GemmMode MODE>
+struct CfgD {
+  // Two matrices per work item: w1 and w3 for SwiGLU; for the down projection two
+  // adjacent 128-feature tiles of w2, so both modes have the same per-stage shape.
+  static constexpr int kMats = 2;
+  static constexpr bool kPairTiles = (MODE == GemmMode::kRouteWeight);
+  static constexpr int kActSub = NT * 128;  // one 64-wide SW128 sub-tile
+  static constexpr int kActBytes = 2 * kActSub;
+  static constexpr int kWordBytes = kMaxWordRows * 128 * 4;
+  static constexpr int kStageBytes = round_up_d(kActBytes + kMats * kWordBytes, 1024);
+  static constexpr int kScBytes = kScRows * 128 * 2;
+  static constexpr int kChunkBytes = kMats * 2 * kScBytes;
+  static constexpr int kBudget = 225 * 1024 - tcw::kMetaBytes - 2 * kChunkBytes - 2048;
+  static constexpr int kStages = cmin_d(8, kBudget / kStageBytes);
+  static constexpr int kChunkOff = kStages * kStageBytes;
+  static constexpr int kBarOff = kChunkOff + 2 * kChunkBytes;
+  static constexpr int kAStages = kMats == 2 ? 3 : 6;
+  static constexpr int kNumBars = 2 * kStages + 4 + 2 * kAStages + 5;
+  static constexpr int kMetaOff = round_up_d(kBarOff + kNumBars * 8 + 16, 16);
+  static constexpr int kSmemBytes = kMetaOff + tcw::kMetaBytes + 1024;
+  static constexpr int kAccCols = kMats * NT;  // one accumulator buffer
+  static constexpr int kACol0 = 2 * kAccCols;  // first A column
+  static constexpr int kACols = kMats * 64;    // one A stage: 128 fp16 k per matrix
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kIdesc = idesc_f16_f32(128, NT);
+  static_assert(kStages >= 3, "shared memory budget too small");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget exceeded");
+  static_assert(kACol0 + kAStages * kACols <= 512, "tensor memory budget exceeded");
+};
+
+struct KArgsD {
+  const int32_t* nbits;
+  const int32_t* wq_strides0;
+  const int32_t* zs_strides0;
+  const int32_t* wq_strides1;
+  const int32_t* zs_strides1;
+  const Seg* segs;
+  const int32_t* tile_prefix;
+  int num_segs;
+  int N;
+  int K;
+  int group_size;
+  int n_tiles;
+  void* out;
+  int64_t out_ld;
+  const __half* row_weight;
+  const int32_t* perm_out_nbits;  // kSwiGLU: store h in the slot order of these bit-widths
+};
+
+// Packed-word maps per matrix and box height (4, 8, 14, 16 rows for b = 1, 2, 3, 4).
+struct WordMapsD {
+  CUtensorMap m[2][4];
+};
+__host__ __device__ constexpr int box_index(int nb) { return nb - 1; }
+
+// ---------------------------------------------------------------- dequant
+struct ScaleSet {
+  __half2 s0, s1, s01, z0, z1, z01;
+};
+
+// Column C (codes of slots 2C, 2C+1) of a stage as the fma.rn.f16 dequant pair.
+// Pairs are (j, j + eps/2) of one word for b in {1, 2, 4} (both codes at offset b*j
+// of their 16-bit halves; offsets past the fp16 mantissa read the word shifted right
+// by 8) and (j, j + 5) for 3-bit (codes j at bit 3j, j + 5 at bit 15 + 3j; the word
+// shifted left by 1 or right by 8 brings each pair inside the mantissas).
+template <int NB, int PH, bool G2, int C>
+__device__ __forceinline__ uint32_t dq_col(const uint32_t (&w)[kMaxWordRows], const ScaleSet& sc) {
+  if constexpr (NB == 3) {
+    constexpr kperm::Pair3 pr = kperm::pair3(PH, C);
+    constexpr bool ga = G2 && pr.qa >= 64, gb = G2 && pr.qb >= 64;
+    const __half2 s2 = ga ? sc.s1 : (gb ? sc.s01 : sc.s0);
+    const __half2 z2 = ga ? sc.z1 : (gb ? sc.z01 : sc.z0);
+    if constexpr (pr.kind == 0) {
+      const uint32_t x = w[pr.wa];
+      if constexpr (pr.sa == 0) return dq_pair_at<3, 1, 0>(x << 1, s2, z2);
+      if constexpr (pr.sa == 1) return dq_pair_at<3, 3, 2>(x, s2, z2);
+      if constexpr (pr.sa == 2) return dq_pair_at<3, 6, 5>(x, s2, z2);
+      if constexpr (pr.sa == 3) return dq_pair_at<3, 1, 0>(x >> 8, s2, z2);
+      return dq_pair_at<3, 4, 3>(x >> 8, s2, z2);
+    } else {
+      const uint32_t x = ((w[pr.wa] >> (3 * pr.sa)) & 7u) | (((w[pr.wb] >> (3 * pr.sb)) & 7u) << 16);
+      return dq_pair_at<3, 0, 0>(x, s2, z2);
+    }
+  } else {
+    constexpr int eps = 32 / NB;
+    constexpr int qa = kperm::perm_pow2(NB, 2 * C);
+    constexpr int wi = qa / eps, j = qa % eps;
+    constexpr int o = NB * j;
+    constexpr int sh = (o + NB <= 10) ? 0 : 8;
+    const uint32_t x = sh ? (w[wi] >> 8) : w[wi];
+    constexpr bool g1 = G2 && qa >= 64;
+    return dq_pair_at<NB, o - sh, o - sh>(x, g1 ? sc.s1 : sc.s0, g1 ? sc.z1 : sc.z0);
+  }
+}
+
+template <int NB, int PH, bool G2, int C0, int NC, int... Cs>
+__device__ __forceinline__ void dq_cols(const uint32_t (&w)[kMaxWordRows], const ScaleSet& sc, uint32_t (&o)[NC],
+                                        std::integer_sequence<int, Cs...>) {
+  ((o[Cs] = dq_col<NB, PH, G2, C0 + Cs>(w, sc)), ...);
+}
+
+// Dequantises columns [C0, C0 + NC) of a stage and stores them to TMEM at `taddr`.
+template <int NB, int PH, bool G2, int C0, int NC>
+__device__ __forceinline__ void dq_store(const uint32_t (&w)[kMaxWordRows], const ScaleSet& sc, uint32_t taddr) {
+  uint32_t o[NC];
+  dq_cols<NB, PH, G2, C0, NC>(w, sc, o, std::make_integer_sequence<int, NC>{});
+  if constexpr (NC == 32) tmem_st32(taddr, o);
+  else tmem_st16(taddr, o);
+}
+
+// Ring positions and barriers a dequant warp walks through; advanced in place.
+struct DqRings {
+  int s, as, c;
+  uint32_t ph, aph, cph;
+};
+
+// Everything a dequant warp needs for one work item besides its rings.
+struct DqEnv {
+  uint8_t* stages;         // stage ring base (shared memory)
+  const uint8_t* chunks;   // scale / zero chunk ring base
+  uint64_t *full, *empty, *sfull, *sempty, *afull, *aempty;
+  uint32_t a_col0;         // TMEM address of this warp's lane quarter, A ring column 0
+  uint32_t n;              // feature row inside the tile (= TMEM lane)
+  int lane, mat, KT, log2g;
+};
+
+// One work item of one dequant warp, specialised by bit-width, group layout and the
+// warp's columns [C0, C0 + NC) of its matrix: per stage, read the packed words and
+// scale / zero of its feature row, release the stage, dequantise into TMEM, and
+// release the A stage to the MMA. Scale group, chunk and 3-bit phase advance
+// incrementally. Returns false if a wait expired.
+template <class C, int NB, bool G2, int C0, int NC>
+__device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
+  constexpr int kRows = kperm::stage_word_rows(NB);
+  int ch = -1;
+  int ph3 = 0;  // 3-bit phase index: P = (128 kt) % 10 = 0, 8, 6, 4, 2 -> index 0, 4, 3, 2, 1
+  for (int kt = 0; kt < e.KT; ++kt) {
+    const int gl = (kt * kSK) >> e.log2g;  // first scale group of the stage
+    const int chn = gl / kScRows;
+    if (chn != ch) {
+      if (ch >= 0) {
+        __syncwarp();
+        if (e.lane == 0) mbar_arrive(&e.sempty[r.c]);
+        if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
+      }
+      if (!warp_wait(&e.sfull[r.c], r.cph, kDevTimeoutTmaFull, kBusySleepNs)) return false;
+      ch = chn;
+    }
+    if (!warp_wait(&e.full[r.s], r.ph, kDevTimeoutTmaFull, kBusySleepNs)) return false;
+    const uint32_t* wcol = reinterpret_cast<const uint32_t*>(e.stages + r.s * C::kStageBytes + C::kActBytes +
+                                                             e.mat * C::kWordBytes) +
+                           e.n;
+    uint32_t wv[kMaxWordRows];
+#pragma unroll
+    for (int i = 0; i < kMaxWordRows; ++i) wv[i] = (i < kRows) ? wcol[i * 128] : 0u;
+    const __half* sp =
+        reinterpret_cast<const __half*>(e.chunks + r.c * C::kChunkBytes + (2 * e.mat) * C::kScBytes) + e.n;
+    const __half* zp = sp + C::kScBytes / 2;
+    const int r0 = (gl - ch * kScRows) * 128;
+    const __half sa = sp[r0], za = zp[r0];
+    __half sb = sa, zb = za;
+    if constexpr (G2) {
+      sb = sp[r0 + 128];
+      zb = zp[r0 + 128];
+    }
+    __syncwarp();
+    if (e.lane == 0) mbar_arrive(&e.empty[r.s]);
+    if (!warp_wait(&e.aempty[r.as], r.aph ^ 1u, kDevTimeoutAEmpty, kBusySleepNs)) return false;
+    tc_fence_after();
+    ScaleSet sc;
+    sc.s0 = __halves2half2(sa, sa);
+    sc.z0 = __halves2half2(za, za);
+    sc.s1 = __halves2half2(sb, sb);
+    sc.z1 = __halves2half2(zb, zb);
+    sc.s01 = __halves2half2(sa, sb);
+    sc.z01 = __halves2half2(za, zb);
+    const uint32_t taddr = e.a_col0 + static_cast<uint32_t>(r.as * C::kACols + e.mat * 64 + C0);
+    if constexpr (NB == 3) {
+      switch (ph3) {
+        case 0: dq_store<3, 0, G2, C0, NC>(wv, sc, taddr); break;
+        case 1: dq_store<3, 1, G2, C0, NC>(wv, sc, taddr); break;
+        case 2: dq_store<3, 2, G2, C0, NC>(wv, sc, taddr); break;
+        case 3: dq_store<3, 3, G2, C0, NC>(wv, sc, taddr); break;
+        default: dq_store<3, 4, G2, C0, NC>(wv, sc, taddr); break;
+      }
+      ph3 = (ph3 == 0) ? 4 : ph3 - 1;
+    } else {
+      dq_store<NB, 0, G2, C0, NC>(wv, sc, taddr);
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (e.lane == 0) mbar_arrive(&e.afull[r.as]);
+    if (++r.s == C::kStages) { r.s = 0; r.ph ^= 1u; }
+    if (++r.as == C::kAStages) { r.as = 0; r.aph ^= 1u; }
+  }
+  // release the item's last scale chunk
+  __syncwarp();
+  if (e.lane == 0) mbar_arrive(&e.sempty[r.c]);
+  if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
+  return true;
+}
+
+template <class C, bool G2, int C0, int NC>
+__device__ __forceinline__ bool dq_item_nb(int nb, DqRings& r, const DqEnv& e) {
+  switch (nb) {
+    case 1: return dq_item<C, 1, G2, C0, NC>(r, e);
+    case 2: return dq_item<C, 2, G2, C0, NC>(r, e);
+    case 3: return dq_item<C, 3, G2, C0, NC>(r, e);
+    default: return dq_item<C, 4, G2, C0, NC>(r, e);
+  }
+}
+
+template <class C, int C0, int NC>
+__device__ __forceinline__ bool dq_item_any(bool g2, int nb, DqRings& r, const DqEnv& e) {
+  return g2 ? dq_item_nb<C, true, C0, NC>(nb, r, e) : dq_item_nb<C, false, C0, NC>(nb, r, e);
+}
+
+// Destination column of source column f of the next projection's input.
+__device__ __forceinline__ int perm_dst(int nb, int f) {
+  const int st = f >> 7, q = f & 127;
+  if (nb == 3) return (st << 7) + c_perm3.inv[kperm::phase3(st)][q];
+  return (st << 7) + kperm::inv_pow2(nb, q);
+}
+
+// ---------------------------------------------------------------- epilogue math
+__device__ __forceinline__ float silu_ref_d(float x) { return x / (1.f + expf(-x)); }
+
+// ---------------------------------------------------------------- the kernel
+template <int NT, GemmMode MODE>
+__global__ void __launch_bounds__(kThreadsD, 1)
+    k_moe_tcd(const KArgsD p, const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ WordMapsD tm_words,
+              const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ CUtensorMap tm_z0,
+              const __grid_constant__ CUtensorMap tm_s1, const __grid_constant__ CUtensorMap tm_z1) {
+  using C = CfgD<NT, MODE>;
+  constexpr int kMats = C::kMats;
+  constexpr int kStages = C::kStages;
+  constexpr int kAStages = C::kAStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* full = bars;                   // [kStages] activations + words landed
+  uint64_t* empty = full + kStages;        // [kStages] stage consumed
+  uint64_t* sfull = empty + kStages;       // [2] scale chunk landed
+  uint64_t* sempty = sfull + 2;            // [2] scale chunk consumed
+  uint64_t* afull = sempty + 2;            // [kAStages] A stage written to TMEM
+  uint64_t* aempty = afull + kAStages;     // [kAStages] A stage read by the MMAs
+  uint64_t* acc_full = aempty + kAStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint64_t* drain = acc_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 2);       // both producers arm the stage
+      mbar_init(&empty[s], 1 + kNumDqWarps);  // MMA commit + every dequant warp
+    }
+    for (int c = 0; c < 2; ++c) {
+      mbar_init(&sfull[c], 1);
+      mbar_init(&sempty[c], kNumDqWarps);
+    }
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&afull[s], kNumDqWarps);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  Meta& meta = *reinterpret_cast<Meta*>(smem + C::kMetaOff);
+  tcw::stage_meta(meta, p, false);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = meta.tp[p.num_segs] * p.n_tiles;
+  const int KT = p.K / kSK;
+  const int g = p.group_size;
+  const int groups = p.K / g;
+  const int nchunks = (groups + kScRows - 1) / kScRows;
+
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------ stage producers
+    {
+      const bool first = (warp == 0);
+      const int mat = first ? 0 : 1;
+      if (elect_one()) {
+        if (first) {
+          tma_prefetch_desc(&tm_act);
+          for (int i = 0; i < 4; ++i) tma_prefetch_desc(&tm_words.m[0][i]);
+        } else if (kMats == 2) {
+          for (int i = 0; i < 4; ++i) tma_prefetch_desc(&tm_words.m[1][i]);
+        }
+      }
+      __syncwarp();
+      int s = 0;
+      uint32_t ph = 0;
+      int armed = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
+        const int nb = min(max(wk.nb, 1), 4);
+        const int rows = kperm::stage_word_rows(nb);
+        const bool words = first || kMats == 2;
+        const uint32_t tx = C::kActSub + (words ? rows * 512 : 0);
+        const CUtensorMap* wmap = &tm_words.m[mat][box_index(nb)];
+        const int wrow = first ? wk.wrow0 : wk.wrow1;
+        const int ncol = C::kPairTiles ? 2 * wk.n0 + mat * 128 : wk.n0;
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!warp_wait(&empty[s], ph ^ 1u, kDevTimeoutTmaEmpty, kIdleSleepNs)) { ok = false; break; }
+          uint8_t* st = smem + s * C::kStageBytes;
+          if (elect_one()) {
+            mbar_arrive_expect_tx(&full[s], tx);
+            tma_load_2d(st + mat * C::kActSub, &tm_act, &full[s], kt * kSK + mat * 64, wk.act_row);
+            if (words)
+              tma_load_2d(st + C::kActBytes + mat * C::kWordBytes, wmap, &full[s], ncol,
+                          wrow + kperm::stage_word_row(nb, kt));
+          }
+          __syncwarp();
+          ++armed;
+          if (++s == kStages) { s = 0; ph ^= 1u; }
+        }
+      }
+      for (int st = 0; st < kStages && st < armed; ++st) {
+        const int times = (armed - 1 - st) / kStages + 1;
+        mbar_wait_drain(&full[st], static_cast<uint32_t>((times - 1) & 1));
+      }
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ scale / zero chunks
+    {
+      if (elect_one()) {
+        tma_prefetch_desc(&tm_s0);
+        tma_prefetch_desc(&tm_z0);
+        if (kMats == 2) {
+          tma_prefetch_desc(&tm_s1);
+          tma_prefetch_desc(&tm_z1);
+        }
+      }
+      __syncwarp();
+      int c = 0;
+      uint32_t cph = 0;
+      int armed = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
+        for (int ch = 0; ch < nchunks; ++ch) {
+          if (!warp_wait(&sempty[c], cph ^ 1u, kDevTimeoutTmaEmpty, kIdleSleepNs)) { ok = false; break; }
+          uint8_t* cb = smem + C::kChunkOff + c * C::kChunkBytes;
+          if (elect_one()) {
+            mbar_arrive_expect_tx(&sfull[c], C::kChunkBytes);
+            const int n0 = C::kPairTiles ? 2 * wk.n0 : wk.n0;
+            tma_load_2d(cb, &tm_s0, &sfull[c], n0, wk.srow0 + ch * kScRows);
+            tma_load_2d(cb + C::kScBytes, &tm_z0, &sfull[c], n0, wk.srow0 + ch * kScRows);
+            if constexpr (kMats == 2) {
+              const int n1 = C::kPairTiles ? 2 * wk.n0 + 128 : wk.n0;
+              tma_load_2d(cb + 2 * C::kScBytes, &tm_s1, &sfull[c], n1, wk.srow1 + ch * kScRows);
+              tma_load_2d(cb + 3 * C::kScBytes, &tm_z1, &sfull[c], n1, wk.srow1 + ch * kScRows);
+            }
+          }
+          __syncwarp();
+          ++armed;
+          if (++c == 2) { c = 0; cph ^= 1u; }
+        }
+      }
+      for (int st = 0; st < 2 && st < armed; ++st) {
+        const int times = (armed - 1 - st) / 2 + 1;
+        mbar_wait_drain(&sfull[st], static_cast<uint32_t>((times - 1) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    // The whole warp runs the loop; one elected lane (always the same, lane 0 of a
+    // converged warp) issues every MMA and commit, so each commit tracks them all.
+    {
+      int s = 0, as = 0;
+      uint32_t ph = 0, aph = 0;
+      int it = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t d_base = tmem + static_cast<uint32_t>(buf * C::kAccCols);
+        if (!warp_wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1u, kDevTimeoutAccEmpty, kBusySleepNs)) break;
+        tc_fence_after();
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!warp_wait(&full[s], ph, kDevTimeoutTmaFull, kBusySleepNs)) { ok = false; break; }
+          if (!warp_wait(&afull[as], aph, kDevTimeoutAFull, kBusySleepNs)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t act = smem_u32(smem + s * C::kStageBytes);
+          const uint64_t b0 = sdesc_sw128(act);
+          const uint32_t a0 = tmem + static_cast<uint32_t>(C::kACol0 + as * C::kACols);
+          if (elect_one()) {
+#pragma unroll
+            for (int m = 0; m < kMats; ++m) {
+#pragma unroll
+              for (int kk = 0; kk < kSK / 16; ++kk) {
+                // +32 B per 16-k step inside a 128-byte row, +NT rows per 64-k sub-tile
+                const uint64_t bd = b0 + static_cast<uint64_t>(((kk >> 2) * C::kActSub + (kk & 3) * 32) >> 4);
+                umma_f16_ts(d_base + static_cast<uint32_t>(m * NT), a0 + static_cast<uint32_t>(m * 64 + kk * 8), bd,
+                            C::kIdesc, (kt | kk) != 0 ? 1u : 0u);
+              }
+            }
+            umma_commit(&empty[s]);
+            umma_commit(&aempty[as]);
+          }
+          __syncwarp();
+          if (++s == kStages) { s = 0; ph ^= 1u; }
+          if (++as == kAStages) { as = 0; aph ^= 1u; }
+        }
+        if (!ok) break;
+        if (elect_one()) umma_commit(&acc_full[buf]);
+        __syncwarp();
+      }
+      if (elect_one()) umma_commit(drain);
+      __syncwarp();
+      mbar_wait_drain(drain, 0);
+    }
+  } else if (warp < kDqWarp0) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    int it = 0;
+    for (int w = blockIdx.x; w < total; w += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const uint32_t lane_base =
+          tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * C::kAccCols);
+      const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
+      if (!warp_wait(&acc_full[buf], (it >> 1) & 1, kDevTimeoutAccFull, kIdleSleepNs)) break;
+      tc_fence_after();
+      __half* out = static_cast<__half*>(p.out);
+      if constexpr (MODE == GemmMode::kSwiGLU) {
+        const int f = wk.n0 + 32 * q + lane;
+        const int col =
+            (p.perm_out_nbits != nullptr) ? perm_dst(min(max(__ldg(p.perm_out_nbits + wk.e), 1), 4), f) : f;
+#pragma unroll
+        for (int c0 = 0; c0 < NT; c0 += 16) {
+          if (c0 >= wk.rows) break;  // warp-uniform
+          uint32_t r0[16], r1[16];
+          tmem_ld16(lane_base + c0, r0);
+          tmem_ld16(lane_base + NT + c0, r1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (c0 + i < wk.rows) {
+              // x1, x3 stored fp16; F.silu(x1) -> fp16; * x3 -> fp16 (moe_block.py:774-775)
+              const float x1 = __half2float(__float2half_rn(__uint_as_float(r0[i])));
+              const float x3 = __half2float(__float2half_rn(__uint_as_float(r1[i])));
+              const float sl = __half2float(__float2half_rn(silu_ref_d(x1)));
+              out[static_cast<int64_t>(wk.out_row + c0 + i) * p.out_ld + col] = __float2half_rn(sl * x3);
+            }
+          }
+        }
+      } else {
+        // two feature tiles: y = fp16(acc), y * w -> fp16 (moe_block.py:778, 811)
+        const int f0 = 2 * wk.n0 + 32 * q + lane;
+#pragma unroll
+        for (int c0 = 0; c0 < NT; c0 += 16) {
+          if (c0 >= wk.rows) break;  // warp-uniform
+          uint32_t r0[16], r1[16];
+          tmem_ld16(lane_base + c0, r0);
+          tmem_ld16(lane_base + NT + c0, r1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (c0 + i < wk.rows) {
+              const int64_t row = wk.out_row + c0 + i;
+              const float wt = __half2float(p.row_weight[row]);
+              const float y0 = __half2float(__float2half_rn(__uint_as_float(r0[i])));
+              const float y1 = __half2float(__float2half_rn(__uint_as_float(r1[i])));
+              out[row * p.out_ld + f0] = __float2half_rn(y0 * wt);
+              out[row * p.out_ld + f0 + 128] = __float2half_rn(y1 * wt);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  } else {
+    // ------------------------------------------------------------ dequant
+    const int dw = warp - kDqWarp0;  // 0..15
+    const int q = warp & 3;           // TMEM lane quarter = features 32q .. 32q+31
+    const int part = dw >> 3;  // k half of the stage
+    DqEnv env;
+    env.stages = smem;
+    env.chunks = smem + C::kChunkOff;
+    env.full = full;
+    env.empty = empty;
+    env.sfull = sfull;
+    env.sempty = sempty;
+    env.afull = afull;
+    env.aempty = aempty;
+    env.a_col0 = tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(C::kACol0);
+    env.n = static_cast<uint32_t>(32 * q + lane);
+    env.lane = lane;
+    env.mat = (dw >> 2) & 1;
+    env.KT = KT;
+    env.log2g = 31 - __clz(g);
+    const bool g2 = (g == 64);
+    DqRings rings{0, 0, 0, 0u, 0u, 0u};
+    for (int w = blockIdx.x; w < total; w += gridDim.x) {
+      const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
+      if ((wk.nb < 1 || wk.nb > 4) && dw == 0 && lane == 0) set_device_error(kDevBadBits);
+      const int nb = min(max(wk.nb, 1), 4);
+      bool ok;
+      ok = (part == 0) ? dq_item_any<C, 0, 32>(g2, nb, rings, env) : dq_item_any<C, 32, 32>(g2, nb, rings, env);
+      if (!ok) break;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn_d() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+  }
+  return fn;
+}
+
+bool make_map_d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                uint64_t outer, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  auto fn = encode_fn_d();
+  if (fn == nullptr || base == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * static_cast<uint64_t>(elem_bytes)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_word_maps_d(CUtensorMap (&maps)[4], const ProjDev& w) {
+  for (int nb = 1; nb <= 4; ++nb) {
+    if (!make_map_d(&maps[box_index(nb)], w.wq, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, w.n, w.wq_rows, 128,
+                    kperm::stage_word_rows(nb), CU_TENSOR_MAP_SWIZZLE_NONE))
+      return false;
+  }
+  return true;
+}
+
+template <int NT, GemmMode MODE>
+cudaError_t launch_d(const GemmArgs& a, cudaStream_t stream) {
+  using C = CfgD<NT, MODE>;
+  CUtensorMap m_act, m_s0, m_z0, m_s1, m_z1;
+  WordMapsD words;
+  const int K = a.w0.k;
+  if (!make_map_d(&m_act, a.act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, static_cast<uint64_t>(a.act_rows), 64, NT,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  const uint64_t srows = static_cast<uint64_t>(a.w0.num_experts) * (a.w0.k / a.w0.group_size);
+  if (!make_word_maps_d(words.m[0], a.w0) ||
+      !make_map_d(&m_s0, a.w0.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w0.n, srows, 128, kScRows,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_d(&m_z0, a.w0.zeros, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w0.n, srows, 128, kScRows,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  if constexpr (!C::kPairTiles) {
+    const uint64_t srows1 = static_cast<uint64_t>(a.w1.num_experts) * (a.w1.k / a.w1.group_size);
+    if (!make_word_maps_d(words.m[1], a.w1) ||
+        !make_map_d(&m_s1, a.w1.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w1.n, srows1, 128, kScRows,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_d(&m_z1, a.w1.zeros, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.w1.n, srows1, 128, kScRows,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  } else {
+    for (int i = 0; i < 4; ++i) words.m[1][i] = words.m[0][i];
+    m_s1 = m_s0;
+    m_z1 = m_z0;
+  }
+  KArgsD p;
+  p.nbits = a.w0.nbits;
+  p.wq_strides0 = a.w0.wq_strides;
+  p.zs_strides0 = a.w0.zs_strides;
+  p.wq_strides1 = C::kPairTiles ? a.w0.wq_strides : a.w1.wq_strides;
+  p.zs_strides1 = C::kPairTiles ? a.w0.zs_strides : a.w1.zs_strides;
+  p.segs = a.segs;
+  p.tile_prefix = a.tile_prefix;
+  p.num_segs = a.num_segs;
+  p.N = a.w0.n;
+  p.K = K;
+  p.group_size = a.w0.group_size;
+  p.n_tiles = a.w0.n / (C::kPairTiles ? 256 : 128);
+  p.out = a.out;
+  p.out_ld = a.out_ld;
+  p.row_weight = reinterpret_cast<const __half*>(a.row_weight);
+  p.perm_out_nbits = a.perm_out_nbits;
+  auto kern = k_moe_tcd<NT, MODE>;
+  static bool attr_set = false;  // set once per instantiation (outside any graph capture)
+  if (!attr_set) {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    attr_set = true;
+  }
+  kern<<<a.num_sms, kThreadsD, C::kSmemBytes, stream>>>(p, m_act, words, m_s0, m_z0, m_s1, m_z1);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tcd_gemm_supported(const GemmArgs& a) {
+  if (encode_fn_d() == nullptr) return false;
+  if (a.nt != kNtSmall) return false;
+  if (a.mode != GemmMode::kSwiGLU && a.mode != GemmMode::kRouteWeight) return false;
+  if (a.w0.k <= 0 || a.w0.k % kSK != 0 || a.w0.n % 128 != 0) return false;
+  const int g = a.w0.group_size;
+  if ((g & (g - 1)) != 0 || (g != 64 && g % 128 != 0)) return false;  // 64 or a power of two >= 128
+  if (a.num_segs <= 0 || a.num_segs > tcw::kMaxSegs) return false;
+  if (a.mode == GemmMode::kSwiGLU && (a.w1.n != a.w0.n || a.w1.k != a.w0.k || a.w1.group_size != a.w0.group_size))
+    return false;
+  if (a.mode == GemmMode::kRouteWeight && a.w0.n % 256 != 0) return false;  // tiles pair up
+  return (reinterpret_cast<uintptr_t>(a.act) & 15u) == 0;
+}
+
+cudaError_t launch_tcd_gemm(const GemmArgs& a, cudaStream_t stream) {
+  if (!tcd_gemm_supported(a)) return cudaErrorNotSupported;
+  return a.mode == GemmMode::kSwiGLU ? launch_d<kNtSmall, GemmMode::kSwiGLU>(a, stream)
+                                     : launch_d<kNtSmall, GemmMode::kRouteWeight>(a, stream);
+}
+
+// Source column of destination column k of an activation row stored in the decode
+// GEMM's slot order for bit-width nb (host copy of the table, for tests).
+int kperm_source_column(int nb, int k) {
+  const int st = k / kSK, s = k % kSK;
+  if (nb == 3) {
+    constexpr kperm::Perm3 t = kperm::make_perm3();
+    return st * kSK + t.fwd[kperm::phase3(st)][s];
+  }
+  return st * kSK + kperm::perm_pow2(nb, s);
+}
+
+}  // namespace gemq
