@@ -171,9 +171,10 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_small(const __half* __r
 
 // Copies token row `src` to `dst` (D fp16, D % 8 == 0) by one warp: as is, or in
 // the decode GEMM's K slot order for bit-width nb (kperm.cuh; D % 128 == 0 then),
-// gathering through the warp's staging buffer `sbuf` (D halves of shared memory).
+// gathering through the warp's staging buffer `sbuf` (D halves of shared memory) and
+// the 3-bit slot table `fwd3` staged in shared memory (lanes index it divergently).
 __device__ __forceinline__ void copy_row(const __half* __restrict__ src, __half* __restrict__ dst, int D, int nb,
-                                         int lane, __half* sbuf) {
+                                         int lane, __half* sbuf, const uint8_t (*fwd3)[128]) {
   const uint4* s4 = reinterpret_cast<const uint4*>(src);
   uint4* d4 = reinterpret_cast<uint4*>(dst);
   if (nb == 0) {
@@ -184,20 +185,34 @@ __device__ __forceinline__ void copy_row(const __half* __restrict__ src, __half*
   for (int i = lane; i < D / 8; i += 32) b4[i] = s4[i];
   __syncwarp();
   const unsigned short* b16 = reinterpret_cast<const unsigned short*>(sbuf);
+  // b in {1, 2, 4}: eps = 32 / b codes per word, slot 2j + h of a word block <-> code
+  // j + h * eps / 2 (kperm::perm_pow2), with shifts and masks instead of divisions
+  const int lg_eps = 5 - (nb >> 1);  // nb = 1, 2, 4 -> 5, 4, 3
+  const int eps_mask = (1 << lg_eps) - 1, half = 1 << (lg_eps - 1);
   for (int i = lane; i < D / 8; i += 32) {
     const int k0 = 8 * i, st = k0 >> 7;
-    const int ph = kperm::phase3(st);
+    const unsigned short* row = b16 + (st << 7);
     uint32_t v[4];
+    if (nb == 3) {
+      const uint8_t* f = fwd3[kperm::phase3(st)] + (k0 & 127);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int sa = (k0 + 2 * m) & 127, sb = sa + 1;
-      const int a = (nb == 3) ? c_perm3_route.fwd[ph][sa] : kperm::perm_pow2(nb, sa);
-      const int b = (nb == 3) ? c_perm3_route.fwd[ph][sb] : kperm::perm_pow2(nb, sb);
-      v[m] = static_cast<uint32_t>(b16[(st << 7) + a]) | (static_cast<uint32_t>(b16[(st << 7) + b]) << 16);
+      for (int m = 0; m < 4; ++m)
+        v[m] = static_cast<uint32_t>(row[f[2 * m]]) | (static_cast<uint32_t>(row[f[2 * m + 1]]) << 16);
+    } else {
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int sa = (k0 + 2 * m) & 127;  // even slot: code j, odd slot sa + 1: code j + eps / 2
+        const int a = (sa & ~eps_mask) + ((sa & eps_mask) >> 1);
+        v[m] = static_cast<uint32_t>(row[a]) | (static_cast<uint32_t>(row[a + half]) << 16);
+      }
     }
     d4[i] = make_uint4(v[0], v[1], v[2], v[3]);
   }
   __syncwarp();
+}
+
+__device__ __forceinline__ void stage_fwd3(uint8_t (*fwd3)[128]) {
+  for (int i = threadIdx.x; i < 5 * 128; i += blockDim.x) fwd3[i >> 7][i & 127] = c_perm3_route.fwd[i >> 7][i & 127];
 }
 
 // ------------------------------------------------------------------ dispatch (large batches)
@@ -248,6 +263,11 @@ __global__ void k_scatter(const int32_t* __restrict__ topk_idx, const __half* __
                           const __half* __restrict__ x, int64_t P, int k, int E, int D, int32_t* __restrict__ cursor,
                           int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm, __half* __restrict__ x_perm,
                           const int32_t* __restrict__ perm_nbits) {
+  __shared__ uint8_t s_fwd3[5][128];
+  if (perm_nbits != nullptr) {
+    stage_fwd3(s_fwd3);
+    __syncthreads();
+  }
   const int64_t slot = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (slot >= P) return;
@@ -267,7 +287,7 @@ __global__ void k_scatter(const int32_t* __restrict__ topk_idx, const __half* __
   const int nb = perm_nbits != nullptr ? min(max(__ldg(perm_nbits + e), 1), 4) : 0;
   extern __shared__ __align__(16) __half s_stage_rows[];
   copy_row(x + t * D, x_perm + static_cast<int64_t>(pos) * D, D, nb, lane,
-           s_stage_rows + static_cast<size_t>(threadIdx.x >> 5) * D);
+           s_stage_rows + static_cast<size_t>(threadIdx.x >> 5) * D, s_fwd3);
 }
 
 // ------------------------------------------------------------------ dispatch (small batches)
@@ -314,8 +334,10 @@ __global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restric
   __shared__ int s_tiles[kMaxExperts];
   __shared__ int s_start[kMaxExperts + 1];
   __shared__ int s_tstart[kMaxExperts + 1];
+  __shared__ uint8_t s_fwd3[5][128];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+  if (perm_nbits != nullptr) stage_fwd3(s_fwd3);
   __syncthreads();
   for (int i = threadIdx.x; i < P; i += blockDim.x) {
     const int e = topk_idx[i];
@@ -356,7 +378,7 @@ __global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restric
   const int nb = perm_nbits != nullptr ? min(max(__ldg(perm_nbits + e), 1), 4) : 0;
   extern __shared__ __align__(16) __half s_stage_rows[];
   copy_row(x + static_cast<int64_t>(slot / k) * D, x_perm + static_cast<int64_t>(pos) * D, D, nb, lane,
-           s_stage_rows + static_cast<size_t>(warp) * D);
+           s_stage_rows + static_cast<size_t>(warp) * D, s_fwd3);
 }
 
 // ------------------------------------------------------------------ combine
