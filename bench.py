@@ -317,7 +317,9 @@ def run_ours(args, rank, world, local_rank):
         "stages": list(names),
         "roofline": {"bound": "hbm", "kernel": f"{names[dom_s]} stage at batch {dom_b}",
                      "achieved": round(achieved, 1) if achieved else None, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(achieved / hbm_peak, 3) if achieved else None, "traffic": None,
+                     "frac": round(achieved / hbm_peak, 3) if achieved else None,
+                     "traffic": profiled_traffic(names[dom_s], dom_b),
+                     "algorithmic_bytes": round(dom_bytes) if dom_bytes else None,
                      "peak_source": peak_src},
         "e2e": {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d,
@@ -333,11 +335,27 @@ def run_ours(args, rank, world, local_rank):
 
 
 def kernel_launches(blocks, batches):
-    """Kernels of ours per step, counted from the pipeline: one-token path 9 per layer
-    (router, top-k, 2 up partials, 2 reduces, down partial, reduce, combine); n-token
-    path 8 (router, top-k, count, scan, scatter, up, down, combine; the counter reset
-    is a memset node)."""
-    return sum(len(blocks) * (9 if B == 1 else 8) for B in batches)
+    """Kernels of ours per step, counted from the pipeline: one-token path 4 per layer
+    (fused router + top-k, gate/up GEMV, down GEMV reducing the up partials, combine
+    reducing the down partials); n-token path at these batch sizes 5 (fused router +
+    top-k, one-launch dispatch, gate/up GEMM, down GEMM, combine)."""
+    return sum(len(blocks) * (4 if B == 1 else 5) for B in batches)
+
+
+def profiled_traffic(kernel: str, batch: int):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary
+    (profiles/k_moe_tcd_olmoe_b64.md), or None when no capture covers it."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "k_moe_tcd_olmoe_b64.md")
+    key = f"{kernel}_b{batch}"
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes:"):
+                name, val = line.split(":", 1)[1].split()
+                if name == key:
+                    return int(val)
+    except OSError:
+        return None
+    return None
 
 
 def run_prefill(args, device, bf16_peak, bf16_sus):
