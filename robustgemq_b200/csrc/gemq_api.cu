@@ -125,8 +125,9 @@ struct Carver {
 
 int choose_nt(int64_t rows_per_expert) { return rows_per_expert > 48 ? kNtLarge : kNtSmall; }
 
-// Up to this many tokens the router runs as one fused gate-GEMV + top-k launch;
-// beyond it, as a tensor-core GEMM followed by the top-k kernel.
+// Up to this many tokens the router's gate logits run as a CUDA-core kernel spread
+// over (expert group x token group) CTAs; beyond it, as a tensor-core GEMM. The
+// top-k kernel follows either.
 constexpr int64_t kSmallRouteTokens = 256;
 
 // Runs one grouped GEMM, tensor cores when the shape allows, CUDA cores otherwise.
@@ -521,14 +522,11 @@ int run_router(gemq_layer_t* L, const uint16_t* x, int64_t T, void* logits_out, 
   const bool norm = d.norm_topk_prob != 0;
   const bool fp16_softmax = (flags & GEMQ_FWD_FP16_SOFTMAX) != 0;
   if (!logits_given && T <= kSmallRouteTokens) {
-    // small batches: gate dot products + top-k in one launch
-    GEMQ_CUDA(launch_route_small(x, T, d.hidden, d.gate_weight, d.num_experts, d.router == GEMQ_ROUTER_FP32,
-                                 logits_out, d.top_k, norm, fp16_softmax, idx, w, s),
+    // small batches: gate dot products spread over (expert group x token group) CTAs
+    GEMQ_CUDA(launch_gate_logits(x, T, d.hidden, d.gate_weight, d.num_experts, d.router == GEMQ_ROUTER_FP32,
+                                 logits_out, s),
               "router");
-    if (tm) tm->end(GEMQ_STAGE_ROUTE);
-    return GEMQ_OK;
-  }
-  if (!logits_given) {
+  } else if (!logits_given) {
     GemmArgs a{};
     a.mode = d.router == GEMQ_ROUTER_FP32 ? GemmMode::kDenseF32 : GemmMode::kDenseF16;
     a.w0.k = d.hidden;
@@ -720,6 +718,8 @@ int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens,
   if (num_tokens < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative token count");
   if (num_tokens == 0) return GEMQ_OK;  // empty batch: nothing to read or write (pointers may be null)
   if (x == nullptr || out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(GEMQ_ERR_UNSUPPORTED, "x and out must be 16-byte aligned");
   const bool one = (flags & GEMQ_FWD_ONE_TOKEN) != 0;
   if (one && num_tokens != 1)
     return fail(GEMQ_ERR_INVALID_ARGUMENT,

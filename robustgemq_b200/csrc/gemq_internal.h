@@ -79,12 +79,11 @@ cudaError_t launch_build_index_segs(const int32_t* indices, int num_indices, int
                                     Seg* segs, int32_t* tile_prefix, cudaStream_t stream);
 
 // Routing / dispatch / combine.
+// Gate logits of a small batch over many CTAs (then launch_topk).
+cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16_t* gate, int E, bool fp32_logits,
+                               void* logits, cudaStream_t stream);
 cudaError_t launch_topk(const void* logits, bool logits_fp32, int64_t T, int E, int k, bool norm, bool fp16_softmax,
                         int32_t* topk_idx, uint16_t* topk_w, cudaStream_t stream);
-// gate GEMM + top-k in one launch, one CTA per token (small batches)
-cudaError_t launch_route_small(const uint16_t* x, int64_t T, int D, const uint16_t* gate, int E, bool fp32_logits,
-                               void* logits_out, int k, bool norm, bool fp16_softmax, int32_t* topk_idx,
-                               uint16_t* topk_w, cudaStream_t stream);
 bool small_dispatch_ok(int64_t P, int E);
 cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t T, int k,
                             int E, int D, int nt, int32_t* counts, int32_t* cursor, Seg* segs, int32_t* tile_prefix,

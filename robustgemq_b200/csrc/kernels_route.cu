@@ -117,56 +117,64 @@ __global__ void k_topk(const void* __restrict__ logits, int logits_fp32, int64_t
   topk_warp(get, E, k, norm, fp16_softmax, topk_idx + t * k, topk_w + t * k);
 }
 
-// Small-batch router: one CTA per token computes the E gate dot products (fp32
-// accumulation; the fp16 router rounds each logit to fp16 as F.linear's fp16 output
-// does) and the top-k in one launch.
-constexpr int kRouteThreads = 1024;  // upper bound; small batches use all of it
+// Gate logits for small batches, spread over many CTAs: CTA (i, j) computes experts
+// 8i .. 8i+7 (one warp each) for tokens 8j .. 8j+7 (rows staged in shared memory),
+// fp32 accumulation; the fp16 router rounds each logit to fp16 as F.linear's fp16
+// output does (moe_block.py:790), the fp32 router keeps it (moe_block.py:549).
+constexpr int kLogitExperts = 8;
+constexpr int kLogitTokens = 8;
 
-__global__ void __launch_bounds__(kRouteThreads) k_route_small(const __half* __restrict__ x, int D,
-                                                               const __half* __restrict__ gate, int E, int fp32_logits,
-                                                               void* __restrict__ logits_out, int k, int norm,
-                                                               int fp16_softmax, int32_t* __restrict__ topk_idx,
-                                                               __half* __restrict__ topk_w) {
-  extern __shared__ uint4 s_x4[];
-  __shared__ float s_logit[kMaxExperts];
-  const int64_t t = blockIdx.x;
+__global__ void __launch_bounds__(256) k_gate_logits(const __half* __restrict__ x, int64_t T, int D,
+                                                     const __half* __restrict__ gate, int E, int fp32_logits,
+                                                     void* __restrict__ logits) {
+  extern __shared__ uint4 s_rows4[];  // [kLogitTokens][D / 8]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + t * D);
-  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) s_x4[i] = xr[i];
+  const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kLogitTokens;
+  const int nt = (T - t0 < kLogitTokens) ? static_cast<int>(T - t0) : kLogitTokens;
+  const int d8 = D / 8;
+  for (int i = threadIdx.x; i < nt * d8; i += blockDim.x) {
+    const int r = i / d8, c = i - r * d8;
+    s_rows4[r * d8 + c] = reinterpret_cast<const uint4*>(x + (t0 + r) * D)[c];
+  }
   __syncthreads();
-  const int nwarps = blockDim.x >> 5;
-  for (int e = warp; e < E; e += nwarps) {
-    const uint4* gr = reinterpret_cast<const uint4*>(gate + static_cast<int64_t>(e) * D);
-    float acc = 0.f;
-#pragma unroll 8
-    for (int i = lane; i < D / 8; i += 32) {
-      const uint4 gv = __ldg(gr + i);
-      const uint4 xv = s_x4[i];
-      const __half2* gh = reinterpret_cast<const __half2*>(&gv);
-      const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+  const int e = blockIdx.x * kLogitExperts + warp;
+  if (e >= E) return;
+  const uint4* gr = reinterpret_cast<const uint4*>(gate + static_cast<int64_t>(e) * D);
+  float acc[kLogitTokens];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 a = __half22float2(xh[j]);
-        const float2 b = __half22float2(gh[j]);
-        acc = fmaf(a.x, b.x, acc);
-        acc = fmaf(a.y, b.y, acc);
-      }
-    }
+  for (int r = 0; r < kLogitTokens; ++r) acc[r] = 0.f;
+#pragma unroll 4
+  for (int c = lane; c < d8; c += 32) {
+    const uint4 gv = __ldg(gr + c);
+    const __half2* gh = reinterpret_cast<const __half2*>(&gv);
+    float2 g2[4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) {
-      if (fp32_logits) {
-        s_logit[e] = acc;
-        if (logits_out) static_cast<float*>(logits_out)[t * E + e] = acc;
-      } else {
-        const __half h = __float2half_rn(acc);
-        s_logit[e] = __half2float(h);
-        if (logits_out) static_cast<__half*>(logits_out)[t * E + e] = h;
+    for (int j = 0; j < 4; ++j) g2[j] = __half22float2(gh[j]);
+#pragma unroll
+    for (int r = 0; r < kLogitTokens; ++r) {
+      if (r < nt) {
+        const uint4 xv = s_rows4[r * d8 + c];
+        const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 a = __half22float2(xh[j]);
+          acc[r] = fmaf(a.x, g2[j].x, acc[r]);
+          acc[r] = fmaf(a.y, g2[j].y, acc[r]);
+        }
       }
     }
   }
-  __syncthreads();
-  if (warp == 0) topk_warp([&](int e) { return s_logit[e]; }, E, k, norm, fp16_softmax, topk_idx + t * k, topk_w + t * k);
+#pragma unroll
+  for (int r = 0; r < kLogitTokens; ++r) {
+    float v = acc[r];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0 && r < nt) {
+      const int64_t i = (t0 + r) * E + e;
+      if (fp32_logits) static_cast<float*>(logits)[i] = v;
+      else static_cast<__half*>(logits)[i] = __float2half_rn(v);
+    }
+  }
 }
 
 // Copies token row `src` to `dst` (D fp16, D % 8 == 0) by one warp: as is, or in
@@ -407,32 +415,36 @@ __global__ void k_combine(const __half* __restrict__ y_perm, const int32_t* __re
     eid[b + 1] = e;
     order[b + 1] = o;
   }
-  for (int d = threadIdx.x * 2; d < D; d += blockDim.x * 2) {
-    float2 acc = make_float2(0.f, 0.f);
+  for (int d = threadIdx.x * 8; d < D; d += blockDim.x * 8) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     for (int j = 0; j < k; ++j) {
       if (order[j] < 0) continue;  // slot with an invalid expert id
-      const float2 y =
-          __half22float2(*reinterpret_cast<const __half2*>(y_perm + static_cast<int64_t>(order[j]) * D + d));
-      if (fp32_sum) {
-        acc.x += y.x;
-        acc.y += y.y;
-      } else {
-        acc.x = __half2float(__float2half_rn(acc.x + y.x));
-        acc.y = __half2float(__float2half_rn(acc.y + y.y));
+      const uint4 yv = *reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(order[j]) * D + d);
+      const __half* yh = reinterpret_cast<const __half*>(&yv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float y = __half2float(yh[i]);
+        acc[i] = fp32_sum ? acc[i] + y : __half2float(__float2half_rn(acc[i] + y));
       }
     }
-    __half2 r = __floats2half2_rn(acc.x, acc.y);
+    __half r[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] = __float2half_rn(acc[i]);
     if (add != nullptr) {
-      const float2 a2 = __half22float2(*reinterpret_cast<const __half2*>(add + t * D + d));
-      const float2 r2 = __half22float2(r);
-      r = __floats2half2_rn(r2.x + a2.x, r2.y + a2.y);
+      const uint4 av = *reinterpret_cast<const uint4*>(add + t * D + d);
+      const __half* ah = reinterpret_cast<const __half*>(&av);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = __float2half_rn(__half2float(r[i]) + __half2float(ah[i]));
     }
     if (residual != nullptr) {
-      const float2 a2 = __half22float2(*reinterpret_cast<const __half2*>(residual + t * D + d));
-      const float2 r2 = __half22float2(r);
-      r = __floats2half2_rn(r2.x + a2.x, r2.y + a2.y);
+      const uint4 rv = *reinterpret_cast<const uint4*>(residual + t * D + d);
+      const __half* rh = reinterpret_cast<const __half*>(&rv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = __float2half_rn(__half2float(r[i]) + __half2float(rh[i]));
     }
-    *reinterpret_cast<__half2*>(out + t * D + d) = r;
+    *reinterpret_cast<uint4*>(out + t * D + d) = *reinterpret_cast<const uint4*>(r);
   }
 }
 
@@ -447,22 +459,24 @@ cudaError_t launch_topk(const void* logits, bool logits_fp32, int64_t T, int E, 
   return cudaGetLastError();
 }
 
-cudaError_t launch_route_small(const uint16_t* x, int64_t T, int D, const uint16_t* gate, int E, bool fp32_logits,
-                               void* logits_out, int k, bool norm, bool fp16_softmax, int32_t* topk_idx,
-                               uint16_t* topk_w, cudaStream_t stream) {
+cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16_t* gate, int E, bool fp32_logits,
+                               void* logits, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  const size_t smem = static_cast<size_t>(D) * 2;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k_route_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const size_t smem = static_cast<size_t>(kLogitTokens) * D * 2;
+  static size_t smem_set = 48 * 1024;
+  if (smem > smem_set) {
+    cudaError_t e = cudaFuncSetAttribute(k_gate_logits, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
+    smem_set = smem;
   }
-  const int threads = T <= 16 ? 1024 : 256;  // one CTA per token: fewer tokens, wider CTAs
-  k_route_small<<<static_cast<unsigned>(T), threads, smem, stream>>>(
-      reinterpret_cast<const __half*>(x), D, reinterpret_cast<const __half*>(gate), E, fp32_logits ? 1 : 0,
-      logits_out, k, norm ? 1 : 0, fp16_softmax ? 1 : 0, topk_idx, reinterpret_cast<__half*>(topk_w));
+  const dim3 grid((E + kLogitExperts - 1) / kLogitExperts, static_cast<unsigned>((T + kLogitTokens - 1) / kLogitTokens));
+  k_gate_logits<<<grid, 32 * kLogitExperts, smem, stream>>>(reinterpret_cast<const __half*>(x), T, D,
+                                                             reinterpret_cast<const __half*>(gate), E,
+                                                             fp32_logits ? 1 : 0, logits);
   return cudaGetLastError();
 }
+
 
 bool small_dispatch_ok(int64_t P, int E) { return P <= kSmallDispatchMaxSlots && E <= kMaxExperts; }
 
