@@ -249,7 +249,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    // The whole warp runs the loop; an elected lane issues (operands stay warp-uniform).
+    {
       int s = 0;
       uint32_t ph = 0;
       int armed = 0;
@@ -261,10 +262,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int box = nb == 1 ? 0 : nb == 2 ? 1 : 2;  // word-row map index
         const uint32_t tx = C::tx_bytes(nb);
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&empty[s], ph ^ 1u, kDevTimeoutTmaEmpty)) { ok = false; break; }
+          if (!warp_wait(&empty[s], ph ^ 1u, kDevTimeoutTmaEmpty, 128)) { ok = false; break; }
           uint8_t* st = smem + s * C::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], tx);
           const int k0 = kt * kBK;
+          if (elect_one()) {
+          mbar_arrive_expect_tx(&full[s], tx);
           tma_load_2d(st, &tm_act, &full[s], k0, wk.act_row);
           if constexpr (kDense) {
             tma_load_2d(st + C::kActBytes, &tm_words.m[0][2], &full[s], k0, wk.n0);
@@ -280,6 +282,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(st + C::kSzOff + 3 * C::kSzBytes, &tm_z1, &full[s], wk.n0, wk.srow1 + sr);
             }
           }
+          }
+          __syncwarp();
           ++armed;
           if (++s == kStages) { s = 0; ph ^= 1u; }
         }
@@ -287,12 +291,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // drain: wait for the last armed phase of every stage (loads still in flight)
       for (int st = 0; st < kStages && st < armed; ++st) {
         const int times = (armed - 1 - st) / kStages + 1;
-        mbar_wait(&full[st], static_cast<uint32_t>((times - 1) & 1), kDevTimeoutDrain);
+        mbar_wait_drain(&full[st], static_cast<uint32_t>((times - 1) & 1));
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop; one elected lane (lane 0 of the converged warp,
+    // always the same one) issues every MMA and commit, so each commit tracks them all.
+    {
       int s = 0, as = 0;
       uint32_t ph = 0, aph = 0;
       int it = 0;
@@ -300,15 +306,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
         const int buf = it & 1;
         const uint32_t d_base = tmem + static_cast<uint32_t>(buf * C::kAccCols);
-        if (!mbar_wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1u, kDevTimeoutAccEmpty)) break;
+        if (!warp_wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1u, kDevTimeoutAccEmpty)) break;
         tc_fence_after();
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&full[s], ph, kDevTimeoutTmaFull)) { ok = false; break; }
+          if (!warp_wait(&full[s], ph, kDevTimeoutTmaFull)) { ok = false; break; }
           if constexpr (!kDense) {
-            if (!mbar_wait(&afull[as], aph, kDevTimeoutAFull)) { ok = false; break; }
+            if (!warp_wait(&afull[as], aph, kDevTimeoutAFull)) { ok = false; break; }
           }
           tc_fence_after();
           const uint32_t act_addr = smem_u32(smem + s * C::kStageBytes);
+          if (elect_one()) {
 #pragma unroll
           for (int m = 0; m < kMats; ++m) {
             const uint32_t a_addr = kDense ? act_addr + C::kActBytes
@@ -321,16 +328,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           umma_commit(&empty[s]);
           if constexpr (!kDense) umma_commit(&aempty[as]);
+          }
+          __syncwarp();
           if (++s == kStages) { s = 0; ph ^= 1u; }
           if constexpr (!kDense) {
             if (++as == kAStages) { as = 0; aph ^= 1u; }
           }
         }
         if (!ok) break;
-        umma_commit(&acc_full[buf]);
+        if (elect_one()) umma_commit(&acc_full[buf]);
+        __syncwarp();
       }
-      umma_commit(drain);
-      mbar_wait(drain, 0, kDevTimeoutDrain);
+      if (elect_one()) umma_commit(drain);
+      __syncwarp();
+      mbar_wait_drain(drain, 0);
     }
   } else if (warp < kDqWarp0) {
     // ------------------------------------------------------------ epilogue

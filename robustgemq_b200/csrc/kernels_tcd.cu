@@ -74,16 +74,20 @@ struct CfgD {
   static constexpr int kStages = cmin_d(8, kBudget / kStageBytes);
   static constexpr int kChunkOff = kStages * kStageBytes;
   static constexpr int kBarOff = kChunkOff + 2 * kChunkBytes;
-  static constexpr int kAStages = kMats == 2 ? 3 : 6;
+  // TMEM: accumulator buffers (two when they fit beside the A ring, so one item's
+  // epilogue overlaps the next item's MMAs), then the A ring.
+  static constexpr int kAccCols = kMats * NT;  // one accumulator buffer
+  static constexpr int kACols = kMats * 64;    // one A stage: 128 fp16 k per matrix
+  static constexpr int kAccBufs = (2 * kAccCols + 2 * kACols <= 512) ? 2 : 1;
+  static constexpr int kACol0 = kAccBufs * kAccCols;  // first A column
+  static constexpr int kAStages = cmin_d(3, (512 - kACol0) / kACols);
   static constexpr int kNumBars = 2 * kStages + 4 + 2 * kAStages + 5;
   static constexpr int kMetaOff = round_up_d(kBarOff + kNumBars * 8 + 16, 16);
   static constexpr int kSmemBytes = kMetaOff + tcw::kMetaBytes + 1024;
-  static constexpr int kAccCols = kMats * NT;  // one accumulator buffer
-  static constexpr int kACol0 = 2 * kAccCols;  // first A column
-  static constexpr int kACols = kMats * 64;    // one A stage: 128 fp16 k per matrix
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kIdesc = idesc_f16_f32(128, NT);
   static_assert(kStages >= 3, "shared memory budget too small");
+  static_assert(kAStages >= 2, "tensor memory budget too small");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget exceeded");
   static_assert(kACol0 + kAStages * kACols <= 512, "tensor memory budget exceeded");
 };
@@ -447,9 +451,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       int it = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
-        const int buf = it & 1;
+        const int buf = it % C::kAccBufs;
         const uint32_t d_base = tmem + static_cast<uint32_t>(buf * C::kAccCols);
-        if (!warp_wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1u, kDevTimeoutAccEmpty, kBusySleepNs)) break;
+        if (!warp_wait(&acc_empty[buf], ((it / C::kAccBufs) & 1) ^ 1u, kDevTimeoutAccEmpty, kBusySleepNs)) break;
         tc_fence_after();
         for (int kt = 0; kt < KT; ++kt) {
           if (!warp_wait(&full[s], ph, kDevTimeoutTmaFull, kBusySleepNs)) { ok = false; break; }
@@ -489,11 +493,11 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     const int q = warp & 3;
     int it = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++it) {
-      const int buf = it & 1;
+      const int buf = it % C::kAccBufs;
       const uint32_t lane_base =
           tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * C::kAccCols);
       const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
-      if (!warp_wait(&acc_full[buf], (it >> 1) & 1, kDevTimeoutAccFull, kIdleSleepNs)) break;
+      if (!warp_wait(&acc_full[buf], (it / C::kAccBufs) & 1, kDevTimeoutAccFull, kIdleSleepNs)) break;
       tc_fence_after();
       __half* out = static_cast<__half*>(p.out);
       if constexpr (MODE == GemmMode::kSwiGLU) {
@@ -680,6 +684,8 @@ cudaError_t launch_d(const GemmArgs& a, cudaStream_t stream) {
 
 bool tcd_gemm_supported(const GemmArgs& a) {
   if (encode_fn_d() == nullptr) return false;
+  // 32-token tiles (decode batches); prefill tiles of 128 stay on k_moe_tc, which
+  // measured as fast there without the permuted dispatch copy
   if (a.nt != kNtSmall) return false;
   if (a.mode != GemmMode::kSwiGLU && a.mode != GemmMode::kRouteWeight) return false;
   if (a.w0.k <= 0 || a.w0.k % kSK != 0 || a.w0.n % 128 != 0) return false;
