@@ -233,6 +233,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
       } else {
         const int64_t mstride = static_cast<int64_t>(src.part_splits) * src.part_rows * src.part_n;
         float g1 = 0.f, g3 = 0.f;
+        // unrolled so that the partial loads of several splits issue together
+#pragma unroll 4
         for (int q = 0; q < src.part_splits; ++q) {
           const int64_t off = (static_cast<int64_t>(q) * src.part_rows + a) * src.part_n + kk;
           g1 += src.part[off];
@@ -257,13 +259,27 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
   const int g0 = k0 / g;
   const int g1 = (min(k0 + max(kspan, 1), K) - 1) / g;
   const int64_t zbase = static_cast<int64_t>(w.zs_strides[e]);
-  for (int i = threadIdx.x; i < (g1 - g0 + 1) * 128; i += blockDim.x) {
-    const int gl = i >> 7, c = i & 127;
-    const int nn = slab * kGemvCols + c;
-    if (nn < N) {
-      const int64_t off = zbase + static_cast<int64_t>(g0 + gl) * N + nn;
-      s_s[i] = __ushort_as_half(__ldg(w.scales + off));
-      s_z[i] = __ushort_as_half(__ldg(w.zeros + off));
+  const int ngr = g1 - g0 + 1;
+  if ((N & 127) == 0 && ((reinterpret_cast<uintptr_t>(w.scales) | reinterpret_cast<uintptr_t>(w.zeros)) & 15) == 0) {
+    // whole slabs: 16-byte loads, scales and zeros in one pass (one load per thread
+    // for up to 8 groups), so their HBM round trips overlap instead of queueing
+    for (int i = threadIdx.x; i < ngr * 32; i += blockDim.x) {
+      const int arr = i / (ngr * 16), j = i - arr * ngr * 16;
+      const int gl = j >> 4, c8 = (j & 15) * 8;
+      const int64_t off = zbase + static_cast<int64_t>(g0 + gl) * N + slab * kGemvCols + c8;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>((arr == 0 ? w.scales : w.zeros) + off));
+      *reinterpret_cast<uint4*>((arr == 0 ? s_s : s_z) + gl * 128 + c8) = v;
+    }
+  } else {
+#pragma unroll 4
+    for (int i = threadIdx.x; i < ngr * 128; i += blockDim.x) {
+      const int gl = i >> 7, c = i & 127;
+      const int nn = slab * kGemvCols + c;
+      if (nn < N) {
+        const int64_t off = zbase + static_cast<int64_t>(g0 + gl) * N + nn;
+        s_s[i] = __ushort_as_half(__ldg(w.scales + off));
+        s_z[i] = __ushort_as_half(__ldg(w.zeros + off));
+      }
     }
   }
   __syncthreads();
@@ -291,6 +307,7 @@ __global__ void k_gemv_reduce(const float* __restrict__ part, int splits, int64_
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (i >= count) return;
   float v = 0.f;
+#pragma unroll 4
   for (int s = 0; s < splits; ++s) v += part[s * count + i];
   out[i] = __float2half_rn(v);
 }
@@ -304,8 +321,10 @@ __global__ void k_decode_combine(const float* __restrict__ part, int splits, int
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float acc = 0.f;
+#pragma unroll 4
   for (int a = 0; a < A; ++a) {
     float v = 0.f;
+#pragma unroll 4
     for (int s = 0; s < splits; ++s) v += part[(static_cast<int64_t>(s) * A + a) * n + i];
     acc = fmaf(__half2float(w[a]), __half2float(__float2half_rn(v)), acc);
   }
