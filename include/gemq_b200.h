@@ -184,6 +184,25 @@ size_t gemq_moe_workspace_size(const gemq_layer_t* layer, int64_t num_tokens, ui
 int gemq_moe_route(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, void* logits, int32_t* topk_idx,
                    uint16_t* topk_w, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same router without a layer handle (the gate and routing options passed
+ * directly): what an expert-parallel rank uses, whose layer holds only its own
+ * experts while routing spans all of them (moe_block.py:790-797, 549-556).
+ * workspace: at least GEMQ_ROUTE_WORKSPACE_BYTES. */
+#define GEMQ_ROUTE_WORKSPACE_BYTES 1024
+int gemq_route(const uint16_t* x, int64_t num_tokens, int32_t hidden, const uint16_t* gate_weight,
+               int32_t num_experts, int32_t top_k, int32_t router, int32_t norm_topk_prob, uint32_t flags,
+               void* logits, int32_t* topk_idx, uint16_t* topk_w, void* workspace, size_t workspace_bytes,
+               void* stream);
+
+/* Combine of forward_n_tokens (moe_block.py:799-812) on already computed expert
+ * outputs: out[t] = sum over the token's k slots of y[slot_row[t*k + j]], in
+ * ascending expert id (topk_idx), every partial sum rounded to fp16 (one fp32 sum
+ * with GEMQ_FWD_FP32_COMBINE), then + residual in fp16 when residual != NULL.
+ * y fp16 [rows, hidden]; slot_row int32 [T*k] (-1 skips the slot). */
+int gemq_moe_combine(const uint16_t* y, const int32_t* slot_row, const int32_t* topk_idx, int64_t num_tokens,
+                     int32_t top_k, int32_t hidden, uint32_t flags, const uint16_t* residual, uint16_t* out,
+                     void* stream);
+
 /* The whole block: replaces QuantFused*MoEBlock.forward -> forward_n_tokens /
  * forward_one_token (moe_block.py:781-858, 234-309, 540-628, 1011-1088).
  *   x fp16 [T, D] -> out fp16 [T, D]

@@ -33,6 +33,7 @@ FWD_FORCE_SIMT = 32
 FWD_RESIDUAL = 64
 FWD_TIME_STAGES = 128
 FWD_SMEM_DEQUANT = 256
+ROUTE_WORKSPACE_BYTES = 1024
 STAGES = ("route", "dispatch", "up", "down", "shared", "combine")
 
 # every symbol include/gemq_b200.h declares
@@ -43,7 +44,7 @@ EXPORTED = [
     "gemq_dequant_gemm",
     "gemq_gemv_workspace_size", "gemq_dequant_gemv", "gemq_fused_up_proj", "gemq_fused_down_proj",
     "gemq_layer_create", "gemq_layer_destroy", "gemq_moe_workspace_size", "gemq_moe_route",
-    "gemq_moe_forward", "gemq_layer_stage_times",
+    "gemq_moe_forward", "gemq_layer_stage_times", "gemq_route", "gemq_moe_combine",
 ]
 
 
@@ -108,6 +109,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "gemq_moe_route": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, u32, vp, sz, vp]),
         "gemq_moe_forward": (ctypes.c_int, [vp, vp, i64, vp, vp, vp, vp, u32, vp, sz, vp]),
         "gemq_layer_stage_times": (ctypes.c_int, [vp, P(ctypes.c_float)]),
+        "gemq_route": (ctypes.c_int, [vp, i64, i32, vp, i32, i32, i32, i32, u32, vp, vp, vp, vp, sz, vp]),
+        "gemq_moe_combine": (ctypes.c_int, [vp, vp, vp, i64, i32, i32, u32, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

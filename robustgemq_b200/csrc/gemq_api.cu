@@ -514,10 +514,10 @@ FwdBufs carve(const gemq_layer_t* L, int64_t T, uint32_t flags, void* base, cons
 }
 
 // logits -> top-k (or nothing when routing is given)
-int run_router(gemq_layer_t* L, const uint16_t* x, int64_t T, void* logits_out, bool logits_given, int32_t* idx,
-               uint16_t* w, uint32_t flags, Seg* one_seg, int32_t* one_tp, cudaStream_t s, StageTimer* tm = nullptr) {
+int run_router(const gemq_layer_desc_t& d, int num_sms, const uint16_t* x, int64_t T, void* logits_out,
+               bool logits_given, int32_t* idx, uint16_t* w, uint32_t flags, Seg* one_seg, int32_t* one_tp,
+               cudaStream_t s, StageTimer* tm = nullptr) {
   if (tm) tm->begin(GEMQ_STAGE_ROUTE);
-  const gemq_layer_desc_t& d = L->d;
   const bool fp32_logits = logits_given || d.router == GEMQ_ROUTER_FP32;
   const bool norm = d.norm_topk_prob != 0;
   const bool fp16_softmax = (flags & GEMQ_FWD_FP16_SOFTMAX) != 0;
@@ -543,7 +543,7 @@ int run_router(gemq_layer_t* L, const uint16_t* x, int64_t T, void* logits_out, 
     a.out = logits_out;
     a.out_ld = d.num_experts;
     a.out_cols = d.num_experts;
-    a.num_sms = L->num_sms;
+    a.num_sms = num_sms;
     a.nt = choose_nt(T);
     const bool tc = !(flags & GEMQ_FWD_FORCE_SIMT) && tc_gemm_supported(a);
     if (tc) {
@@ -707,7 +707,8 @@ int gemq_moe_route(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, v
   Seg* seg = c.take<Seg>(1);
   int32_t* tp = c.take<int32_t>(2);
   if (workspace == nullptr || workspace_bytes < c.off + 256) return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
-  return run_router(layer, x, num_tokens, logits, (flags & GEMQ_FWD_GIVEN_LOGITS) != 0, topk_idx, topk_w, flags, seg,
+  return run_router(layer->d, layer->num_sms, x, num_tokens, logits, (flags & GEMQ_FWD_GIVEN_LOGITS) != 0, topk_idx,
+                    topk_w, flags, seg,
                     tp, static_cast<cudaStream_t>(stream));
 }
 
@@ -739,7 +740,8 @@ int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens,
   const uint16_t* w = topk_w;
   if (!given_routing) {
     void* logits = (router_logits != nullptr) ? router_logits : b.logits;
-    if (int rc = run_router(layer, x, num_tokens, logits, given_logits, b.topk_idx, b.topk_w, flags, b.one_seg,
+    if (int rc = run_router(layer->d, layer->num_sms, x, num_tokens, logits, given_logits, b.topk_idx, b.topk_w,
+                            flags, b.one_seg,
                             b.one_tp, s, &tm))
       return rc;
     idx = b.topk_idx;
@@ -747,6 +749,53 @@ int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens,
   }
   if (one) return forward_one_token(layer, x, out, idx, w, flags, b, s, tm);
   return forward_n_tokens(layer, x, num_tokens, out, idx, w, flags, b, s, tm);
+}
+
+int gemq_route(const uint16_t* x, int64_t num_tokens, int32_t hidden, const uint16_t* gate_weight,
+               int32_t num_experts, int32_t top_k, int32_t router, int32_t norm_topk_prob, uint32_t flags,
+               void* logits, int32_t* topk_idx, uint16_t* topk_w, void* workspace, size_t workspace_bytes,
+               void* stream) {
+  if (num_tokens < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative token count");
+  if (num_tokens == 0) return GEMQ_OK;
+  if (x == nullptr || gate_weight == nullptr || logits == nullptr || topk_idx == nullptr || topk_w == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  if (hidden <= 0 || hidden % 8 != 0) return fail(GEMQ_ERR_UNSUPPORTED, "hidden size must be a positive multiple of 8");
+  if (num_experts <= 0 || num_experts > 256 || top_k <= 0 || top_k > num_experts || top_k > 16)
+    return fail(GEMQ_ERR_UNSUPPORTED, "need 0 < top_k <= min(num_experts, 16), num_experts <= 256");
+  if (router != GEMQ_ROUTER_FP16 && router != GEMQ_ROUTER_FP32)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "unknown router flavour");
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return fail(GEMQ_ERR_UNSUPPORTED, "x must be 16-byte aligned");
+  Carver c(workspace);
+  Seg* seg = c.take<Seg>(1);
+  int32_t* tp = c.take<int32_t>(2);
+  static_assert(GEMQ_ROUTE_WORKSPACE_BYTES >= 256 + 8 + 256, "router workspace constant");
+  if (workspace == nullptr || workspace_bytes < GEMQ_ROUTE_WORKSPACE_BYTES)
+    return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
+  gemq_layer_desc_t d{};
+  d.hidden = hidden;
+  d.num_experts = num_experts;
+  d.top_k = top_k;
+  d.norm_topk_prob = norm_topk_prob;
+  d.router = router;
+  d.gate_weight = gate_weight;
+  return run_router(d, device_sm_count(), x, num_tokens, logits, (flags & GEMQ_FWD_GIVEN_LOGITS) != 0, topk_idx,
+                    topk_w, flags, seg, tp, static_cast<cudaStream_t>(stream));
+}
+
+int gemq_moe_combine(const uint16_t* y, const int32_t* slot_row, const int32_t* topk_idx, int64_t num_tokens,
+                     int32_t top_k, int32_t hidden, uint32_t flags, const uint16_t* residual, uint16_t* out,
+                     void* stream) {
+  if (num_tokens < 0 || top_k <= 0 || top_k > 16) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad token or top_k count");
+  if (num_tokens == 0) return GEMQ_OK;
+  if (y == nullptr || slot_row == nullptr || topk_idx == nullptr || out == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  if (hidden <= 0 || hidden % 8 != 0) return fail(GEMQ_ERR_UNSUPPORTED, "hidden size must be a positive multiple of 8");
+  if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(residual)) & 15u)
+    return fail(GEMQ_ERR_UNSUPPORTED, "y, out and residual must be 16-byte aligned");
+  GEMQ_CUDA(launch_combine(y, slot_row, topk_idx, num_tokens, top_k, hidden, (flags & GEMQ_FWD_FP32_COMBINE) != 0,
+                           nullptr, residual, out, static_cast<cudaStream_t>(stream)),
+            "combine");
+  return GEMQ_OK;
 }
 
 int gemq_layer_stage_times(gemq_layer_t* layer, float* ms_out) {

@@ -1,0 +1,193 @@
+"""Expert parallelism: slot bookkeeping, expert slicing and the all-to-all exchange.
+
+CPU tests run two gloo ranks; the router, the local experts and the combine are the
+oracle's (the exchange, the send order and the slot -> row mapping are the module's
+own), and every rank's output must equal the 1-process oracle block's on its tokens,
+bit for bit. GPU tests run the CUDA defaults: one rank against the block itself,
+and two NCCL ranks when the machine has two GPUs.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, proj_from, rel_l2
+
+F16, F32 = np.float16, np.float32
+
+
+def _golden_block(device="cpu"):
+    from gpu_helpers import family_config
+    from robustgemq_b200.inference import QuantFusedOlmoeMoEBlock
+
+    d = load_golden("block_olmoe.npz")
+    blk = QuantFusedOlmoeMoEBlock(family_config("olmoe", d))
+    blk.gate.weight.data = torch.from_numpy(d["gate_w"]).to(device)
+    for name in ("w1", "w2", "w3"):
+        for f in ("wq", "scales", "zeros", "nbits", "group_sizes", "wq_strides", "zs_strides"):
+            setattr(blk, f"{name}_{f}", torch.from_numpy(np.ascontiguousarray(d[f"{name}_{f}"])).to(device))
+    blk.block_group_size = int(d["group_size"])
+    return blk, d
+
+
+def _oracle_weights(d):
+    from oracle import gemq_oracle as O
+
+    return O.BlockWeights(gate_w=d["gate_w"], w1=proj_from(d, "w1"), w3=proj_from(d, "w3"), w2=proj_from(d, "w2"),
+                          top_k=int(d["top_k"]), norm_topk_prob=bool(d["norm_topk_prob"]))
+
+
+def test_plan_dispatch_orders_slots_by_owner():
+    from robustgemq_b200.inference.expert_parallel import plan_dispatch
+
+    idx = torch.tensor([[5, 0], [2, 7], [3, 4]])
+    order, counts, local = plan_dispatch(idx, experts_per_rank=4, world=2)
+    assert counts.tolist() == [3, 3]
+    assert order.tolist() == [1, 2, 4, 0, 3, 5]  # stable inside each destination
+    assert local.tolist() == [0, 2, 3, 1, 3, 0]
+    with pytest.raises(ValueError):
+        plan_dispatch(torch.tensor([[8]]), experts_per_rank=4, world=2)
+
+
+def test_slice_projection_keeps_each_experts_dequant():
+    from oracle import gemq_oracle as O
+    from robustgemq_b200.inference.expert_parallel import slice_projection
+
+    blk, d = _golden_block()
+    full = proj_from(d, "w2")
+    sl = slice_projection(blk, "w2", 3, 7, int(d["w2_K"]))
+    part = O.PackedProj(wq=sl["wq"].numpy(), scales=sl["scales"].numpy(), zeros=sl["zeros"].numpy(),
+                        nbits=sl["nbits"].numpy(), group_sizes=sl["group_sizes"].numpy(),
+                        wq_strides=sl["wq_strides"].numpy(), zs_strides=sl["zs_strides"].numpy(), K=full.K, N=full.N)
+    for j in range(4):
+        assert np.array_equal(O.dequantize_expert(part, j).view(np.uint16),
+                              O.dequantize_expert(full, 3 + j).view(np.uint16))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cpu_rank(rank, world, port, results):
+    import torch.distributed as dist
+    from oracle import gemq_oracle as O
+    from robustgemq_b200.inference.expert_parallel import ExpertParallelMoE
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        blk, d = _golden_block()
+        ow = _oracle_weights(d)
+        k = ow.top_k
+        ep = None
+
+        def route_fn(x):
+            r = O.route(x.numpy(), ow.gate_w, k, ow.norm_topk_prob)
+            return (torch.from_numpy(r.logits), torch.from_numpy(r.topk_idx.astype(np.int32)),
+                    torch.from_numpy(r.topk_w))
+
+        def experts_fn(rows, ids, wts):
+            rows_np, ids_np, w_np = rows.numpy(), ids.numpy(), wts.numpy()
+            y = np.zeros_like(rows_np)
+            for e in np.unique(ids_np):
+                sel = np.nonzero(ids_np == e)[0]
+                ye = O.expert_ffn_n_tokens(ow, ep.e0 + int(e), rows_np[sel])
+                y[sel] = (ye.astype(F32) * w_np[sel].astype(F32)[:, None]).astype(F16)
+            return torch.from_numpy(y)
+
+        def combine_fn(y, slot_row, idx, residual):
+            y_np, sr, ix = y.numpy(), slot_row.numpy(), idx.numpy()
+            T = ix.shape[0]
+            out = np.zeros((T, y_np.shape[1]), dtype=F16)
+            for t in range(T):
+                for j in np.argsort(ix[t], kind="stable"):
+                    out[t] = (out[t].astype(F32) + y_np[sr[t * k + j]].astype(F32)).astype(F16)
+            return torch.from_numpy(out)
+
+        ep = ExpertParallelMoE(blk, route_fn=route_fn, experts_fn=experts_fn, combine_fn=combine_fn)
+        x = d["x"].astype(F16)
+        mine = x[rank::world]
+        out, _ = ep.forward_tokens(torch.from_numpy(np.ascontiguousarray(mine)))
+        ref, _ = O.moe_forward_n_tokens(ow, mine)
+        results[rank] = bool(np.array_equal(out.numpy().view(np.uint16), ref.view(np.uint16)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_two_gloo_ranks_match_the_single_block():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_cpu_rank, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(results) == {0: True, 1: True}
+
+
+@pytest.mark.gpu
+def test_expert_parallel_one_rank_matches_block_on_gpu():
+    from robustgemq_b200 import _lib
+    from robustgemq_b200.inference.expert_parallel import ExpertParallelMoE
+
+    blk, d = _golden_block("cuda")
+    x = torch.from_numpy(d["x"].astype(F16)).cuda()
+    ref, ref_logits = blk.forward_n_tokens(x.unsqueeze(0))
+    ep = ExpertParallelMoE(blk)
+    out, logits = ep.forward_tokens(x)
+    torch.cuda.synchronize()
+    assert rel_l2(out.cpu().numpy(), ref[0].cpu().numpy()) < 1e-3
+    assert torch.equal(out, ref[0])  # same kernels per row, same combine order
+    assert torch.equal(logits, ref_logits)
+    assert _lib.device_error() == 0
+
+
+def _nccl_rank(rank, world, port, results):
+    import torch.distributed as dist
+    from robustgemq_b200.inference.expert_parallel import ExpertParallelMoE
+
+    torch.cuda.set_device(rank)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        blk, d = _golden_block(f"cuda:{rank}")
+        x = torch.from_numpy(d["x"].astype(F16)).cuda(rank)
+        ref, _ = blk.forward_n_tokens(x.unsqueeze(0))
+        ep = ExpertParallelMoE(blk)
+        mine = x[rank::world].contiguous()
+        out, _ = ep.forward_tokens(mine)
+        torch.cuda.synchronize()
+        results[rank] = rel_l2(out.cpu().numpy(), ref[0][rank::world].cpu().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_expert_parallel_two_nccl_ranks_match_the_single_block():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert all(results[r] < 1e-3 for r in range(2)), dict(results)
