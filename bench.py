@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--prefill-layers", type=int, default=48)
     ap.add_argument("--prefill-tokens", type=int, default=4096)
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--ep-layers", type=int, default=2)
+    ap.add_argument("--ep-tokens", type=int, default=8192)
+    ap.add_argument("--no-ep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     return ap.parse_args()
@@ -294,6 +297,9 @@ def run_ours(args, rank, world, local_rank):
     prefill = None
     if not args.no_prefill:
         prefill = run_prefill(args, device, bf16_peak, bf16_sus)
+    ep = None
+    if not args.no_ep:
+        ep = run_ep(args, rank, world, device, bf16_sus)
     cpu = None
     if rank == 0 and not args.no_cpu:
         cpu = cpu_baseline(blocks[0], inputs, args.cpu_seconds)
@@ -329,6 +335,8 @@ def run_ours(args, rank, world, local_rank):
     }
     if prefill:
         line["prefill"] = prefill
+    if ep:
+        line["expert_parallel"] = ep
     if cpu:
         line["cpu_baseline"] = cpu
     return line
@@ -408,6 +416,56 @@ def run_prefill(args, device, bf16_peak, bf16_sus):
             "stage_ms_layer0": [round(v, 4) for v in st],
             "up_tflops": round(up_flops / (st[2] * 1e-3) / 1e12, 1) if st[2] > 0 else None,
             "down_tflops": round(dn_flops / (st[3] * 1e-3) / 1e12, 1) if st[3] > 0 else None}
+
+
+def run_ep(args, rank, world, device, bf16_sus):
+    """Mixtral-shaped prefill with expert parallelism over all ranks:
+    each rank owns E / world experts and its own ``ep_tokens`` tokens (weak scaling);
+    tokens reach their experts' ranks and return by NCCL all-to-all."""
+    import torch
+    import torch.distributed as dist
+
+    from robustgemq_b200 import synth
+    from robustgemq_b200.inference import QuantFusedMixtralMoEBlock
+    from robustgemq_b200.inference.expert_parallel import ExpertParallelMoE
+
+    cfg, shp = synth.mixtral_config()
+    L, T = args.ep_layers, args.ep_tokens
+    layers = []
+    for l in range(L):
+        blk = synth.random_block(QuantFusedMixtralMoEBlock, cfg, shp["hidden"], shp["inter"], shp["num_experts"],
+                                 shp["mean_bits"], shp["group_size"], 7000 + l, device)
+        layers.append(ExpertParallelMoE(blk))
+    gen = torch.Generator(device=device).manual_seed(900 + rank)
+    x = torch.randn((T, shp["hidden"]), generator=gen, device=device).half()
+
+    def fwd():
+        for ep in layers:  # every layer reads the same input; outputs are discarded
+            ep.forward_tokens(x)
+
+    for _ in range(2):
+        fwd()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    reps = 3
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fwd()
+    e.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([s.elapsed_time(e) / reps], device=device)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    D, F, k = shp["hidden"], shp["inter"], cfg.num_experts_per_tok
+    flops = world * T * L * k * 6 * D * F
+    return {"workload": f"mixtral-8x7b-shaped prefill, {L} layers, {T} tokens per rank, experts sharded over "
+                        f"{world} rank(s), NCCL all-to-all dispatch/combine (config 4)",
+            "layers": L, "tokens_per_rank": T, "n_ranks": world, "ms_per_pass": round(ms, 3),
+            "tokens_per_s": round(world * T / (ms * 1e-3), 1), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+            "frac_bf16_peak_per_gpu": round(flops / world / (ms * 1e-3) / 1e12 / bf16_sus, 3)}
 
 
 # ----------------------------------------------------------------------------- CPU baseline
