@@ -77,9 +77,17 @@ class Clocks:
             self.path.parent.mkdir(exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                          "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        # the timed region starts only once the sampler is producing rows
+        deadline = time.time() + 5.0
+        while time.time() < deadline:
+            self.f.flush()
+            if self.path.exists() and self.path.stat().st_size > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self, gpus):
         if self.proc is None:
@@ -224,11 +232,11 @@ def run_ours(args, rank, world, local_rank):
         per_b[B] = s.elapsed_time(e) / reps
 
     clocks = Clocks() if rank == 0 else None
+    if clocks:
+        clocks.start()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    if clocks:
-        clocks.start()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for i in range(args.steps):

@@ -13,18 +13,19 @@
 //     the A tile is one shift + one mask of a packed word, then the exact
 //     fma.rn.f16 dequant (utils.py:206-210);
 //   * scale / zero rows are fetched 16 groups at a time into their own ring, and
-//     the per-stage copies are issued by two producer warps (a single thread issues
-//     one bulk tensor copy every ~100+ cycles).
+//     the per-stage copies are issued by two producer warps (one issuing lane
+//     sustains roughly one bulk tensor copy per 100+ cycles);
+//   * the down projection (route-weight mode) pairs two 128-feature tiles of the
+//     same expert in one work item, as the two "matrices" of the gate/up item.
 //
-// Warps (512 threads, one CTA per SM, grid-stride over work items):
+// Warps (768 threads, one CTA per SM, grid-stride over work items):
 //   0      producer: activation sub-tile 0 (k0..k0+63) and packed words of matrix 0
-//   1      TMEM allocation, single-thread tcgen05.mma issue and commits
+//   1      TMEM allocation; MMA issue and commits from an elected lane
 //   2      producer: activation sub-tile 1 (k0+64..k0+127) and words of matrix 1
 //   3      producer: scale / zero chunks
 //   4-7    epilogue: tcgen05.ld -> rounding -> global stores (lane quarter = warp % 4)
-//   8-15   dequant: warp w owns features 32*(w%4) .. +31 (its TMEM lane quarter);
-//          two matrices: warps 8-11 matrix 0, 12-15 matrix 1, all 128 k of a stage;
-//          one matrix: warps 8-11 k 0..63, 12-15 k 64..127
+//   8-23   dequant: 16 warps = (K half, matrix) x lane quarter; warp w owns features
+//          32*(w%4) .. +31 (its TMEM lane quarter) of matrix ((w-8)/4)%2, k half (w-8)/8
 // Every wait is bounded (gemq_common.cuh); on expiry all roles drain and return.
 #include <cudaTypedefs.h>
 
