@@ -340,7 +340,7 @@ int gemq_fused_up_proj(const gemq_proj_t* w1, const gemq_proj_t* w3, const uint1
   if (workspace == nullptr || workspace_bytes < gemq_gemv_workspace_size(w1, num_idx))
     return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int splits = gemv_default_splits(w1->k, w1->n, num_idx, device_sm_count());
+  const int splits = gemv_default_splits(w1->k, w1->n, num_idx, device_sm_count(), 2);
   Carver c(workspace);
   float* p1 = c.take<float>(2ull * splits * num_idx * w1->n);  // [w1, w3][split][a][n]
   float* p3 = p1 + static_cast<size_t>(splits) * num_idx * w1->n;
@@ -484,12 +484,12 @@ FwdBufs carve(const gemq_layer_t* L, int64_t T, uint32_t flags, void* base, cons
   b.one_seg = c.take<Seg>(1);
   b.one_tp = c.take<int32_t>(2);
   if (flags & GEMQ_FWD_ONE_TOKEN) {
-    b.splits_up = gemv_default_splits(D, F, k, L->num_sms);
+    b.splits_up = gemv_default_splits(D, F, k, L->num_sms, 2);
     b.splits_dn = gemv_default_splits(F, D, k, L->num_sms);
     b.part_up = c.take<float>(2ull * b.splits_up * k * F);  // [w1, w3][split][a][F]
     b.part_dn = c.take<float>(static_cast<size_t>(b.splits_dn) * k * D);
     if (d.has_shared) {
-      b.splits_s = gemv_default_splits(D, Fs, 1, L->num_sms);
+      b.splits_s = gemv_default_splits(D, Fs, 1, L->num_sms, 2);
       b.splits_s2 = gemv_default_splits(Fs, D, 1, L->num_sms);
       b.part_s = c.take<float>(2ull * b.splits_s * Fs);
       b.part_s2 = c.take<float>(static_cast<size_t>(b.splits_s2) * D);

@@ -72,9 +72,10 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) { mbar_arrive(smem_u32(bar)); }
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
@@ -116,8 +117,7 @@ constexpr uint32_t kPollSleepNs = 100000;
 // between polls. The abort word and the time bound are checked every 16 polls.
 // Returns false (recording `code`) if the wait exceeds kWaitLimitNs, or once another
 // wait expired (so a failed pipeline drains instead of spinning).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code, uint32_t sleep_ns = 0) {
-  const uint32_t a = smem_u32(bar);
+__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, uint32_t code, uint32_t sleep_ns = 0) {
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t polls = 1;; ++polls) {
@@ -133,11 +133,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   }
 }
 
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code, uint32_t sleep_ns = 0) {
+  return mbar_wait(smem_u32(bar), parity, code, sleep_ns);
+}
+
 // Bounded wait by every lane of a converged warp; the lanes agree on the outcome so
-// the warp stays converged on every path.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t code, uint32_t sleep_ns = 0) {
+// the warp stays converged on every path. `bar` is a shared-memory address.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint32_t code, uint32_t sleep_ns = 0) {
   const bool ok = mbar_wait(bar, parity, code, sleep_ns);
   return __all_sync(0xffffffffu, ok);
+}
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t code, uint32_t sleep_ns = 0) {
+  return warp_wait(smem_u32(bar), parity, code, sleep_ns);
+}
+
+// Completes a wait whose first try_wait (`tok`) was issued earlier, so that its
+// latency overlapped other work; polls only if that try found the phase open.
+__device__ __forceinline__ bool warp_wait_tok(uint32_t bar, uint32_t parity, bool tok, uint32_t code,
+                                              uint32_t sleep_ns = 0) {
+  if (__all_sync(0xffffffffu, tok)) return true;
+  return warp_wait(bar, parity, code, sleep_ns);
 }
 
 // Waits for copies still in flight before a CTA exits: bounded by time only, so it

@@ -110,7 +110,9 @@ struct GemvSrc {
   const float* part;    // kGemvPart*: up partials [2][part_splits][part_rows][part_n]
   int part_splits, part_rows, part_n;
 };
-int gemv_default_splits(int k, int n, int rows_a, int num_sms);
+// Split-K factor of a GEMV over rows_a rows and nmat matrices. Fewer matrices never
+// give fewer splits, so a workspace sized with nmat = 1 also fits nmat = 2.
+int gemv_default_splits(int k, int n, int rows_a, int num_sms, int nmat = 1);
 // part[mat][s][a][n] for mat in {w0, w1 (optional)}
 cudaError_t launch_gemv(const ProjDev& w0, const ProjDev* w1, const int32_t* idx, int rows_a, const GemvSrc& src,
                         float* part, int splits, cudaStream_t s);

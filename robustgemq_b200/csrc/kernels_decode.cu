@@ -54,10 +54,48 @@ __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, 
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
-// Accumulates one word (codes j = 0..eps-1 at k0 + j) of one feature column.
-// Pair p holds codes (p, p + eps/2): 16 bits apart, so one shift + mask per pair.
+// x values of one word row (codes j = 0..eps-1 at k0 + j), read from shared memory
+// with 16-byte loads (pow2 widths: a row starts on a multiple of eps elements, so on
+// a 16-byte boundary) or 4-byte loads (3-bit: ten fp16 / fp32 values at 20 / 40-byte
+// offsets).
 template <int NB, bool XF16>
-__device__ __forceinline__ void word_pow2(uint32_t w, __half2 s2, __half2 z2, const void* xr, float& acc0,
+struct XRow {
+  static constexpr int kN = (NB == 3) ? 10 : 32 / NB;
+  static constexpr int kBytes = kN * (XF16 ? 2 : 4);
+  static constexpr int kVec = (NB == 3) ? 4 : 16;  // load width in bytes
+  uint32_t v[kBytes / 4];
+  __device__ __forceinline__ void load(const void* xr) {
+    if constexpr (kVec == 16) {
+#pragma unroll
+      for (int i = 0; i < kBytes / 16; ++i) {
+        const uint4 t = static_cast<const uint4*>(xr)[i];
+        v[4 * i] = t.x;
+        v[4 * i + 1] = t.y;
+        v[4 * i + 2] = t.z;
+        v[4 * i + 3] = t.w;
+      }
+    } else if constexpr (XF16) {
+#pragma unroll
+      for (int i = 0; i < kBytes / 4; ++i) v[i] = static_cast<const uint32_t*>(xr)[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < kBytes / 8; ++i) {
+        const uint2 t = static_cast<const uint2*>(xr)[i];
+        v[2 * i] = t.x;
+        v[2 * i + 1] = t.y;
+      }
+    }
+  }
+  __device__ __forceinline__ __half h(int j) const {
+    return __ushort_as_half(static_cast<unsigned short>(v[j >> 1] >> (16 * (j & 1))));
+  }
+  __device__ __forceinline__ float f(int j) const { return __uint_as_float(v[j]); }
+};
+
+// Accumulates one word of one feature column. Pair p holds codes (p, p + eps/2):
+// 16 bits apart, so one shift + mask per pair.
+template <int NB, bool XF16>
+__device__ __forceinline__ void word_pow2(uint32_t w, __half2 s2, __half2 z2, const XRow<NB, XF16>& x, float& acc0,
                                           float& acc1) {
   constexpr int kEps = 32 / NB, kHalf = kEps / 2;
   constexpr uint32_t kMask = ((1u << NB) - 1u) * 0x00010001u;
@@ -65,13 +103,11 @@ __device__ __forceinline__ void word_pow2(uint32_t w, __half2 s2, __half2 z2, co
   for (int j = 0; j < kHalf; ++j) {
     const __half2 wq = u32_as_h2(dq_pair(((w >> (NB * j)) & kMask) | 0x64006400u, s2, z2));
     if constexpr (XF16) {
-      const __half* x = static_cast<const __half*>(xr);
-      acc0 = fma_f32_f16(__low2half(wq), x[j], acc0);
-      acc1 = fma_f32_f16(__high2half(wq), x[j + kHalf], acc1);
+      acc0 = fma_f32_f16(__low2half(wq), x.h(j), acc0);
+      acc1 = fma_f32_f16(__high2half(wq), x.h(j + kHalf), acc1);
     } else {
-      const float* x = static_cast<const float*>(xr);
       const float2 wf = __half22float2(wq);
-      ffma2(acc0, acc1, x[j], x[j + kHalf], wf.x, wf.y);
+      ffma2(acc0, acc1, x.f(j), x.f(j + kHalf), wf.x, wf.y);
     }
   }
 }
@@ -81,7 +117,7 @@ __device__ __forceinline__ void word_pow2(uint32_t w, __half2 s2, __half2 z2, co
 // j >= b the next group's (sb, zb) (b = 10 when the word lies in one group).
 template <bool XF16>
 __device__ __forceinline__ void word_3bit(uint32_t w, __half sa, __half za, __half sb, __half zb, int b,
-                                          const void* xr, float& acc0, float& acc1) {
+                                          const XRow<3, XF16>& x, float& acc0, float& acc1) {
 #pragma unroll
   for (int j = 0; j < 5; ++j) {
     const uint32_t t = w >> (3 * j);        // code j at bits 0..2
@@ -91,13 +127,11 @@ __device__ __forceinline__ void word_3bit(uint32_t w, __half sa, __half za, __ha
     const __half2 z2 = __halves2half2(j >= b ? zb : za, j + 5 >= b ? zb : za);
     const __half2 wq = u32_as_h2(dq_pair(m, s2, z2));
     if constexpr (XF16) {
-      const __half* x = static_cast<const __half*>(xr);
-      acc0 = fma_f32_f16(__low2half(wq), x[j], acc0);
-      acc1 = fma_f32_f16(__high2half(wq), x[j + 5], acc1);
+      acc0 = fma_f32_f16(__low2half(wq), x.h(j), acc0);
+      acc1 = fma_f32_f16(__high2half(wq), x.h(j + 5), acc1);
     } else {
-      const float* x = static_cast<const float*>(xr);
       const float2 wf = __half22float2(wq);
-      ffma2(acc0, acc1, x[j], x[j + 5], wf.x, wf.y);
+      ffma2(acc0, acc1, x.f(j), x.f(j + 5), wf.x, wf.y);
     }
   }
 }
@@ -110,11 +144,34 @@ struct GroupStage {
   int g0;  // first staged group
 };
 
+constexpr int kBatch = 8;  // word rows of a warp whose loads are in flight together
+
+// Loads word rows [rb, min(rb + kBatch, wr1)) of features n..n+3.
+__device__ __forceinline__ void load_words(const int32_t* wbase, int N, int n, int rb, int wr1, uint4 (&wv)[kBatch]) {
+#pragma unroll
+  for (int i = 0; i < kBatch; ++i)
+    wv[i] = (rb + i < wr1) ? __ldg(reinterpret_cast<const uint4*>(wbase + static_cast<int64_t>(rb + i) * N + n))
+                           : make_uint4(0, 0, 0, 0);
+}
+
+// One word row of the four feature columns of a lane.
+template <int NB, bool XF16>
+__device__ __forceinline__ void row_pow2(const uint4& wv, const void* xr, const __half2 (&s_c)[4],
+                                         const __half2 (&z_c)[4], float (&acc)[4][2]) {
+  XRow<NB, XF16> x;
+  x.load(xr);
+  const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) word_pow2<NB, XF16>(words[c], s_c[c], z_c[c], x, acc[c][0], acc[c][1]);
+}
+
+// Accumulates word rows [wr0, wr1) of a warp; `wv` holds the first batch, loaded by
+// the caller before it staged x and the scales. The next batch's loads are issued
+// before the current one is used.
 template <bool XF16>
-__device__ __forceinline__ void gemv_rows(const ProjDev& w, int e, int nb, int lane, int n, int wr0, int wr1, int k0,
-                                          const void* s_x, const GroupStage& gs, float (&acc)[4][2]) {
-  const int K = w.k, N = w.n, g = w.group_size;
-  const int32_t* wbase = w.wq + static_cast<int64_t>(w.wq_strides[e]);
+__device__ __forceinline__ void gemv_rows(const int32_t* wbase, int K, int N, int g, int nb, int lane, int n, int wr0,
+                                          int wr1, int k0, const void* s_x, const GroupStage& gs, uint4 (&wv)[kBatch],
+                                          float (&acc)[4][2]) {
   const int eps = 32 / nb;
   int cur_g = -1;
   __half2 s_c[4], z_c[4];  // scale / zero of the current group, per column
@@ -131,19 +188,15 @@ __device__ __forceinline__ void gemv_rows(const ProjDev& w, int e, int nb, int l
     }
   };
   constexpr int kXBytes = XF16 ? 2 : 4;
-  constexpr int kBatch = 8;  // word rows whose loads are issued before any is used
   const char* xbase = static_cast<const char*>(s_x);
   for (int rb = wr0; rb < wr1; rb += kBatch) {
-    uint4 wv[kBatch];
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i)
-      wv[i] = (rb + i < wr1) ? __ldg(reinterpret_cast<const uint4*>(wbase + static_cast<int64_t>(rb + i) * N + n))
-                             : make_uint4(0, 0, 0, 0);
+    uint4 nx[kBatch];
+    const bool more = rb + kBatch < wr1;
+    if (more) load_words(wbase, N, n, rb + kBatch, wr1, nx);
 #pragma unroll
     for (int i = 0; i < kBatch; ++i) {
       const int r = rb + i;
       if (r >= wr1) break;
-      const uint32_t words[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
       const int kr = r * eps;
       const int ga = kr / g;
       if (ga != cur_g) {
@@ -152,12 +205,15 @@ __device__ __forceinline__ void gemv_rows(const ProjDev& w, int e, int nb, int l
       }
       const void* xr = xbase + static_cast<size_t>(kr - k0) * kXBytes;
       if (nb == 3) {
+        XRow<3, XF16> x;
+        x.load(xr);
+        const uint32_t words[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
         const int gb = min(kr + 9, K - 1) / g;
         if (gb == ga) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_c[c]), __low2half(z_c[c]),
-                            10, xr, acc[c][0], acc[c][1]);
+                            10, x, acc[c][0], acc[c][1]);
         } else {
           // codes at k >= gb * g use the next group's scale and zero
           __half2 s_n[4], z_n[4];
@@ -166,7 +222,7 @@ __device__ __forceinline__ void gemv_rows(const ProjDev& w, int e, int nb, int l
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_n[c]), __low2half(z_n[c]),
-                            b, xr, acc[c][0], acc[c][1]);
+                            b, x, acc[c][0], acc[c][1]);
           cur_g = gb;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -176,15 +232,16 @@ __device__ __forceinline__ void gemv_rows(const ProjDev& w, int e, int nb, int l
         }
         // codes past K in a ragged last word are zero-padded and their x staged as 0
       } else if (nb == 2) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) word_pow2<2, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
+        row_pow2<2, XF16>(wv[i], xr, s_c, z_c, acc);
       } else if (nb == 4) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) word_pow2<4, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
+        row_pow2<4, XF16>(wv[i], xr, s_c, z_c, acc);
       } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) word_pow2<1, XF16>(words[c], s_c[c], z_c[c], xr, acc[c][0], acc[c][1]);
+        row_pow2<1, XF16>(wv[i], xr, s_c, z_c, acc);
       }
+    }
+    if (more) {
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) wv[i] = nx[i];
     }
   }
 }
@@ -221,6 +278,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
   const int r1 = static_cast<int>((static_cast<int64_t>(rows) * (s + 1)) / splits);
   const int k0 = r0 * eps;
   const int kspan = (r1 - r0) * eps;  // padded to whole words; entries past K are 0
+  // this warp's word rows; their first loads go out before x and the scales are
+  // staged, so the three HBM round trips overlap
+  const int n = slab * kGemvCols + lane * 4;
+  const int per = (r1 - r0 + 7) / 8;
+  const int wr0 = r0 + warp * per, wr1 = min(r1, wr0 + per);
+  const int32_t* wbase = w.wq + static_cast<int64_t>(w.wq_strides[e]);
+  uint4 wv[kBatch];
+  if (n < N) load_words(wbase, N, n, wr0, wr1, wv);
   // stage x
   for (int i = threadIdx.x; i < kspan; i += blockDim.x) {
     const int kk = k0 + i;
@@ -283,12 +348,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
     }
   }
   __syncthreads();
-  const int n = slab * kGemvCols + lane * 4;
   float acc[4][2] = {};
-  const int per = (r1 - r0 + 7) / 8;
-  const int wr0 = r0 + warp * per, wr1 = min(r1, wr0 + per);
   const GroupStage gs{s_s, s_z, g0};
-  if (n < N) gemv_rows<XF16>(w, e, nb, lane, n, wr0, wr1, k0, s_raw, gs, acc);
+  if (n < N) gemv_rows<XF16>(wbase, K, N, g, nb, lane, n, wr0, wr1, k0, s_raw, gs, wv, acc);
 #pragma unroll
   for (int c = 0; c < 4; ++c) s_red[warp][lane * 4 + c] = acc[c][0] + acc[c][1];
   __syncthreads();
@@ -360,10 +422,13 @@ cudaError_t launch_gemv_t(const ProjDev& w0, const ProjDev* w1, const int32_t* i
 
 }  // namespace
 
-int gemv_default_splits(int k, int n, int rows_a, int num_sms) {
-  const int ctas = ((n + kGemvCols - 1) / kGemvCols) * rows_a;
+int gemv_default_splits(int k, int n, int rows_a, int num_sms, int nmat) {
+  // the largest power-of-two split that keeps the grid within one wave of two CTAs
+  // per SM (each CTA issues all its word loads early; a second wave would pay the
+  // HBM latency again), with at least 256 k per split
+  const int ctas = ((n + kGemvCols - 1) / kGemvCols) * rows_a * nmat;
   int s = 1;
-  while (ctas * s < 2 * num_sms && s < 16 && (k / (s * 2)) >= 256) s *= 2;
+  while (ctas * s * 2 <= 2 * num_sms && s < 16 && (k / (s * 2)) >= 256) s *= 2;
   return s;
 }
 

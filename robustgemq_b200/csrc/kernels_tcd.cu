@@ -165,12 +165,14 @@ __device__ __forceinline__ void dq_cols(const uint32_t (&w)[kMaxWordRows], const
 }
 
 // Dequantises columns [C0, C0 + NC) of a stage and stores them to TMEM at `taddr`.
+// Stored 16 columns at a time, so that only 16 results are live at once.
 template <int NB, int PH, bool G2, int C0, int NC>
 __device__ __forceinline__ void dq_store(const uint32_t (&w)[kMaxWordRows], const ScaleSet& sc, uint32_t taddr) {
-  uint32_t o[NC];
-  dq_cols<NB, PH, G2, C0, NC>(w, sc, o, std::make_integer_sequence<int, NC>{});
-  if constexpr (NC == 32) tmem_st32(taddr, o);
-  else tmem_st16(taddr, o);
+  static_assert(NC % 16 == 0, "columns are stored 16 at a time");
+  uint32_t o[16];
+  dq_cols<NB, PH, G2, C0, 16>(w, sc, o, std::make_integer_sequence<int, 16>{});
+  tmem_st16(taddr, o);
+  if constexpr (NC > 16) dq_store<NB, PH, G2, C0 + 16, NC - 16>(w, sc, taddr + 16u);
 }
 
 // Ring positions and barriers a dequant warp walks through; advanced in place.
@@ -179,89 +181,127 @@ struct DqRings {
   uint32_t ph, aph, cph;
 };
 
+// Shared addresses of the kernel's mbarriers, in array order: full[kStages],
+// empty[kStages], sfull[2], sempty[2], afull[kAStages], aempty[kAStages].
+template <class C>
+struct BarsD {
+  static __device__ __forceinline__ uint32_t full(uint32_t b, int s) { return b + 8u * s; }
+  static __device__ __forceinline__ uint32_t empty(uint32_t b, int s) { return b + 8u * (C::kStages + s); }
+  static __device__ __forceinline__ uint32_t sfull(uint32_t b, int c) { return b + 8u * (2 * C::kStages + c); }
+  static __device__ __forceinline__ uint32_t sempty(uint32_t b, int c) { return b + 8u * (2 * C::kStages + 2 + c); }
+  static __device__ __forceinline__ uint32_t afull(uint32_t b, int a) { return b + 8u * (2 * C::kStages + 4 + a); }
+  static __device__ __forceinline__ uint32_t aempty(uint32_t b, int a) {
+    return b + 8u * (2 * C::kStages + 4 + C::kAStages + a);
+  }
+};
+
 // Everything a dequant warp needs for one work item besides its rings.
 struct DqEnv {
   uint8_t* stages;         // stage ring base (shared memory)
   const uint8_t* chunks;   // scale / zero chunk ring base
-  uint64_t *full, *empty, *sfull, *sempty, *afull, *aempty;
+  uint32_t bars;           // shared address of the barrier array (layout: BarsD)
   uint32_t a_col0;         // TMEM address of this warp's lane quarter, A ring column 0
   uint32_t n;              // feature row inside the tile (= TMEM lane)
   int lane, mat, KT, log2g;
 };
 
+// Packed words and scale / zero of one stage and feature row, held in registers.
+struct DqStage {
+  uint32_t w[kMaxWordRows];
+  __half sa, za, sb, zb;
+};
+
+// Reads stage kt (ring slot r.s) of a dequant warp's feature row into `d` and
+// releases the slot; `tok` is the result of an earlier try_wait on its full barrier.
+// `ch` is the scale chunk in use (-1 before the item's first stage).
+template <class C, int NB, bool G2>
+__device__ __forceinline__ bool dq_fetch(int kt, DqStage& d, bool tok, int& ch, DqRings& r, const DqEnv& e) {
+  constexpr int kRows = kperm::stage_word_rows(NB);
+  using Bar = BarsD<C>;
+  const int gl = (kt * kSK) >> e.log2g;  // first scale group of the stage
+  const int chn = gl / kScRows;
+  if (chn != ch) {
+    if (ch >= 0) {
+      __syncwarp();
+      if (e.lane == 0) mbar_arrive(Bar::sempty(e.bars, r.c));
+      if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
+    }
+    if (!warp_wait(Bar::sfull(e.bars, r.c), r.cph, kDevTimeoutTmaFull, kBusySleepNs)) return false;
+    ch = chn;
+  }
+  if (!warp_wait_tok(Bar::full(e.bars, r.s), r.ph, tok, kDevTimeoutTmaFull, kBusySleepNs)) return false;
+  const uint32_t* wcol =
+      reinterpret_cast<const uint32_t*>(e.stages + r.s * C::kStageBytes + C::kActBytes + e.mat * C::kWordBytes) + e.n;
+#pragma unroll
+  for (int i = 0; i < kMaxWordRows; ++i) d.w[i] = (i < kRows) ? wcol[i * 128] : 0u;
+  const __half* sp = reinterpret_cast<const __half*>(e.chunks + r.c * C::kChunkBytes + (2 * e.mat) * C::kScBytes) + e.n;
+  const __half* zp = sp + C::kScBytes / 2;
+  const int r0 = (gl - ch * kScRows) * 128;
+  d.sa = sp[r0];
+  d.za = zp[r0];
+  d.sb = d.sa;
+  d.zb = d.za;
+  if constexpr (G2) {
+    d.sb = sp[r0 + 128];
+    d.zb = zp[r0 + 128];
+  }
+  __syncwarp();
+  if (e.lane == 0) mbar_arrive(Bar::empty(e.bars, r.s));
+  if (++r.s == C::kStages) { r.s = 0; r.ph ^= 1u; }
+  return true;
+}
+
 // One work item of one dequant warp, specialised by bit-width, group layout and the
 // warp's columns [C0, C0 + NC) of its matrix: per stage, read the packed words and
-// scale / zero of its feature row, release the stage, dequantise into TMEM, and
-// release the A stage to the MMA. Scale group, chunk and 3-bit phase advance
-// incrementally. Returns false if a wait expired.
+// scale / zero of its feature row, release the stage, dequantise into TMEM and hand
+// the A stage to the MMA. The first polls of the next stage's two waits are issued
+// while this stage's TMEM stores are in flight, so their latencies overlap. Scale
+// group, chunk and 3-bit phase advance incrementally. Returns false if a wait expired.
 template <class C, int NB, bool G2, int C0, int NC>
 __device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
-  constexpr int kRows = kperm::stage_word_rows(NB);
+  using Bar = BarsD<C>;
   int ch = -1;
   int ph3 = 0;  // 3-bit phase index: P = (128 kt) % 10 = 0, 8, 6, 4, 2 -> index 0, 4, 3, 2, 1
+  bool tok_f = mbar_try_wait(Bar::full(e.bars, r.s), r.ph);
+  bool tok_a = mbar_try_wait(Bar::aempty(e.bars, r.as), r.aph ^ 1u);
   for (int kt = 0; kt < e.KT; ++kt) {
-    const int gl = (kt * kSK) >> e.log2g;  // first scale group of the stage
-    const int chn = gl / kScRows;
-    if (chn != ch) {
-      if (ch >= 0) {
-        __syncwarp();
-        if (e.lane == 0) mbar_arrive(&e.sempty[r.c]);
-        if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
-      }
-      if (!warp_wait(&e.sfull[r.c], r.cph, kDevTimeoutTmaFull, kBusySleepNs)) return false;
-      ch = chn;
-    }
-    if (!warp_wait(&e.full[r.s], r.ph, kDevTimeoutTmaFull, kBusySleepNs)) return false;
-    const uint32_t* wcol = reinterpret_cast<const uint32_t*>(e.stages + r.s * C::kStageBytes + C::kActBytes +
-                                                             e.mat * C::kWordBytes) +
-                           e.n;
-    uint32_t wv[kMaxWordRows];
-#pragma unroll
-    for (int i = 0; i < kMaxWordRows; ++i) wv[i] = (i < kRows) ? wcol[i * 128] : 0u;
-    const __half* sp =
-        reinterpret_cast<const __half*>(e.chunks + r.c * C::kChunkBytes + (2 * e.mat) * C::kScBytes) + e.n;
-    const __half* zp = sp + C::kScBytes / 2;
-    const int r0 = (gl - ch * kScRows) * 128;
-    const __half sa = sp[r0], za = zp[r0];
-    __half sb = sa, zb = za;
-    if constexpr (G2) {
-      sb = sp[r0 + 128];
-      zb = zp[r0 + 128];
-    }
-    __syncwarp();
-    if (e.lane == 0) mbar_arrive(&e.empty[r.s]);
-    if (!warp_wait(&e.aempty[r.as], r.aph ^ 1u, kDevTimeoutAEmpty, kBusySleepNs)) return false;
+    DqStage cur;
+    if (!dq_fetch<C, NB, G2>(kt, cur, tok_f, ch, r, e)) return false;
+    if (!warp_wait_tok(Bar::aempty(e.bars, r.as), r.aph ^ 1u, tok_a, kDevTimeoutAEmpty, kBusySleepNs)) return false;
     tc_fence_after();
     ScaleSet sc;
-    sc.s0 = __halves2half2(sa, sa);
-    sc.z0 = __halves2half2(za, za);
-    sc.s1 = __halves2half2(sb, sb);
-    sc.z1 = __halves2half2(zb, zb);
-    sc.s01 = __halves2half2(sa, sb);
-    sc.z01 = __halves2half2(za, zb);
+    sc.s0 = __halves2half2(cur.sa, cur.sa);
+    sc.z0 = __halves2half2(cur.za, cur.za);
+    sc.s1 = __halves2half2(cur.sb, cur.sb);
+    sc.z1 = __halves2half2(cur.zb, cur.zb);
+    sc.s01 = __halves2half2(cur.sa, cur.sb);
+    sc.z01 = __halves2half2(cur.za, cur.zb);
     const uint32_t taddr = e.a_col0 + static_cast<uint32_t>(r.as * C::kACols + e.mat * 64 + C0);
     if constexpr (NB == 3) {
       switch (ph3) {
-        case 0: dq_store<3, 0, G2, C0, NC>(wv, sc, taddr); break;
-        case 1: dq_store<3, 1, G2, C0, NC>(wv, sc, taddr); break;
-        case 2: dq_store<3, 2, G2, C0, NC>(wv, sc, taddr); break;
-        case 3: dq_store<3, 3, G2, C0, NC>(wv, sc, taddr); break;
-        default: dq_store<3, 4, G2, C0, NC>(wv, sc, taddr); break;
+        case 0: dq_store<3, 0, G2, C0, NC>(cur.w, sc, taddr); break;
+        case 1: dq_store<3, 1, G2, C0, NC>(cur.w, sc, taddr); break;
+        case 2: dq_store<3, 2, G2, C0, NC>(cur.w, sc, taddr); break;
+        case 3: dq_store<3, 3, G2, C0, NC>(cur.w, sc, taddr); break;
+        default: dq_store<3, 4, G2, C0, NC>(cur.w, sc, taddr); break;
       }
       ph3 = (ph3 == 0) ? 4 : ph3 - 1;
     } else {
-      dq_store<NB, 0, G2, C0, NC>(wv, sc, taddr);
+      dq_store<NB, 0, G2, C0, NC>(cur.w, sc, taddr);
     }
+    const int as = r.as;
+    if (++r.as == C::kAStages) { r.as = 0; r.aph ^= 1u; }
+    // next stage's first polls, in flight with the stores (r.s already advanced)
+    tok_f = mbar_try_wait(Bar::full(e.bars, r.s), r.ph);
+    tok_a = mbar_try_wait(Bar::aempty(e.bars, r.as), r.aph ^ 1u);
     tmem_st_wait();
     tc_fence_before();
     __syncwarp();
-    if (e.lane == 0) mbar_arrive(&e.afull[r.as]);
-    if (++r.s == C::kStages) { r.s = 0; r.ph ^= 1u; }
-    if (++r.as == C::kAStages) { r.as = 0; r.aph ^= 1u; }
+    if (e.lane == 0) mbar_arrive(Bar::afull(e.bars, as));
   }
   // release the item's last scale chunk
   __syncwarp();
-  if (e.lane == 0) mbar_arrive(&e.sempty[r.c]);
+  if (e.lane == 0) mbar_arrive(Bar::sempty(e.bars, r.c));
   if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
   return true;
 }
@@ -302,7 +342,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   constexpr int kStages = C::kStages;
   constexpr int kAStages = C::kAStages;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned, derived from the shared array by pointer arithmetic so that the
+  // compiler keeps reads through it as shared-memory loads
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* full = bars;                   // [kStages] activations + words landed
   uint64_t* empty = full + kStages;        // [kStages] stage consumed
@@ -457,8 +499,11 @@ __global__ void __launch_bounds__(kThreadsD, 1)
         if (!warp_wait(&acc_empty[buf], ((it / C::kAccBufs) & 1) ^ 1u, kDevTimeoutAccEmpty, kBusySleepNs)) break;
         tc_fence_after();
         for (int kt = 0; kt < KT; ++kt) {
-          if (!warp_wait(&full[s], ph, kDevTimeoutTmaFull, kBusySleepNs)) { ok = false; break; }
-          if (!warp_wait(&afull[as], aph, kDevTimeoutAFull, kBusySleepNs)) { ok = false; break; }
+          // both first polls in flight together
+          const bool tf = mbar_try_wait(smem_u32(&full[s]), ph);
+          const bool ta = mbar_try_wait(smem_u32(&afull[as]), aph);
+          if (!warp_wait_tok(smem_u32(&full[s]), ph, tf, kDevTimeoutTmaFull, kBusySleepNs)) { ok = false; break; }
+          if (!warp_wait_tok(smem_u32(&afull[as]), aph, ta, kDevTimeoutAFull, kBusySleepNs)) { ok = false; break; }
           tc_fence_after();
           const uint32_t act = smem_u32(smem + s * C::kStageBytes);
           const uint64_t b0 = sdesc_sw128(act);
@@ -558,12 +603,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     DqEnv env;
     env.stages = smem;
     env.chunks = smem + C::kChunkOff;
-    env.full = full;
-    env.empty = empty;
-    env.sfull = sfull;
-    env.sempty = sempty;
-    env.afull = afull;
-    env.aempty = aempty;
+    env.bars = smem_u32(bars);
     env.a_col0 = tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(C::kACol0);
     env.n = static_cast<uint32_t>(32 * q + lane);
     env.lane = lane;
