@@ -43,9 +43,14 @@ namespace {
 using tcw::Meta;
 using tcw::Work;
 
-constexpr int kThreadsD = 768;
+// Two groups of eight dequant warps take alternate stages; in a group, one warp per
+// (matrix, TMEM lane quarter) dequantises all 128 k of its matrix. While one group
+// waits for and reads a stage, the other group's warps on the same sub-partition
+// compute, so the integer and fp16 pipes stay busy.
 constexpr int kDqWarp0 = 8;
-constexpr int kNumDqWarps = 16;
+constexpr int kDqGroup = 8;  // warps per group
+constexpr int kNumDqWarps = 2 * kDqGroup;
+constexpr int kThreadsD = 32 * (kDqWarp0 + kNumDqWarps);
 constexpr int kSK = kperm::kStageK;  // 128
 constexpr int kScRows = 16;          // scale rows (groups) per chunk
 constexpr int kMaxWordRows = 16;
@@ -202,7 +207,7 @@ struct DqEnv {
   uint32_t bars;           // shared address of the barrier array (layout: BarsD)
   uint32_t a_col0;         // TMEM address of this warp's lane quarter, A ring column 0
   uint32_t n;              // feature row inside the tile (= TMEM lane)
-  int lane, mat, KT, log2g;
+  int lane, mat, grp, KT, log2g;
 };
 
 // Packed words and scale / zero of one stage and feature row, held in registers.
@@ -211,24 +216,29 @@ struct DqStage {
   __half sa, za, sb, zb;
 };
 
+// Keeps a dequant warp's scale chunk current for stage kt: on entering a new chunk
+// it releases the previous one and waits for the new one. Every warp runs this for
+// every stage, its group's or not, so each chunk gets all warps' releases.
+template <class C>
+__device__ __forceinline__ bool dq_chunk(int kt, int& ch, DqRings& r, const DqEnv& e) {
+  using Bar = BarsD<C>;
+  const int chn = ((kt * kSK) >> e.log2g) / kScRows;
+  if (chn == ch) return true;
+  if (ch >= 0) {
+    __syncwarp();
+    if (e.lane == 0) mbar_arrive(Bar::sempty(e.bars, r.c));
+    if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
+  }
+  ch = chn;
+  return warp_wait(Bar::sfull(e.bars, r.c), r.cph, kDevTimeoutTmaFull, kBusySleepNs);
+}
+
 // Reads stage kt (ring slot r.s) of a dequant warp's feature row into `d` and
 // releases the slot; `tok` is the result of an earlier try_wait on its full barrier.
-// `ch` is the scale chunk in use (-1 before the item's first stage).
 template <class C, int NB, bool G2>
-__device__ __forceinline__ bool dq_fetch(int kt, DqStage& d, bool tok, int& ch, DqRings& r, const DqEnv& e) {
+__device__ __forceinline__ bool dq_fetch(int kt, DqStage& d, bool tok, int ch, const DqRings& r, const DqEnv& e) {
   constexpr int kRows = kperm::stage_word_rows(NB);
   using Bar = BarsD<C>;
-  const int gl = (kt * kSK) >> e.log2g;  // first scale group of the stage
-  const int chn = gl / kScRows;
-  if (chn != ch) {
-    if (ch >= 0) {
-      __syncwarp();
-      if (e.lane == 0) mbar_arrive(Bar::sempty(e.bars, r.c));
-      if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
-    }
-    if (!warp_wait(Bar::sfull(e.bars, r.c), r.cph, kDevTimeoutTmaFull, kBusySleepNs)) return false;
-    ch = chn;
-  }
   if (!warp_wait_tok(Bar::full(e.bars, r.s), r.ph, tok, kDevTimeoutTmaFull, kBusySleepNs)) return false;
   const uint32_t* wcol =
       reinterpret_cast<const uint32_t*>(e.stages + r.s * C::kStageBytes + C::kActBytes + e.mat * C::kWordBytes) + e.n;
@@ -236,7 +246,7 @@ __device__ __forceinline__ bool dq_fetch(int kt, DqStage& d, bool tok, int& ch, 
   for (int i = 0; i < kMaxWordRows; ++i) d.w[i] = (i < kRows) ? wcol[i * 128] : 0u;
   const __half* sp = reinterpret_cast<const __half*>(e.chunks + r.c * C::kChunkBytes + (2 * e.mat) * C::kScBytes) + e.n;
   const __half* zp = sp + C::kScBytes / 2;
-  const int r0 = (gl - ch * kScRows) * 128;
+  const int r0 = (((kt * kSK) >> e.log2g) - ch * kScRows) * 128;
   d.sa = sp[r0];
   d.za = zp[r0];
   d.sb = d.sa;
@@ -247,57 +257,69 @@ __device__ __forceinline__ bool dq_fetch(int kt, DqStage& d, bool tok, int& ch, 
   }
   __syncwarp();
   if (e.lane == 0) mbar_arrive(Bar::empty(e.bars, r.s));
-  if (++r.s == C::kStages) { r.s = 0; r.ph ^= 1u; }
   return true;
 }
 
 // One work item of one dequant warp, specialised by bit-width, group layout and the
-// warp's columns [C0, C0 + NC) of its matrix: per stage, read the packed words and
-// scale / zero of its feature row, release the stage, dequantise into TMEM and hand
-// the A stage to the MMA. The first polls of the next stage's two waits are issued
-// while this stage's TMEM stores are in flight, so their latencies overlap. Scale
-// group, chunk and 3-bit phase advance incrementally. Returns false if a wait expired.
+// warp's columns [C0, C0 + NC) of its matrix. The warp takes the stages of its group
+// (kt = grp, grp + 2, ...): read the packed words and scale / zero of its feature
+// row, release the stage, dequantise into TMEM and hand the A stage to the MMA. The
+// first poll of its next stage's A slot is issued while the TMEM stores are in
+// flight. Ring positions, scale chunk and 3-bit phase advance on every stage.
+// Returns false if a wait expired.
 template <class C, int NB, bool G2, int C0, int NC>
 __device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
   using Bar = BarsD<C>;
   int ch = -1;
   int ph3 = 0;  // 3-bit phase index: P = (128 kt) % 10 = 0, 8, 6, 4, 2 -> index 0, 4, 3, 2, 1
-  bool tok_f = mbar_try_wait(Bar::full(e.bars, r.s), r.ph);
-  bool tok_a = mbar_try_wait(Bar::aempty(e.bars, r.as), r.aph ^ 1u);
+  bool tok_a = false;
   for (int kt = 0; kt < e.KT; ++kt) {
-    DqStage cur;
-    if (!dq_fetch<C, NB, G2>(kt, cur, tok_f, ch, r, e)) return false;
-    if (!warp_wait_tok(Bar::aempty(e.bars, r.as), r.aph ^ 1u, tok_a, kDevTimeoutAEmpty, kBusySleepNs)) return false;
-    tc_fence_after();
-    ScaleSet sc;
-    sc.s0 = __halves2half2(cur.sa, cur.sa);
-    sc.z0 = __halves2half2(cur.za, cur.za);
-    sc.s1 = __halves2half2(cur.sb, cur.sb);
-    sc.z1 = __halves2half2(cur.zb, cur.zb);
-    sc.s01 = __halves2half2(cur.sa, cur.sb);
-    sc.z01 = __halves2half2(cur.za, cur.zb);
-    const uint32_t taddr = e.a_col0 + static_cast<uint32_t>(r.as * C::kACols + e.mat * 64 + C0);
-    if constexpr (NB == 3) {
-      switch (ph3) {
-        case 0: dq_store<3, 0, G2, C0, NC>(cur.w, sc, taddr); break;
-        case 1: dq_store<3, 1, G2, C0, NC>(cur.w, sc, taddr); break;
-        case 2: dq_store<3, 2, G2, C0, NC>(cur.w, sc, taddr); break;
-        case 3: dq_store<3, 3, G2, C0, NC>(cur.w, sc, taddr); break;
-        default: dq_store<3, 4, G2, C0, NC>(cur.w, sc, taddr); break;
+    if (!dq_chunk<C>(kt, ch, r, e)) return false;
+    if (((kt ^ e.grp) & 1) == 0) {
+      const bool tok_f = mbar_try_wait(Bar::full(e.bars, r.s), r.ph);
+      if (kt < 2) tok_a = mbar_try_wait(Bar::aempty(e.bars, r.as), r.aph ^ 1u);  // item's first own stage
+      DqStage cur;
+      if (!dq_fetch<C, NB, G2>(kt, cur, tok_f, ch, r, e)) return false;
+      if (!warp_wait_tok(Bar::aempty(e.bars, r.as), r.aph ^ 1u, tok_a, kDevTimeoutAEmpty, kBusySleepNs))
+        return false;
+      tc_fence_after();
+      ScaleSet sc;
+      sc.s0 = __halves2half2(cur.sa, cur.sa);
+      sc.z0 = __halves2half2(cur.za, cur.za);
+      sc.s1 = __halves2half2(cur.sb, cur.sb);
+      sc.z1 = __halves2half2(cur.zb, cur.zb);
+      sc.s01 = __halves2half2(cur.sa, cur.sb);
+      sc.z01 = __halves2half2(cur.za, cur.zb);
+      const uint32_t taddr = e.a_col0 + static_cast<uint32_t>(r.as * C::kACols + e.mat * 64 + C0);
+      if constexpr (NB == 3) {
+        switch (ph3) {
+          case 0: dq_store<3, 0, G2, C0, NC>(cur.w, sc, taddr); break;
+          case 1: dq_store<3, 1, G2, C0, NC>(cur.w, sc, taddr); break;
+          case 2: dq_store<3, 2, G2, C0, NC>(cur.w, sc, taddr); break;
+          case 3: dq_store<3, 3, G2, C0, NC>(cur.w, sc, taddr); break;
+          default: dq_store<3, 4, G2, C0, NC>(cur.w, sc, taddr); break;
+        }
+      } else {
+        dq_store<NB, 0, G2, C0, NC>(cur.w, sc, taddr);
       }
-      ph3 = (ph3 == 0) ? 4 : ph3 - 1;
-    } else {
-      dq_store<NB, 0, G2, C0, NC>(cur.w, sc, taddr);
+      // first poll of the A slot of this warp's next stage (two positions on), in
+      // flight with the stores. No false positive from an older phase: this warp's
+      // wait above saw the MMA finish position - 3, hence also the slot's use before
+      // last (position - 4).
+      {
+        int as2 = r.as + 2;
+        uint32_t aph2 = r.aph;
+        if (as2 >= C::kAStages) { as2 -= C::kAStages; aph2 ^= 1u; }
+        tok_a = mbar_try_wait(Bar::aempty(e.bars, as2), aph2 ^ 1u);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (e.lane == 0) mbar_arrive(Bar::afull(e.bars, r.as));
     }
-    const int as = r.as;
+    if (++r.s == C::kStages) { r.s = 0; r.ph ^= 1u; }
     if (++r.as == C::kAStages) { r.as = 0; r.aph ^= 1u; }
-    // next stage's first polls, in flight with the stores (r.s already advanced)
-    tok_f = mbar_try_wait(Bar::full(e.bars, r.s), r.ph);
-    tok_a = mbar_try_wait(Bar::aempty(e.bars, r.as), r.aph ^ 1u);
-    tmem_st_wait();
-    tc_fence_before();
-    __syncwarp();
-    if (e.lane == 0) mbar_arrive(Bar::afull(e.bars, as));
+    if constexpr (NB == 3) ph3 = (ph3 == 0) ? 4 : ph3 - 1;
   }
   // release the item's last scale chunk
   __syncwarp();
@@ -363,14 +385,14 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 2);       // both producers arm the stage
-      mbar_init(&empty[s], 1 + kNumDqWarps);  // MMA commit + every dequant warp
+      mbar_init(&empty[s], 1 + kDqGroup);  // MMA commit + the stage's dequant group
     }
     for (int c = 0; c < 2; ++c) {
       mbar_init(&sfull[c], 1);
       mbar_init(&sempty[c], kNumDqWarps);
     }
     for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&afull[s], kNumDqWarps);
+      mbar_init(&afull[s], kDqGroup);
       mbar_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -599,7 +621,6 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     // ------------------------------------------------------------ dequant
     const int dw = warp - kDqWarp0;  // 0..15
     const int q = warp & 3;           // TMEM lane quarter = features 32q .. 32q+31
-    const int part = dw >> 3;  // k half of the stage
     DqEnv env;
     env.stages = smem;
     env.chunks = smem + C::kChunkOff;
@@ -608,6 +629,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     env.n = static_cast<uint32_t>(32 * q + lane);
     env.lane = lane;
     env.mat = (dw >> 2) & 1;
+    env.grp = dw >> 3;
     env.KT = KT;
     env.log2g = 31 - __clz(g);
     const bool g2 = (g == 64);
@@ -617,7 +639,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       if ((wk.nb < 1 || wk.nb > 4) && dw == 0 && lane == 0) set_device_error(kDevBadBits);
       const int nb = min(max(wk.nb, 1), 4);
       bool ok;
-      ok = (part == 0) ? dq_item_any<C, 0, 32>(g2, nb, rings, env) : dq_item_any<C, 32, 32>(g2, nb, rings, env);
+      ok = dq_item_any<C, 0, 64>(g2, nb, rings, env);
       if (!ok) break;
     }
   }
