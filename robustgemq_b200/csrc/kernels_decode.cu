@@ -255,6 +255,7 @@ template <bool XF16>
 __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1, const int32_t* __restrict__ idx,
                                                           int rows_a, GemvSrc src, float* __restrict__ part,
                                                           int splits) {
+  grid_dep_wait();
   extern __shared__ __align__(16) unsigned char s_raw[];
   __shared__ float s_red[8][kGemvCols];
   const int slab = blockIdx.x, s = blockIdx.y;
@@ -366,6 +367,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
 }
 
 __global__ void k_gemv_reduce(const float* __restrict__ part, int splits, int64_t count, __half* __restrict__ out) {
+  grid_dep_wait();
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (i >= count) return;
   float v = 0.f;
@@ -380,6 +382,7 @@ __global__ void k_gemv_reduce(const float* __restrict__ part, int splits, int64_
 __global__ void k_decode_combine(const float* __restrict__ part, int splits, int A, int n, const __half* __restrict__ w,
                                  const float* __restrict__ shared_part, int shared_splits,
                                  const __half* __restrict__ residual, __half* __restrict__ out) {
+  grid_dep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float acc = 0.f;
@@ -416,8 +419,8 @@ cudaError_t launch_gemv_t(const ProjDev& w0, const ProjDev* w1, const int32_t* i
     smem_set = static_cast<int>(smem);
   }
   dim3 grid((w0.n + kGemvCols - 1) / kGemvCols, splits, nmat * rows_a);
-  k_gemv<XF16><<<grid, kGemvThreads, smem, s>>>(w0, w1 != nullptr ? *w1 : w0, idx, rows_a, src, part, splits);
-  return cudaGetLastError();
+  return launch_dep(k_gemv<XF16>, grid, dim3(kGemvThreads), smem, s, w0, w1 != nullptr ? *w1 : w0, idx, rows_a, src,
+                    part, splits);
 }
 
 }  // namespace
@@ -444,18 +447,16 @@ cudaError_t launch_gemv(const ProjDev& w0, const ProjDev* w1, const int32_t* idx
 cudaError_t launch_gemv_reduce(const float* part, int splits, int rows_a, int n, uint16_t* out, cudaStream_t s) {
   const int64_t count = static_cast<int64_t>(rows_a) * n;
   if (count == 0) return cudaSuccess;
-  k_gemv_reduce<<<static_cast<unsigned>((count + 255) / 256), 256, 0, s>>>(part, splits, count,
-                                                                            reinterpret_cast<__half*>(out));
-  return cudaGetLastError();
+  return launch_dep(k_gemv_reduce, dim3(static_cast<unsigned>((count + 255) / 256)), dim3(256), 0, s, part, splits,
+                    count, reinterpret_cast<__half*>(out));
 }
 
 cudaError_t launch_decode_combine(const float* part, int splits, int A, int n, const uint16_t* w,
                                   const float* shared_part, int shared_splits, const uint16_t* residual, uint16_t* out,
                                   cudaStream_t s) {
-  k_decode_combine<<<(n + 255) / 256, 256, 0, s>>>(part, splits, A, n, reinterpret_cast<const __half*>(w), shared_part,
-                                                    shared_splits, reinterpret_cast<const __half*>(residual),
-                                                    reinterpret_cast<__half*>(out));
-  return cudaGetLastError();
+  return launch_dep(k_decode_combine, dim3((n + 255) / 256), dim3(256), 0, s, part, splits, A, n,
+                    reinterpret_cast<const __half*>(w), shared_part, shared_splits,
+                    reinterpret_cast<const __half*>(residual), reinterpret_cast<__half*>(out));
 }
 
 }  // namespace gemq

@@ -108,6 +108,7 @@ __device__ __forceinline__ void topk_warp(GetLogit get, int E, int k, int norm, 
 // or given logits).
 __global__ void k_topk(const void* __restrict__ logits, int logits_fp32, int64_t T, int E, int k, int norm,
                        int fp16_softmax, int32_t* __restrict__ topk_idx, __half* __restrict__ topk_w) {
+  grid_dep_wait();
   const int64_t t = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   if (t >= T) return;
   auto get = [&](int e) {
@@ -127,6 +128,7 @@ constexpr int kLogitTokens = 8;
 __global__ void __launch_bounds__(256) k_gate_logits(const __half* __restrict__ x, int64_t T, int D,
                                                      const __half* __restrict__ gate, int E, int fp32_logits,
                                                      void* __restrict__ logits) {
+  grid_dep_wait();
   extern __shared__ uint4 s_rows4[];  // [kLogitTokens][D / 8]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kLogitTokens;
@@ -225,6 +227,7 @@ __device__ __forceinline__ void stage_fwd3(uint8_t (*fwd3)[128]) {
 
 // ------------------------------------------------------------------ dispatch (large batches)
 __global__ void k_count(const int32_t* __restrict__ topk_idx, int64_t P, int E, int32_t* __restrict__ counts) {
+  grid_dep_wait();
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (i >= P) return;
   const int e = topk_idx[i];
@@ -238,6 +241,7 @@ __global__ void k_count(const int32_t* __restrict__ topk_idx, int64_t P, int E, 
 // Single block: exclusive scans over experts (E <= 1024).
 __global__ void k_scan_segs(const int32_t* __restrict__ counts, int E, int nt, Seg* __restrict__ segs,
                             int32_t* __restrict__ tile_prefix, int32_t* __restrict__ cursor) {
+  grid_dep_wait();
   __shared__ int s_rows[1024];
   __shared__ int s_tiles[1024];
   const int e = threadIdx.x;
@@ -271,6 +275,7 @@ __global__ void k_scatter(const int32_t* __restrict__ topk_idx, const __half* __
                           const __half* __restrict__ x, int64_t P, int k, int E, int D, int32_t* __restrict__ cursor,
                           int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm, __half* __restrict__ x_perm,
                           const int32_t* __restrict__ perm_nbits) {
+  grid_dep_wait();
   __shared__ uint8_t s_fwd3[5][128];
   if (perm_nbits != nullptr) {
     stage_fwd3(s_fwd3);
@@ -337,6 +342,7 @@ __global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restric
                                                         int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm,
                                                         __half* __restrict__ x_perm,
                                                         const int32_t* __restrict__ perm_nbits) {
+  grid_dep_wait();
   __shared__ int s_idx[kSmallDispatchMaxSlots];
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_tiles[kMaxExperts];
@@ -398,6 +404,7 @@ __global__ void k_combine(const __half* __restrict__ y_perm, const int32_t* __re
                           const int32_t* __restrict__ topk_idx, int64_t T, int k, int D, int fp32_sum,
                           const __half* __restrict__ add, const __half* __restrict__ residual,
                           __half* __restrict__ out) {
+  grid_dep_wait();
   const int64_t t = blockIdx.x;
   int order[16];
   int eid[16];
@@ -453,10 +460,9 @@ __global__ void k_combine(const __half* __restrict__ y_perm, const int32_t* __re
 cudaError_t launch_topk(const void* logits, bool logits_fp32, int64_t T, int E, int k, bool norm, bool fp16_softmax,
                         int32_t* topk_idx, uint16_t* topk_w, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  k_topk<<<static_cast<unsigned>((T * 32 + 255) / 256), 256, 0, stream>>>(
-      logits, logits_fp32 ? 1 : 0, T, E, k, norm ? 1 : 0, fp16_softmax ? 1 : 0, topk_idx,
-      reinterpret_cast<__half*>(topk_w));
-  return cudaGetLastError();
+  return launch_dep(k_topk, dim3(static_cast<unsigned>((T * 32 + 255) / 256)), dim3(256), 0, stream, logits,
+                    logits_fp32 ? 1 : 0, T, E, k, norm ? 1 : 0, fp16_softmax ? 1 : 0, topk_idx,
+                    reinterpret_cast<__half*>(topk_w));
 }
 
 cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16_t* gate, int E, bool fp32_logits,
@@ -471,10 +477,8 @@ cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16
     smem_set = smem;
   }
   const dim3 grid((E + kLogitExperts - 1) / kLogitExperts, static_cast<unsigned>((T + kLogitTokens - 1) / kLogitTokens));
-  k_gate_logits<<<grid, 32 * kLogitExperts, smem, stream>>>(reinterpret_cast<const __half*>(x), T, D,
-                                                             reinterpret_cast<const __half*>(gate), E,
-                                                             fp32_logits ? 1 : 0, logits);
-  return cudaGetLastError();
+  return launch_dep(k_gate_logits, grid, dim3(32 * kLogitExperts), smem, stream, reinterpret_cast<const __half*>(x), T,
+                    D, reinterpret_cast<const __half*>(gate), E, fp32_logits ? 1 : 0, logits);
 }
 
 
@@ -502,32 +506,31 @@ cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, con
   cudaError_t err;
   if (small_dispatch_ok(P, E)) {
     const unsigned grid = static_cast<unsigned>(P > 0 ? (P + 7) / 8 : 1);
-    k_dispatch_small<<<grid, 256, row_smem, stream>>>(topk_idx, reinterpret_cast<const __half*>(topk_w),
-                                                reinterpret_cast<const __half*>(x), static_cast<int>(P), k, E, D, nt,
-                                                counts, segs, tile_prefix, slot_pos, reinterpret_cast<__half*>(w_perm),
-                                                reinterpret_cast<__half*>(x_perm), perm_nbits);
-    return cudaGetLastError();
+    return launch_dep(k_dispatch_small, dim3(grid), dim3(256), row_smem, stream, topk_idx,
+                      reinterpret_cast<const __half*>(topk_w), reinterpret_cast<const __half*>(x), static_cast<int>(P),
+                      k, E, D, nt, counts, segs, tile_prefix, slot_pos, reinterpret_cast<__half*>(w_perm),
+                      reinterpret_cast<__half*>(x_perm), perm_nbits);
   }
   err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, stream);
   if (err != cudaSuccess) return err;
-  k_count<<<static_cast<unsigned>((P + 255) / 256), 256, 0, stream>>>(topk_idx, P, E, counts);
-  if ((err = cudaGetLastError()) != cudaSuccess) return err;
-  k_scan_segs<<<1, 1024, 0, stream>>>(counts, E, nt, segs, tile_prefix, cursor);
-  if ((err = cudaGetLastError()) != cudaSuccess) return err;
-  k_scatter<<<static_cast<unsigned>((P * 32 + 255) / 256), 256, row_smem, stream>>>(
-      topk_idx, reinterpret_cast<const __half*>(topk_w), reinterpret_cast<const __half*>(x), P, k, E, D, cursor,
-      slot_pos, reinterpret_cast<__half*>(w_perm), reinterpret_cast<__half*>(x_perm), perm_nbits);
-  return cudaGetLastError();
+  err = launch_dep(k_count, dim3(static_cast<unsigned>((P + 255) / 256)), dim3(256), 0, stream, topk_idx, P, E, counts);
+  if (err != cudaSuccess) return err;
+  err = launch_dep(k_scan_segs, dim3(1), dim3(1024), 0, stream, counts, E, nt, segs, tile_prefix, cursor);
+  if (err != cudaSuccess) return err;
+  return launch_dep(k_scatter, dim3(static_cast<unsigned>((P * 32 + 255) / 256)), dim3(256), row_smem, stream,
+                    topk_idx, reinterpret_cast<const __half*>(topk_w), reinterpret_cast<const __half*>(x), P, k, E, D,
+                    cursor, slot_pos, reinterpret_cast<__half*>(w_perm), reinterpret_cast<__half*>(x_perm),
+                    perm_nbits);
 }
 
 cudaError_t launch_combine(const uint16_t* y_perm, const int32_t* slot_pos, const int32_t* topk_idx, int64_t T, int k,
                            int D, bool fp32_sum, const uint16_t* add, const uint16_t* residual, uint16_t* out,
                            cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  k_combine<<<static_cast<unsigned>(T), 256, 0, stream>>>(
-      reinterpret_cast<const __half*>(y_perm), slot_pos, topk_idx, T, k, D, fp32_sum ? 1 : 0,
-      reinterpret_cast<const __half*>(add), reinterpret_cast<const __half*>(residual), reinterpret_cast<__half*>(out));
-  return cudaGetLastError();
+  return launch_dep(k_combine, dim3(static_cast<unsigned>(T)), dim3(256), 0, stream,
+                    reinterpret_cast<const __half*>(y_perm), slot_pos, topk_idx, T, k, D, fp32_sum ? 1 : 0,
+                    reinterpret_cast<const __half*>(add), reinterpret_cast<const __half*>(residual),
+                    reinterpret_cast<__half*>(out));
 }
 
 }  // namespace gemq

@@ -239,6 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
+  // everything above is private to this CTA; from here on it reads the segment
+  // table, activations and weights, and writes outputs other kernels use
+  grid_dep_wait();
   Meta& meta = *reinterpret_cast<Meta*>(smem + C::kMetaOff);
   tcw::stage_meta(meta, p, kDense);
   __syncthreads();
@@ -522,8 +525,8 @@ cudaError_t launch_t(const GemmArgs& a, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     attr_set = true;
   }
-  kern<<<a.num_sms, kThreads, C::kSmemBytes, stream>>>(p, m_act, words, m_s0, m_z0, m_s1, m_z1);
-  return cudaGetLastError();
+  return launch_dep(kern, dim3(a.num_sms), dim3(kThreads), C::kSmemBytes, stream, p, m_act, words, m_s0, m_z0, m_s1,
+                    m_z1);
 }
 
 template <int NT>

@@ -406,6 +406,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
+  // everything above is private to this CTA; from here on it reads the segment
+  // table, activations and weights, and writes outputs other kernels use
+  grid_dep_wait();
   Meta& meta = *reinterpret_cast<Meta*>(smem + C::kMetaOff);
   tcw::stage_meta(meta, p, false);
   __syncthreads();
@@ -739,8 +742,8 @@ cudaError_t launch_d(const GemmArgs& a, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     attr_set = true;
   }
-  kern<<<a.num_sms, kThreadsD, C::kSmemBytes, stream>>>(p, m_act, words, m_s0, m_z0, m_s1, m_z1);
-  return cudaGetLastError();
+  return launch_dep(kern, dim3(a.num_sms), dim3(kThreadsD), C::kSmemBytes, stream, p, m_act, words, m_s0, m_z0, m_s1,
+                    m_z1);
 }
 
 }  // namespace
