@@ -287,37 +287,62 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
   const int32_t* wbase = w.wq + static_cast<int64_t>(w.wq_strides[e]);
   uint4 wv[kBatch];
   if (n < N) load_words(wbase, N, n, wr0, wr1, wv);
-  // stage x
-  for (int i = threadIdx.x; i < kspan; i += blockDim.x) {
-    const int kk = k0 + i;
-    float v = 0.f;
-    if (kk < K) {
-      if (src.mode == kGemvX) {
-        v = __half2float(src.x[a * src.x_stride + kk]);
-      } else if (src.mode == kGemvSwiGLU) {
-        v = silu_f32(__half2float(src.x[a * src.x_stride + kk])) * __half2float(src.x3[a * src.x_stride + kk]);
-      } else {
-        const int64_t mstride = static_cast<int64_t>(src.part_splits) * src.part_rows * src.part_n;
-        float g1 = 0.f, g3 = 0.f;
-        // unrolled so that the partial loads of several splits issue together
-#pragma unroll 4
-        for (int q = 0; q < src.part_splits; ++q) {
-          const int64_t off = (static_cast<int64_t>(q) * src.part_rows + a) * src.part_n + kk;
-          g1 += src.part[off];
-          g3 += src.part[mstride + off];
+  // Stage x and the scale / zero rows. Every thread first issues all of its loads
+  // for a batch of elements into registers and only then stores them, so a batch
+  // costs one memory round trip instead of one per element.
+  constexpr int kXB = 4;  // elements per thread per batch
+  for (int base = 0; base < kspan; base += kXB * kGemvThreads) {
+    float v[kXB];
+    if (src.mode == kGemvX || src.mode == kGemvSwiGLU) {
+      __half x1[kXB], x3[kXB];
+#pragma unroll
+      for (int j = 0; j < kXB; ++j) {
+        const int kk = k0 + base + j * kGemvThreads + threadIdx.x;
+        const bool in = (base + j * kGemvThreads + threadIdx.x < kspan) && kk < K;
+        x1[j] = in ? src.x[a * src.x_stride + kk] : __float2half_rn(0.f);
+        x3[j] = (in && src.mode == kGemvSwiGLU) ? src.x3[a * src.x_stride + kk] : __float2half_rn(0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < kXB; ++j)
+        v[j] = (src.mode == kGemvX) ? __half2float(x1[j]) : silu_f32(__half2float(x1[j])) * __half2float(x3[j]);
+    } else {
+      const int64_t mstride = static_cast<int64_t>(src.part_splits) * src.part_rows * src.part_n;
+      float g1[kXB], g3[kXB];
+#pragma unroll
+      for (int j = 0; j < kXB; ++j) g1[j] = g3[j] = 0.f;
+      // split-major: the loads of all elements of one split issue together
+      for (int q = 0; q < src.part_splits; ++q) {
+#pragma unroll
+        for (int j = 0; j < kXB; ++j) {
+          const int kk = k0 + base + j * kGemvThreads + threadIdx.x;
+          if (base + j * kGemvThreads + threadIdx.x < kspan && kk < K) {
+            const int64_t off = (static_cast<int64_t>(q) * src.part_rows + a) * src.part_n + kk;
+            g1[j] += src.part[off];
+            g3[j] += src.part[mstride + off];
+          }
         }
-        const float x1 = __half2float(__float2half_rn(g1));
-        const float x3 = __half2float(__float2half_rn(g3));
-        v = (src.mode == kGemvPartF32) ? silu_f32(x1) * x3
-                                       : __half2float(__float2half_rn(__half2float(__float2half_rn(silu_f32(x1))) * x3));
+      }
+#pragma unroll
+      for (int j = 0; j < kXB; ++j) {
+        const float x1 = __half2float(__float2half_rn(g1[j]));
+        const float x3 = __half2float(__float2half_rn(g3[j]));
+        v[j] = (src.mode == kGemvPartF32)
+                   ? silu_f32(x1) * x3
+                   : __half2float(__float2half_rn(__half2float(__float2half_rn(silu_f32(x1))) * x3));
       }
     }
-    if constexpr (XF16)
-      reinterpret_cast<__half*>(s_raw)[i] = __float2half_rn(v);  // exact: kGemvX inputs are fp16
-    else
-      reinterpret_cast<float*>(s_raw)[i] = v;
+#pragma unroll
+    for (int j = 0; j < kXB; ++j) {
+      const int i = base + j * kGemvThreads + threadIdx.x;
+      if (i < kspan) {
+        if constexpr (XF16)
+          reinterpret_cast<__half*>(s_raw)[i] = __float2half_rn(v[j]);  // exact: kGemvX inputs are fp16
+        else
+          reinterpret_cast<float*>(s_raw)[i] = v[j];
+      }
+    }
   }
-  // stage the scale / zero rows of the groups [g0, g1] this block's K range touches
+  // the scale / zero rows of the groups [g0, g1] this block's K range touches
   const int xbytes = (XF16 ? 2 : 4) * gemv_x_elems(K, splits);
   __half* s_s = reinterpret_cast<__half*>(s_raw + ((xbytes + 15) & ~15));
   const int ng_max = gemv_groups(K, splits, g);
@@ -327,14 +352,29 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
   const int64_t zbase = static_cast<int64_t>(w.zs_strides[e]);
   const int ngr = g1 - g0 + 1;
   if ((N & 127) == 0 && ((reinterpret_cast<uintptr_t>(w.scales) | reinterpret_cast<uintptr_t>(w.zeros)) & 15) == 0) {
-    // whole slabs: 16-byte loads, scales and zeros in one pass (one load per thread
-    // for up to 8 groups), so their HBM round trips overlap instead of queueing
-    for (int i = threadIdx.x; i < ngr * 32; i += blockDim.x) {
-      const int arr = i / (ngr * 16), j = i - arr * ngr * 16;
-      const int gl = j >> 4, c8 = (j & 15) * 8;
-      const int64_t off = zbase + static_cast<int64_t>(g0 + gl) * N + slab * kGemvCols + c8;
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>((arr == 0 ? w.scales : w.zeros) + off));
-      *reinterpret_cast<uint4*>((arr == 0 ? s_s : s_z) + gl * 128 + c8) = v;
+    // whole slabs: 16-byte loads of scales and zeros, a batch of them per thread
+    const int n16 = ngr * 32;
+    for (int base = 0; base < n16; base += kXB * kGemvThreads) {
+      uint4 sv[kXB];
+#pragma unroll
+      for (int j = 0; j < kXB; ++j) {
+        const int i = base + j * kGemvThreads + threadIdx.x;
+        if (i < n16) {
+          const int arr = i / (ngr * 16), jj = i - arr * ngr * 16;
+          const int gl = jj >> 4, c8 = (jj & 15) * 8;
+          const int64_t off = zbase + static_cast<int64_t>(g0 + gl) * N + slab * kGemvCols + c8;
+          sv[j] = __ldg(reinterpret_cast<const uint4*>((arr == 0 ? w.scales : w.zeros) + off));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kXB; ++j) {
+        const int i = base + j * kGemvThreads + threadIdx.x;
+        if (i < n16) {
+          const int arr = i / (ngr * 16), jj = i - arr * ngr * 16;
+          const int gl = jj >> 4, c8 = (jj & 15) * 8;
+          *reinterpret_cast<uint4*>((arr == 0 ? s_s : s_z) + gl * 128 + c8) = sv[j];
+        }
+      }
     }
   } else {
 #pragma unroll 4
