@@ -425,14 +425,20 @@ __global__ void k_decode_combine(const float* __restrict__ part, int splits, int
   grid_dep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  float acc = 0.f;
-#pragma unroll 4
-  for (int a = 0; a < A; ++a) {
-    float v = 0.f;
-#pragma unroll 4
-    for (int s = 0; s < splits; ++s) v += part[(static_cast<int64_t>(s) * A + a) * n + i];
-    acc = fmaf(__half2float(w[a]), __half2float(__float2half_rn(v)), acc);
+  // split-major, so the partials of all rows a of one split load together; each
+  // x2[a] is still summed in split order
+  float x2[16];
+#pragma unroll
+  for (int a = 0; a < 16; ++a) x2[a] = 0.f;
+  for (int s = 0; s < splits; ++s) {
+#pragma unroll
+    for (int a = 0; a < 16; ++a)
+      if (a < A) x2[a] += part[(static_cast<int64_t>(s) * A + a) * n + i];
   }
+  float acc = 0.f;
+#pragma unroll
+  for (int a = 0; a < 16; ++a)
+    if (a < A) acc = fmaf(__half2float(w[a]), __half2float(__float2half_rn(x2[a])), acc);
   __half r = __float2half_rn(acc);
   if (shared_part != nullptr) {
     float v = 0.f;

@@ -23,6 +23,64 @@ namespace {
 
 constexpr int kMaxExperts = 256;
 
+// Top-k of one token's probabilities v (slot i of lane l = expert 32 i + l; NV slots
+// in use) by rank: a value's rank is the number of values ahead of it in the order
+// "larger probability first, lower expert id on ties" (NaN ahead of every number:
+// torch.topk's order), so the values of rank < k are the top k, in order. All
+// comparisons run at once instead of k rounds of an argmax. The selected weights
+// are summed in rank order (the order of the k-round selection), then lane r writes
+// the rank-r expert and its (renormalised) weight.
+template <int NV>
+__device__ __forceinline__ void select_topk(const float (&v)[kMaxExperts / 32], int E, int k, int norm,
+                                            int fp16_softmax, int32_t* __restrict__ idx_out,
+                                            __half* __restrict__ w_out) {
+  const int lane = threadIdx.x & 31;
+  auto key = [](float a) { return (a != a) ? FLT_MAX : a; };
+  float m[NV];
+  int rank[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    m[i] = key(v[i]);
+    rank[i] = 0;
+  }
+#pragma unroll
+  for (int jo = 0; jo < NV; ++jo) {
+#pragma unroll 8
+    for (int src = 0; src < 32; ++src) {
+      const float o = __shfl_sync(0xffffffffu, m[jo], src);
+      const int oe = jo * 32 + src;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int e = i * 32 + lane;
+        rank[i] += (oe < E && (o > m[i] || (o == m[i] && oe < e))) ? 1 : 0;
+      }
+    }
+  }
+  float wsum = 0.f, myw = 0.f;
+  int mye = 0;
+  for (int r = 0; r < k; ++r) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const unsigned b = __ballot_sync(0xffffffffu, i * 32 + lane < E && rank[i] == r);
+      if (b != 0u) {  // warp-uniform
+        const int src = __ffs(b) - 1;
+        const float val = __shfl_sync(0xffffffffu, v[i], src);
+        wsum += val;
+        if (lane == r) {
+          myw = val;
+          mye = i * 32 + src;
+        }
+        break;
+      }
+    }
+  }
+  if (lane < k) {
+    if (fp16_softmax) wsum = __half2float(__float2half_rn(wsum));
+    idx_out[lane] = mye;
+    w_out[lane] = __float2half_rn(norm ? myw / wsum : myw);
+  }
+}
+
 // Softmax + top-k + optional renormalisation of one token's logits by one warp.
 // Softmax in fp32 with expf; selection takes the larger probability first and the
 // lower expert id on ties; NaN ranks above every number (torch.topk's order), so
@@ -59,49 +117,11 @@ __device__ __forceinline__ void topk_warp(GetLogit get, int E, int k, int norm, 
     if (fp16_softmax && e < E) pr = __half2float(__float2half_rn(pr));
     v[i] = pr;
   }
-  auto key = [](float a) { return (a != a) ? FLT_MAX : a; };
-  float wsel[16];
-  int isel[16];
-  float wsum = 0.f;
-  for (int j = 0; j < k; ++j) {
-    float best = -FLT_MAX, bestv = 0.f;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < kMaxExperts / 32; ++i) {
-      const int e = i * 32 + lane;
-      if (e < E && v[i] != -3.f && (key(v[i]) > best || (key(v[i]) == best && e < bi))) {
-        best = key(v[i]);
-        bestv = v[i];
-        bi = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const float ov = __shfl_xor_sync(0xffffffffu, bestv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ob > best || (ob == best && oi < bi)) {
-        best = ob;
-        bestv = ov;
-        bi = oi;
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < kMaxExperts / 32; ++i)
-      if (i * 32 + lane == bi) v[i] = -3.f;
-    wsel[j] = bestv;
-    isel[j] = bi;
-    wsum += bestv;
-  }
-  if (lane == 0) {
-    if (fp16_softmax) wsum = __half2float(__float2half_rn(wsum));
-    for (int j = 0; j < k; ++j) {
-      float w = wsel[j];
-      if (norm) w = w / wsum;
-      idx_out[j] = isel[j];
-      w_out[j] = __float2half_rn(w);
-    }
-  }
+  const int nv = (E + 31) / 32;  // value slots per lane in use
+  if (nv <= 1) select_topk<1>(v, E, k, norm, fp16_softmax, idx_out, w_out);
+  else if (nv <= 2) select_topk<2>(v, E, k, norm, fp16_softmax, idx_out, w_out);
+  else if (nv <= 4) select_topk<4>(v, E, k, norm, fp16_softmax, idx_out, w_out);
+  else select_topk<8>(v, E, k, norm, fp16_softmax, idx_out, w_out);
 }
 
 // One warp per token, logits from global memory (the tensor-core router's output
@@ -134,9 +154,22 @@ __global__ void __launch_bounds__(256) k_gate_logits(const __half* __restrict__ 
   const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kLogitTokens;
   const int nt = (T - t0 < kLogitTokens) ? static_cast<int>(T - t0) : kLogitTokens;
   const int d8 = D / 8;
-  for (int i = threadIdx.x; i < nt * d8; i += blockDim.x) {
-    const int r = i / d8, c = i - r * d8;
-    s_rows4[r * d8 + c] = reinterpret_cast<const uint4*>(x + (t0 + r) * D)[c];
+  // all of a thread's row loads in flight before any store (one round trip)
+  for (int base = threadIdx.x; base < nt * d8; base += 8 * blockDim.x) {
+    uint4 t[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + j * blockDim.x;
+      if (i < nt * d8) {
+        const int r = i / d8, c = i - r * d8;
+        t[j] = reinterpret_cast<const uint4*>(x + (t0 + r) * D)[c];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + j * blockDim.x;
+      if (i < nt * d8) s_rows4[i] = t[j];
+    }
   }
   __syncthreads();
   const int e = blockIdx.x * kLogitExperts + warp;
@@ -145,7 +178,7 @@ __global__ void __launch_bounds__(256) k_gate_logits(const __half* __restrict__ 
   float acc[kLogitTokens];
 #pragma unroll
   for (int r = 0; r < kLogitTokens; ++r) acc[r] = 0.f;
-#pragma unroll 4
+#pragma unroll 8
   for (int c = lane; c < d8; c += 32) {
     const uint4 gv = __ldg(gr + c);
     const __half2* gh = reinterpret_cast<const __half2*>(&gv);
@@ -187,12 +220,22 @@ __device__ __forceinline__ void copy_row(const __half* __restrict__ src, __half*
                                          int lane, __half* sbuf, const uint8_t (*fwd3)[128]) {
   const uint4* s4 = reinterpret_cast<const uint4*>(src);
   uint4* d4 = reinterpret_cast<uint4*>(dst);
-  if (nb == 0) {
-    for (int i = lane; i < D / 8; i += 32) d4[i] = s4[i];
-    return;
-  }
+  // each lane's loads of a batch of 8 chunks go out before any store
   uint4* b4 = reinterpret_cast<uint4*>(sbuf);
-  for (int i = lane; i < D / 8; i += 32) b4[i] = s4[i];
+  for (int base = lane; base < D / 8; base += 8 * 32) {
+    uint4 t[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (base + 32 * j < D / 8) t[j] = s4[base + 32 * j];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (base + 32 * j < D / 8) {
+        if (nb == 0) d4[base + 32 * j] = t[j];
+        else b4[base + 32 * j] = t[j];
+      }
+    }
+  }
+  if (nb == 0) return;
   __syncwarp();
   const unsigned short* b16 = reinterpret_cast<const unsigned short*>(sbuf);
   // b in {1, 2, 4}: eps = 32 / b codes per word, slot 2j + h of a word block <-> code
@@ -426,10 +469,16 @@ __global__ void k_combine(const __half* __restrict__ y_perm, const int32_t* __re
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int j = 0; j < k; ++j) {
+    // the token's rows are loaded together (one round trip), then summed in order
+    uint4 yv[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < k && order[j] >= 0) yv[j] = *reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(order[j]) * D + d);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j >= k) break;
       if (order[j] < 0) continue;  // slot with an invalid expert id
-      const uint4 yv = *reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(order[j]) * D + d);
-      const __half* yh = reinterpret_cast<const __half*>(&yv);
+      const __half* yh = reinterpret_cast<const __half*>(&yv[j]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float y = __half2float(yh[i]);
