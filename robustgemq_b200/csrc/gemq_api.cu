@@ -626,9 +626,13 @@ int forward_n_tokens(gemq_layer_t* L, const uint16_t* x, int64_t T, uint16_t* ou
   // decode batches: the tensor-memory dequant GEMM, with activations in its K order
   const bool dec = tc && (flags & GEMQ_FWD_SMEM_DEQUANT) == 0 && tcd_gemm_supported(up) && tcd_gemm_supported(dn);
   if (dec) up.perm_out_nbits = L->w2.nbits;
+  // Few slots per expert (well under three waves of work items): order the segments
+  // by dequant cost so the decode GEMM's last wave holds its cheapest items. With
+  // more waves a mix of bit-widths on the SMs at any time measured faster.
+  const bool sort_segs = dec && P <= 2 * static_cast<int64_t>(E);
   tm.begin(GEMQ_STAGE_DISPATCH);
   GEMQ_CUDA(launch_dispatch(idx, w, x, T, k, E, D, up.nt, b.counts, b.cursor, b.segs, b.tile_prefix, b.slot_pos,
-                            b.w_perm, b.x_perm, dec ? L->w1.nbits : nullptr, s),
+                            b.w_perm, b.x_perm, dec ? L->w1.nbits : nullptr, sort_segs ? L->w1.nbits : nullptr, s),
             "dispatch");
   tm.end(GEMQ_STAGE_DISPATCH);
   tm.begin(GEMQ_STAGE_UP);

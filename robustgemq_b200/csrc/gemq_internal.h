@@ -107,7 +107,7 @@ bool small_dispatch_ok(int64_t P, int E);
 cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t T, int k,
                             int E, int D, int nt, int32_t* counts, int32_t* cursor, Seg* segs, int32_t* tile_prefix,
                             int32_t* slot_pos, uint16_t* w_perm, uint16_t* x_perm, const int32_t* perm_nbits,
-                            cudaStream_t stream);
+                            const int32_t* order_nbits, cudaStream_t stream);
 cudaError_t launch_combine(const uint16_t* y_perm, const int32_t* slot_pos, const int32_t* topk_idx, int64_t T, int k,
                            int D, bool fp32_sum, const uint16_t* add, const uint16_t* residual, uint16_t* out,
                            cudaStream_t stream);

@@ -384,7 +384,8 @@ __global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restric
                                                         Seg* __restrict__ segs, int32_t* __restrict__ tile_prefix,
                                                         int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm,
                                                         __half* __restrict__ x_perm,
-                                                        const int32_t* __restrict__ perm_nbits) {
+                                                        const int32_t* __restrict__ perm_nbits,
+                                                        const int32_t* __restrict__ order_nbits) {
   grid_dep_wait();
   __shared__ int s_idx[kSmallDispatchMaxSlots];
   __shared__ int s_cnt[kMaxExperts];
@@ -406,12 +407,46 @@ __global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restric
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_tiles[e] = (s_cnt[e] + nt - 1) / nt;
   __syncthreads();
   if (warp == 0) warp_exclusive_scan_256(s_cnt, s_start, E, lane);
-  if (warp == 1) warp_exclusive_scan_256(s_tiles, s_tstart, E, lane);
   __syncthreads();
   if (blockIdx.x == 0) {
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    // Segment order (rows keep their expert-order positions): expert id, or with
+    // order_nbits the dequant cost of the expert's bit-width, 3-bit first, then 4, 2
+    // and 1 bits, stable in expert id. The decode GEMM hands out work items in this
+    // order, whole waves round-robin, so its last, partial wave holds the cheapest.
+    __shared__ int s_wcnt[8][4];
+    __shared__ int s_order[kMaxExperts];
+    const int e = threadIdx.x;  // E <= 256 = blockDim.x
+    const bool valid = e < E;
+    int cls = 0;
+    if (order_nbits != nullptr && valid) {
+      const int nb = order_nbits[e];
+      cls = (nb == 3) ? 0 : (nb == 4) ? 1 : (nb == 2) ? 2 : 3;
+    }
+    const unsigned lt = (1u << lane) - 1u;
+    int within = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const unsigned b = __ballot_sync(0xffffffffu, valid && cls == c);
+      if (lane == 0) s_wcnt[warp][c] = __popc(b);
+      if (cls == c) within = __popc(b & lt);
+    }
+    __syncthreads();
+    int pos = within;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int w = 0; w < 8; ++w) pos += (c < cls || (c == cls && w < warp)) ? s_wcnt[w][c] : 0;
+    if (valid) {
+      s_order[pos] = e;
+      s_tstart[pos] = s_tiles[e];  // tiles in segment order, scanned below
+    }
+    __syncthreads();
+    if (warp == 0) warp_exclusive_scan_256(s_tstart, s_tstart, E, lane);
+    __syncthreads();
+    if (valid) {
+      const int eo = s_order[e];  // segment e
       counts[e] = s_cnt[e];
-      segs[e] = make_int4(e, s_start[e], s_start[e], s_cnt[e]);
+      segs[e] = make_int4(eo, s_start[eo], s_start[eo], s_cnt[eo]);
       tile_prefix[e] = s_tstart[e];
     }
     if (threadIdx.x == 0) tile_prefix[E] = s_tstart[E];
@@ -536,7 +571,7 @@ bool small_dispatch_ok(int64_t P, int E) { return P <= kSmallDispatchMaxSlots &&
 cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t T, int k,
                             int E, int D, int nt, int32_t* counts, int32_t* cursor, Seg* segs, int32_t* tile_prefix,
                             int32_t* slot_pos, uint16_t* w_perm, uint16_t* x_perm, const int32_t* perm_nbits,
-                            cudaStream_t stream) {
+                            const int32_t* order_nbits, cudaStream_t stream) {
   const int64_t P = T * k;
   if (perm_nbits != nullptr && D % kperm::kStageK != 0) return cudaErrorInvalidValue;
   // permuted copies stage each warp's row in shared memory (8 warps per block)
@@ -558,7 +593,7 @@ cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, con
     return launch_dep(k_dispatch_small, dim3(grid), dim3(256), row_smem, stream, topk_idx,
                       reinterpret_cast<const __half*>(topk_w), reinterpret_cast<const __half*>(x), static_cast<int>(P),
                       k, E, D, nt, counts, segs, tile_prefix, slot_pos, reinterpret_cast<__half*>(w_perm),
-                      reinterpret_cast<__half*>(x_perm), perm_nbits);
+                      reinterpret_cast<__half*>(x_perm), perm_nbits, order_nbits);
   }
   err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, stream);
   if (err != cudaSuccess) return err;

@@ -123,6 +123,27 @@ struct WordMapsD {
 };
 __host__ __device__ constexpr int box_index(int nb) { return nb - 1; }
 
+// ---------------------------------------------------------------- work order
+// CTA c's work items: round-robin over the whole waves (items c, c + G, ...), then
+// one item of the last, partial wave in reverse CTA order. Dispatch orders the
+// segments by dequant cost, heaviest bit-width first, so the last wave holds the
+// cheapest items and they go to the CTAs whose earlier items were the cheapest.
+struct ItemWalk {
+  int j, n, full;
+  __device__ __forceinline__ explicit ItemWalk(int total) : j(0) {
+    const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+    full = total / G * G;
+    n = total / G + ((G - 1 - c) < total - full ? 1 : 0);
+  }
+  __device__ __forceinline__ bool next(int& w) {
+    if (j >= n) return false;
+    const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+    w = (j * G < full) ? j * G + c : full + (G - 1 - c);
+    ++j;
+    return true;
+  }
+};
+
 // ---------------------------------------------------------------- dequant
 struct ScaleSet {
   __half2 s0, s1, s01, z0, z1, z01;
@@ -438,7 +459,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       uint32_t ph = 0;
       int armed = 0;
       bool ok = true;
-      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      ItemWalk items(total);
+      int w;
+      while (ok && items.next(w)) {
         const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
         const int nb = min(max(wk.nb, 1), 4);
         const int rows = kperm::stage_word_rows(nb);
@@ -483,7 +506,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       uint32_t cph = 0;
       int armed = 0;
       bool ok = true;
-      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      ItemWalk items(total);
+      int w;
+      while (ok && items.next(w)) {
         const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
         for (int ch = 0; ch < nchunks; ++ch) {
           if (!warp_wait(&sempty[c], cph ^ 1u, kDevTimeoutTmaEmpty, kIdleSleepNs)) { ok = false; break; }
@@ -518,7 +543,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       uint32_t ph = 0, aph = 0;
       int it = 0;
       bool ok = true;
-      for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
+      ItemWalk items(total);
+      int w;
+      for (; ok && items.next(w); ++it) {
         const int buf = it % C::kAccBufs;
         const uint32_t d_base = tmem + static_cast<uint32_t>(buf * C::kAccCols);
         if (!warp_wait(&acc_empty[buf], ((it / C::kAccBufs) & 1) ^ 1u, kDevTimeoutAccEmpty, kBusySleepNs)) break;
@@ -563,7 +590,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     int it = 0;
-    for (int w = blockIdx.x; w < total; w += gridDim.x, ++it) {
+    ItemWalk items(total);
+    int w;
+    for (; items.next(w); ++it) {
       const int buf = it % C::kAccBufs;
       const uint32_t lane_base =
           tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * C::kAccCols);
@@ -637,7 +666,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     env.log2g = 31 - __clz(g);
     const bool g2 = (g == 64);
     DqRings rings{0, 0, 0, 0u, 0u, 0u};
-    for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    ItemWalk items(total);
+    int w;
+    while (items.next(w)) {
       const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
       if ((wk.nb < 1 || wk.nb > 4) && dw == 0 && lane == 0) set_device_error(kDevBadBits);
       const int nb = min(max(wk.nb, 1), 4);
