@@ -292,11 +292,19 @@ template <class C, int NB, bool G2, int C0, int NC>
 __device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
   using Bar = BarsD<C>;
   int ch = -1;
-  int ph3 = 0;  // 3-bit phase index: P = (128 kt) % 10 = 0, 8, 6, 4, 2 -> index 0, 4, 3, 2, 1
+  // 3-bit phase index: P = (128 kt) % 10 = 0, 8, 6, 4, 2 -> index 0, 4, 3, 2, 1
+  int ph3 = (e.grp == 0) ? 0 : 4;
   bool tok_a = false;
-  for (int kt = 0; kt < e.KT; ++kt) {
+  // this warp's ring positions start at its group's first stage
+  if (e.grp == 1) {
+    if (++r.s == C::kStages) { r.s = 0; r.ph ^= 1u; }
+    if (++r.as == C::kAStages) { r.as = 0; r.aph ^= 1u; }
+  }
+  // the group's stages only (each chunk of 16 scale groups spans at least two
+  // stages, so both groups visit, and release, every chunk)
+  for (int kt = e.grp; kt < e.KT; kt += 2) {
     if (!dq_chunk<C>(kt, ch, r, e)) return false;
-    if (((kt ^ e.grp) & 1) == 0) {
+    {
       const bool tok_f = mbar_try_wait(Bar::full(e.bars, r.s), r.ph);
       if (kt < 2) tok_a = mbar_try_wait(Bar::aempty(e.bars, r.as), r.aph ^ 1u);  // item's first own stage
       DqStage cur;
@@ -338,9 +346,18 @@ __device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
       __syncwarp();
       if (e.lane == 0) mbar_arrive(Bar::afull(e.bars, r.as));
     }
-    if (++r.s == C::kStages) { r.s = 0; r.ph ^= 1u; }
-    if (++r.as == C::kAStages) { r.as = 0; r.aph ^= 1u; }
-    if constexpr (NB == 3) ph3 = (ph3 == 0) ? 4 : ph3 - 1;
+    // two ring positions on
+    r.s += 2;
+    if (r.s >= C::kStages) { r.s -= C::kStages; r.ph ^= 1u; }
+    r.as += 2;
+    if (r.as >= C::kAStages) { r.as -= C::kAStages; r.aph ^= 1u; }
+    if constexpr (NB == 3) ph3 = (ph3 + 3) % 5;
+  }
+  // ring positions end at the item's end: back off the overshoot past KT
+  const int over = (e.KT - e.grp + 1) / 2 * 2 + e.grp - e.KT;  // stages walked past KT (0 or 1)
+  if (over == 1) {
+    if (--r.s < 0) { r.s += C::kStages; r.ph ^= 1u; }
+    if (--r.as < 0) { r.as += C::kAStages; r.aph ^= 1u; }
   }
   // release the item's last scale chunk
   __syncwarp();
