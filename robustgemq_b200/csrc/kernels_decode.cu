@@ -150,8 +150,8 @@ constexpr int kBatch = 8;  // word rows of a warp whose loads are in flight toge
 __device__ __forceinline__ void load_words(const int32_t* wbase, int N, int n, int rb, int wr1, uint4 (&wv)[kBatch]) {
 #pragma unroll
   for (int i = 0; i < kBatch; ++i)
-    wv[i] = (rb + i < wr1) ? __ldg(reinterpret_cast<const uint4*>(wbase + static_cast<int64_t>(rb + i) * N + n))
-                           : make_uint4(0, 0, 0, 0);
+    wv[i] = (rb + i < wr1) ? __ldcs(reinterpret_cast<const uint4*>(wbase + static_cast<int64_t>(rb + i) * N + n))
+                           : make_uint4(0, 0, 0, 0);  // read once: streamed, evicted first
 }
 
 // One word row of the four feature columns of a lane.
@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
           const int arr = i / (ngr * 16), jj = i - arr * ngr * 16;
           const int gl = jj >> 4, c8 = (jj & 15) * 8;
           const int64_t off = zbase + static_cast<int64_t>(g0 + gl) * N + slab * kGemvCols + c8;
-          sv[j] = __ldg(reinterpret_cast<const uint4*>((arr == 0 ? w.scales : w.zeros) + off));
+          sv[j] = __ldcs(reinterpret_cast<const uint4*>((arr == 0 ? w.scales : w.zeros) + off));
         }
       }
 #pragma unroll

@@ -463,6 +463,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     {
       const bool first = (warp == 0);
       const int mat = first ? 0 : 1;
+      const uint64_t stream_policy = l2_evict_first_policy();
       if (elect_one()) {
         if (first) {
           tma_prefetch_desc(&tm_act);
@@ -494,8 +495,8 @@ __global__ void __launch_bounds__(kThreadsD, 1)
             mbar_arrive_expect_tx(&full[s], tx);
             tma_load_2d(st + mat * C::kActSub, &tm_act, &full[s], kt * kSK + mat * 64, wk.act_row);
             if (words)
-              tma_load_2d(st + C::kActBytes + mat * C::kWordBytes, wmap, &full[s], ncol,
-                          wrow + kperm::stage_word_row(nb, kt));
+              tma_load_2d_hint(st + C::kActBytes + mat * C::kWordBytes, wmap, &full[s], ncol,
+                               wrow + kperm::stage_word_row(nb, kt), stream_policy);
           }
           __syncwarp();
           ++armed;
@@ -510,6 +511,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   } else if (warp == 3) {
     // ------------------------------------------------------------ scale / zero chunks
     {
+      const uint64_t stream_policy = l2_evict_first_policy();
       if (elect_one()) {
         tma_prefetch_desc(&tm_s0);
         tma_prefetch_desc(&tm_z0);
@@ -533,12 +535,12 @@ __global__ void __launch_bounds__(kThreadsD, 1)
           if (elect_one()) {
             mbar_arrive_expect_tx(&sfull[c], C::kChunkBytes);
             const int n0 = C::kPairTiles ? 2 * wk.n0 : wk.n0;
-            tma_load_2d(cb, &tm_s0, &sfull[c], n0, wk.srow0 + ch * kScRows);
-            tma_load_2d(cb + C::kScBytes, &tm_z0, &sfull[c], n0, wk.srow0 + ch * kScRows);
+            tma_load_2d_hint(cb, &tm_s0, &sfull[c], n0, wk.srow0 + ch * kScRows, stream_policy);
+            tma_load_2d_hint(cb + C::kScBytes, &tm_z0, &sfull[c], n0, wk.srow0 + ch * kScRows, stream_policy);
             if constexpr (kMats == 2) {
               const int n1 = C::kPairTiles ? 2 * wk.n0 + 128 : wk.n0;
-              tma_load_2d(cb + 2 * C::kScBytes, &tm_s1, &sfull[c], n1, wk.srow1 + ch * kScRows);
-              tma_load_2d(cb + 3 * C::kScBytes, &tm_z1, &sfull[c], n1, wk.srow1 + ch * kScRows);
+              tma_load_2d_hint(cb + 2 * C::kScBytes, &tm_s1, &sfull[c], n1, wk.srow1 + ch * kScRows, stream_policy);
+              tma_load_2d_hint(cb + 3 * C::kScBytes, &tm_z1, &sfull[c], n1, wk.srow1 + ch * kScRows, stream_policy);
             }
           }
           __syncwarp();
