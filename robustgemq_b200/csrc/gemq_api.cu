@@ -626,6 +626,11 @@ int forward_n_tokens(gemq_layer_t* L, const uint16_t* x, int64_t T, uint16_t* ou
   // decode batches: the tensor-memory dequant GEMM, with activations in its K order
   const bool dec = tc && (flags & GEMQ_FWD_SMEM_DEQUANT) == 0 && tcd_gemm_supported(up) && tcd_gemm_supported(dn);
   if (dec) up.perm_out_nbits = L->w2.nbits;
+  // Token tiles of 16 halve the MMA width. With at most 16 tokens no expert gets more
+  // than 16 rows (a token picks an expert once); up to about 10 rows per expert on
+  // average the few experts that need a second tile (and stream their weights twice)
+  // cost less than the wider MMAs of 32-row tiles, measured on B200.
+  if (dec && (T <= kNtTiny || P <= 10 * static_cast<int64_t>(E))) up.nt = dn.nt = kNtTiny;
   // Few slots per expert (well under three waves of work items): order the segments
   // by dequant cost so the decode GEMM's last wave holds its cheapest items. With
   // more waves a mix of bit-widths on the SMs at any time measured faster.

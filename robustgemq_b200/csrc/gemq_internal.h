@@ -37,6 +37,7 @@ inline cudaError_t launch_dep(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 using Seg = int4;
 
 // Token-tile widths the tensor-core GEMM is instantiated for (UMMA N).
+constexpr int kNtTiny = 16;  // decode GEMM, batches of at most 16 tokens (16 rows per expert at most)
 constexpr int kNtSmall = 32;
 constexpr int kNtLarge = 128;
 

@@ -802,7 +802,7 @@ bool tcd_gemm_supported(const GemmArgs& a) {
   if (encode_fn_d() == nullptr) return false;
   // 32-token tiles (decode batches); prefill tiles of 128 stay on k_moe_tc, which
   // measured as fast there without the permuted dispatch copy
-  if (a.nt != kNtSmall) return false;
+  if (a.nt != kNtSmall && a.nt != kNtTiny) return false;
   if (a.mode != GemmMode::kSwiGLU && a.mode != GemmMode::kRouteWeight) return false;
   if (a.w0.k <= 0 || a.w0.k % kSK != 0 || a.w0.n % 128 != 0) return false;
   const int g = a.w0.group_size;
@@ -816,6 +816,9 @@ bool tcd_gemm_supported(const GemmArgs& a) {
 
 cudaError_t launch_tcd_gemm(const GemmArgs& a, cudaStream_t stream) {
   if (!tcd_gemm_supported(a)) return cudaErrorNotSupported;
+  if (a.nt == kNtTiny)
+    return a.mode == GemmMode::kSwiGLU ? launch_d<kNtTiny, GemmMode::kSwiGLU>(a, stream)
+                                       : launch_d<kNtTiny, GemmMode::kRouteWeight>(a, stream);
   return a.mode == GemmMode::kSwiGLU ? launch_d<kNtSmall, GemmMode::kSwiGLU>(a, stream)
                                      : launch_d<kNtSmall, GemmMode::kRouteWeight>(a, stream);
 }
