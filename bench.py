@@ -351,11 +351,11 @@ def run_ours(args, rank, world, local_rank):
 
 
 def kernel_launches(blocks, batches):
-    """Kernels of ours per step, counted from the pipeline: one-token path 4 per layer
-    (fused router + top-k, gate/up GEMV, down GEMV reducing the up partials, combine
-    reducing the down partials); n-token path at these batch sizes 5 (fused router +
+    """Kernels of ours per step, counted from the pipeline: one-token path 5 per layer
+    (gate logits, top-k, gate/up GEMV, down GEMV reducing the up partials, combine
+    reducing the down partials); n-token path at these batch sizes 6 (gate logits,
     top-k, one-launch dispatch, gate/up GEMM, down GEMM, combine)."""
-    return sum(len(blocks) * (4 if B == 1 else 5) for B in batches)
+    return sum(len(blocks) * (5 if B == 1 else 6) for B in batches)
 
 
 def profiled_traffic(kernel: str, batch: int):
