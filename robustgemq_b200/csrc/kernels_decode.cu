@@ -144,7 +144,7 @@ struct GroupStage {
   int g0;  // first staged group
 };
 
-constexpr int kBatch = 8;  // word rows of a warp whose loads are in flight together
+constexpr int kBatch = 4;  // word rows of a warp whose loads are in flight together (8 spills registers)
 
 // Loads word rows [rb, min(rb + kBatch, wr1)) of features n..n+3.
 __device__ __forceinline__ void load_words(const int32_t* wbase, int N, int n, int rb, int wr1, uint4 (&wv)[kBatch]) {
