@@ -237,22 +237,26 @@ struct DqStage {
   __half sa, za, sb, zb;
 };
 
-// Keeps a dequant warp's scale chunk current for stage kt: on entering a new chunk
-// it releases the previous one and waits for the new one. Every warp runs this for
-// every stage, its group's or not, so each chunk gets all warps' releases.
+// Moves a dequant warp's scale-chunk ring to chunk `target` (the chunk of 16 scale
+// groups its next stage reads): every chunk passed is released, the chunks this
+// warp never reads included (an item's last chunk may hold only stages of the other
+// group), so each chunk slot the producer fills gets all warps' releases. With
+// `wait`, waits for the target chunk to land. `ch` is the current chunk (-1 before
+// the item's first).
 template <class C>
-__device__ __forceinline__ bool dq_chunk(int kt, int& ch, DqRings& r, const DqEnv& e) {
+__device__ __forceinline__ bool dq_chunk_to(int target, bool wait, int& ch, DqRings& r, const DqEnv& e) {
   using Bar = BarsD<C>;
-  const int chn = ((kt * kSK) >> e.log2g) / kScRows;
-  if (chn == ch) return true;
-  if (ch >= 0) {
-    __syncwarp();
-    if (e.lane == 0) mbar_arrive(Bar::sempty(e.bars, r.c));
-    if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
+  if (ch == target) return true;
+  for (; ch < target; ++ch) {
+    if (ch >= 0) {
+      __syncwarp();
+      if (e.lane == 0) mbar_arrive(Bar::sempty(e.bars, r.c));
+      if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
+    }
   }
-  ch = chn;
-  return warp_wait(Bar::sfull(e.bars, r.c), r.cph, kDevTimeoutTmaFull, kBusySleepNs);
+  return !wait || warp_wait(Bar::sfull(e.bars, r.c), r.cph, kDevTimeoutTmaFull, kBusySleepNs);
 }
+__device__ __forceinline__ int chunk_of(int kt, int log2g) { return ((kt * kSK) >> log2g) / kScRows; }
 
 // Reads stage kt (ring slot r.s) of a dequant warp's feature row into `d` and
 // releases the slot; `tok` is the result of an earlier try_wait on its full barrier.
@@ -303,7 +307,7 @@ __device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
   // the group's stages only (each chunk of 16 scale groups spans at least two
   // stages, so both groups visit, and release, every chunk)
   for (int kt = e.grp; kt < e.KT; kt += 2) {
-    if (!dq_chunk<C>(kt, ch, r, e)) return false;
+    if (!dq_chunk_to<C>(chunk_of(kt, e.log2g), true, ch, r, e)) return false;
     {
       const bool tok_f = mbar_try_wait(Bar::full(e.bars, r.s), r.ph);
       if (kt < 2) tok_a = mbar_try_wait(Bar::aempty(e.bars, r.as), r.aph ^ 1u);  // item's first own stage
@@ -359,10 +363,8 @@ __device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
     if (--r.s < 0) { r.s += C::kStages; r.ph ^= 1u; }
     if (--r.as < 0) { r.as += C::kAStages; r.aph ^= 1u; }
   }
-  // release the item's last scale chunk
-  __syncwarp();
-  if (e.lane == 0) mbar_arrive(Bar::sempty(e.bars, r.c));
-  if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
+  // release the item's remaining scale chunks, through its last
+  dq_chunk_to<C>(chunk_of(e.KT - 1, e.log2g) + 1, false, ch, r, e);
   return true;
 }
 
