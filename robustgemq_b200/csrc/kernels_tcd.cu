@@ -238,22 +238,27 @@ struct DqStage {
 };
 
 // Moves a dequant warp's scale-chunk ring to chunk `target` (the chunk of 16 scale
-// groups its next stage reads): every chunk passed is released, the chunks this
-// warp never reads included (an item's last chunk may hold only stages of the other
-// group), so each chunk slot the producer fills gets all warps' releases. With
-// `wait`, waits for the target chunk to land. `ch` is the current chunk (-1 before
-// the item's first).
+// groups its next stage reads): the chunk held is released, and so is every chunk
+// passed over without being read (an item's last chunk may hold only stages of the
+// other group), so each slot the producer fills gets all warps' releases. A chunk
+// passed over is waited for before its release, so that the release cannot count
+// toward the slot's previous round. With `wait`, waits for the target chunk too.
+// `ch` is the chunk held (-1: none).
 template <class C>
 __device__ __forceinline__ bool dq_chunk_to(int target, bool wait, int& ch, DqRings& r, const DqEnv& e) {
   using Bar = BarsD<C>;
   if (ch == target) return true;
-  for (; ch < target; ++ch) {
-    if (ch >= 0) {
-      __syncwarp();
-      if (e.lane == 0) mbar_arrive(Bar::sempty(e.bars, r.c));
-      if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
-    }
+  auto release = [&]() {
+    __syncwarp();
+    if (e.lane == 0) mbar_arrive(Bar::sempty(e.bars, r.c));
+    if (++r.c == 2) { r.c = 0; r.cph ^= 1u; }
+  };
+  if (ch >= 0) release();
+  for (int c2 = ch + 1; c2 < target; ++c2) {
+    if (!warp_wait(Bar::sfull(e.bars, r.c), r.cph, kDevTimeoutTmaFull, kBusySleepNs)) return false;
+    release();
   }
+  ch = target;
   return !wait || warp_wait(Bar::sfull(e.bars, r.c), r.cph, kDevTimeoutTmaFull, kBusySleepNs);
 }
 __device__ __forceinline__ int chunk_of(int kt, int log2g) { return ((kt * kSK) >> log2g) / kScRows; }
