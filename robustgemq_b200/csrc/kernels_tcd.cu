@@ -3,7 +3,7 @@
 //
 // Same product as k_moe_tc (D[n, t] = sum_k deq(W_e)[k, n] * act[row_t, k], fp32 in
 // TMEM; the reference's x @ deq(W), dequant_group_gemm.py:109-138) for token tiles
-// of NT <= 32 rows, where each expert sees a handful of tokens and the kernel must
+// of 16 or 32 rows, where each expert sees a handful of tokens and the kernel must
 // stream packed weights at HBM speed. Differences from k_moe_tc:
 //   * the dequant warps write the A tile (128 features x 128 k per stage and
 //     matrix) straight into tensor memory with tcgen05.st, and the MMA reads A from
@@ -14,18 +14,20 @@
 //     fma.rn.f16 dequant (utils.py:206-210);
 //   * scale / zero rows are fetched 16 groups at a time into their own ring, and
 //     the per-stage copies are issued by two producer warps (one issuing lane
-//     sustains roughly one bulk tensor copy per 100+ cycles);
+//     sustains roughly one bulk tensor copy per 100+ cycles); packed words, scales
+//     and zeros are read with an L2 evict-first policy (read once per launch);
 //   * the down projection (route-weight mode) pairs two 128-feature tiles of the
 //     same expert in one work item, as the two "matrices" of the gate/up item.
 //
-// Warps (768 threads, one CTA per SM, grid-stride over work items):
+// Warps (768 threads, one CTA per SM; work items round-robin, see ItemWalk):
 //   0      producer: activation sub-tile 0 (k0..k0+63) and packed words of matrix 0
 //   1      TMEM allocation; MMA issue and commits from an elected lane
 //   2      producer: activation sub-tile 1 (k0+64..k0+127) and words of matrix 1
 //   3      producer: scale / zero chunks
 //   4-7    epilogue: tcgen05.ld -> rounding -> global stores (lane quarter = warp % 4)
-//   8-23   dequant: 16 warps = (K half, matrix) x lane quarter; warp w owns features
-//          32*(w%4) .. +31 (its TMEM lane quarter) of matrix ((w-8)/4)%2, k half (w-8)/8
+//   8-23   dequant: two groups of 8 warps taking alternate stages (group (w-8)/8 the
+//          stages kt with kt % 2 == group); in a group, warp w owns features
+//          32*(w%4) .. +31 (its TMEM lane quarter) of matrix ((w-8)/4)%2, all 128 k
 // Every wait is bounded (gemq_common.cuh); on expiry all roles drain and return.
 #include <cudaTypedefs.h>
 
