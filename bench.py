@@ -544,7 +544,10 @@ def main():
         torch.cuda.set_device(local_rank)
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+        # NCCL's own messages (its version banner when NCCL_DEBUG is set) go to stderr,
+        # so that stdout carries only the result line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
     line = run_ours(args, rank, world, local_rank)
     if world > 1:
         dist.barrier()
