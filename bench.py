@@ -524,6 +524,20 @@ def run_reference(args):
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def claim_stdout():
+    """Point file descriptor 1 at stderr for the rest of the run; return a stream on the real stdout.
+
+    Native libraries print to the C-level stdout (NCCL its version banner when NCCL_DEBUG is
+    set in the environment), which would put text before the result line. After this call
+    everything written to fd 1 lands on stderr, and the result line alone goes to the stream
+    returned here. dup2 shares the open file, so a log that holds both streams is not reopened
+    or truncated."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -537,6 +551,7 @@ def main():
         torch.set_num_threads(os.cpu_count() or 1)
         print(json.dumps(run_reference(args)))
         return
+    result_out = claim_stdout()
     import torch
     import torch.distributed as dist
 
@@ -544,16 +559,13 @@ def main():
         torch.cuda.set_device(local_rank)
         from datetime import timedelta
 
-        # NCCL's own messages (its version banner when NCCL_DEBUG is set) go to stderr,
-        # so that stdout carries only the result line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
     line = run_ours(args, rank, world, local_rank)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(line))
+        print(json.dumps(line), file=result_out, flush=True)
 
 
 if __name__ == "__main__":
