@@ -20,6 +20,17 @@ strides rebased). A forward on a rank's own tokens:
 DeepSeek's shared experts are replicated and run on the token's own rank; their
 output is added in fp16 after the combine (moe_block.py:575).
 
+Failures end in ``ExpertParallelError`` on every rank, never in a hang:
+
+* an invalid routing table on one rank (an expert id outside ``[0, E)``) travels
+  with the counts of step 2 as a per-peer status, so every rank learns of it in
+  the same exchange and raises before any row is sent; all ranks took the same
+  collective steps, so the group stays usable for the next forward;
+* a rank that is gone or never joins ends the others' pending exchange through
+  the process group's timeout (or the closed connection); the error names the
+  step, and the wrapper refuses further forwards, since the group's state is no
+  longer known (rebuild the group and the wrapper).
+
 With NCCL the exchange runs over NVLink; with gloo (CPU tests) the local expert
 compute, the router and the combine can be replaced by callables (``route_fn``,
 ``experts_fn``, ``combine_fn``) so the dispatch / combine bookkeeping is tested
@@ -38,6 +49,10 @@ from torch import Tensor, nn
 from .. import _lib
 from .._lib import check, ptr, stream_ptr
 from .moe_block import _QuantFusedMoEBlock
+
+
+class ExpertParallelError(RuntimeError):
+    """An expert-parallel forward failed: invalid routing on some rank, or a failed exchange."""
 
 
 def plan_dispatch(topk_idx: Tensor, experts_per_rank: int, world: int) -> Tuple[Tensor, Tensor, Tensor]:
@@ -111,6 +126,7 @@ class ExpertParallelMoE(nn.Module):
         self.route_fn = route_fn or self._route
         self.experts_fn = experts_fn or self._experts
         self.combine_fn = combine_fn or self._combine
+        self._broken: Optional[str] = None  # set when an exchange failed
 
     def _load_local(self, block: _QuantFusedMoEBlock):
         e1 = self.e0 + self.experts_per_rank
@@ -150,32 +166,52 @@ class ExpertParallelMoE(nn.Module):
         return out
 
     # ------------------------------------------------------------------ exchange
-    def _a2a(self, send: Tensor, send_counts, recv_counts) -> Tensor:
+    def _a2a(self, send: Tensor, send_counts, recv_counts, step: str) -> Tensor:
         recv = send.new_empty((int(sum(recv_counts)),) + tuple(send.shape[1:]))
         if self.world == 1:
             recv.copy_(send)
             return recv
-        dist.all_to_all_single(recv, send.contiguous(), [int(c) for c in recv_counts],
-                               [int(c) for c in send_counts], group=self.group)
+        try:
+            dist.all_to_all_single(recv, send.contiguous(), [int(c) for c in recv_counts],
+                                   [int(c) for c in send_counts], group=self.group)
+        except Exception as exc:  # a peer is gone, timed out or aborted
+            self._broken = f"exchange of {step} failed on rank {self.rank} of {self.world}: {exc}"
+            raise ExpertParallelError(self._broken) from exc
         return recv
 
     def forward_tokens(self, x: Tensor) -> Tuple[Tensor, Tensor]:
         """``x [T, D]`` fp16 on this rank -> ``(out [T, D], router_logits [T, E])``."""
+        if self._broken is not None:
+            raise ExpertParallelError(f"an earlier exchange failed ({self._broken}); rebuild the process group")
         x = x.contiguous()
         T, k = x.shape[0], self.top_k
         logits, idx, w = self.route_fn(x)
-        order, send_counts, local_ids = plan_dispatch(idx, self.experts_per_rank, self.world)
+        flat = idx.reshape(-1)
+        valid = not bool(((flat < 0) | (flat >= self.num_experts)).any())
+        if valid:
+            order, send_counts, local_ids = plan_dispatch(idx, self.experts_per_rank, self.world)
+        else:  # send no rows; the status below tells every peer
+            order = torch.arange(T * k, device=x.device)
+            send_counts = torch.zeros(self.world, dtype=torch.int64)
+            local_ids = torch.zeros(T * k, dtype=torch.int64)
         order = order.to(x.device)
-        # counts first, so every rank can size its receive buffers
+        # counts first, so every rank can size its receive buffers, each sent with
+        # this rank's routing status
         sc = send_counts.to(device=x.device, dtype=torch.int64)
-        rc = self._a2a(sc, [1] * self.world, [1] * self.world) if self.world > 1 else sc.clone()
-        send_counts, recv_counts = sc.tolist(), rc.tolist()
+        msg = torch.stack([sc, torch.full_like(sc, 0 if valid else 1)], dim=1).reshape(-1)
+        rmsg = self._a2a(msg, [2] * self.world, [2] * self.world, "counts").reshape(self.world, 2)
+        bad = [r for r in range(self.world) if int(rmsg[r, 1]) != 0]
+        if bad:
+            raise ExpertParallelError(
+                f"invalid routing table (expert id outside [0, {self.num_experts})) on rank(s) {bad}; "
+                "no rows were exchanged")
+        send_counts, recv_counts = sc.tolist(), rmsg[:, 0].tolist()
         tok = torch.div(order, k, rounding_mode="floor")
-        rows = self._a2a(x.index_select(0, tok), send_counts, recv_counts)
-        ids = self._a2a(local_ids.to(device=x.device, dtype=torch.int32), send_counts, recv_counts)
-        wts = self._a2a(w.reshape(-1).index_select(0, order), send_counts, recv_counts)
+        rows = self._a2a(x.index_select(0, tok), send_counts, recv_counts, "activation rows")
+        ids = self._a2a(local_ids.to(device=x.device, dtype=torch.int32), send_counts, recv_counts, "expert ids")
+        wts = self._a2a(w.reshape(-1).index_select(0, order), send_counts, recv_counts, "routing weights")
         y = self.experts_fn(rows, ids, wts)
-        back = self._a2a(y, recv_counts, send_counts)
+        back = self._a2a(y, recv_counts, send_counts, "expert outputs")
         slot_row = torch.empty(T * k, dtype=torch.int32, device=x.device)
         slot_row[order] = torch.arange(T * k, dtype=torch.int32, device=x.device)
         residual = None

@@ -3,8 +3,11 @@
 CPU tests run two gloo ranks; the router, the local experts and the combine are the
 oracle's (the exchange, the send order and the slot -> row mapping are the module's
 own), and every rank's output must equal the 1-process oracle block's on its tokens,
-bit for bit. GPU tests run the CUDA defaults: one rank against the block itself,
-and two NCCL ranks when the machine has two GPUs.
+bit for bit. Failure tests (gloo, CPU) make the failure on the host: one rank's
+router returns an expert id past E, or one rank never joins the exchange; every
+waiting rank must end with ``ExpertParallelError``, not hang. GPU tests run the CUDA
+defaults: one rank against the block itself, and two NCCL ranks when the machine has
+two GPUs.
 """
 
 from __future__ import annotations
@@ -75,47 +78,62 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _cpu_rank(rank, world, port, results):
-    import torch.distributed as dist
+def _cpu_ep(route_hook=None):
+    """An ExpertParallelMoE on the golden OLMoE block whose router, local experts and
+    combine are the oracle's; ``route_hook(idx)`` may rewrite the routed expert ids."""
     from oracle import gemq_oracle as O
     from robustgemq_b200.inference.expert_parallel import ExpertParallelMoE
 
+    blk, d = _golden_block()
+    ow = _oracle_weights(d)
+    k = ow.top_k
+    ep = None
+
+    def route_fn(x):
+        r = O.route(x.numpy(), ow.gate_w, k, ow.norm_topk_prob)
+        idx = r.topk_idx.astype(np.int32)
+        if route_hook is not None:
+            idx = route_hook(idx)
+        return torch.from_numpy(r.logits), torch.from_numpy(idx), torch.from_numpy(r.topk_w)
+
+    def experts_fn(rows, ids, wts):
+        rows_np, ids_np, w_np = rows.numpy(), ids.numpy(), wts.numpy()
+        y = np.zeros_like(rows_np)
+        for e in np.unique(ids_np):
+            sel = np.nonzero(ids_np == e)[0]
+            ye = O.expert_ffn_n_tokens(ow, ep.e0 + int(e), rows_np[sel])
+            y[sel] = (ye.astype(F32) * w_np[sel].astype(F32)[:, None]).astype(F16)
+        return torch.from_numpy(y)
+
+    def combine_fn(y, slot_row, idx, residual):
+        y_np, sr, ix = y.numpy(), slot_row.numpy(), idx.numpy()
+        T = ix.shape[0]
+        out = np.zeros((T, y_np.shape[1]), dtype=F16)
+        for t in range(T):
+            for j in np.argsort(ix[t], kind="stable"):
+                out[t] = (out[t].astype(F32) + y_np[sr[t * k + j]].astype(F32)).astype(F16)
+        return torch.from_numpy(out)
+
+    ep = ExpertParallelMoE(blk, route_fn=route_fn, experts_fn=experts_fn, combine_fn=combine_fn)
+    return ep, ow, d
+
+
+def _matches_oracle(ep, ow, d, rank, world):
+    from oracle import gemq_oracle as O
+
+    mine = np.ascontiguousarray(d["x"].astype(F16)[rank::world])
+    out, _ = ep.forward_tokens(torch.from_numpy(mine))
+    ref, _ = O.moe_forward_n_tokens(ow, mine)
+    return bool(np.array_equal(out.numpy().view(np.uint16), ref.view(np.uint16)))
+
+
+def _cpu_rank(rank, world, port, results):
+    import torch.distributed as dist
+
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
-        blk, d = _golden_block()
-        ow = _oracle_weights(d)
-        k = ow.top_k
-        ep = None
-
-        def route_fn(x):
-            r = O.route(x.numpy(), ow.gate_w, k, ow.norm_topk_prob)
-            return (torch.from_numpy(r.logits), torch.from_numpy(r.topk_idx.astype(np.int32)),
-                    torch.from_numpy(r.topk_w))
-
-        def experts_fn(rows, ids, wts):
-            rows_np, ids_np, w_np = rows.numpy(), ids.numpy(), wts.numpy()
-            y = np.zeros_like(rows_np)
-            for e in np.unique(ids_np):
-                sel = np.nonzero(ids_np == e)[0]
-                ye = O.expert_ffn_n_tokens(ow, ep.e0 + int(e), rows_np[sel])
-                y[sel] = (ye.astype(F32) * w_np[sel].astype(F32)[:, None]).astype(F16)
-            return torch.from_numpy(y)
-
-        def combine_fn(y, slot_row, idx, residual):
-            y_np, sr, ix = y.numpy(), slot_row.numpy(), idx.numpy()
-            T = ix.shape[0]
-            out = np.zeros((T, y_np.shape[1]), dtype=F16)
-            for t in range(T):
-                for j in np.argsort(ix[t], kind="stable"):
-                    out[t] = (out[t].astype(F32) + y_np[sr[t * k + j]].astype(F32)).astype(F16)
-            return torch.from_numpy(out)
-
-        ep = ExpertParallelMoE(blk, route_fn=route_fn, experts_fn=experts_fn, combine_fn=combine_fn)
-        x = d["x"].astype(F16)
-        mine = x[rank::world]
-        out, _ = ep.forward_tokens(torch.from_numpy(np.ascontiguousarray(mine)))
-        ref, _ = O.moe_forward_n_tokens(ow, mine)
-        results[rank] = bool(np.array_equal(out.numpy().view(np.uint16), ref.view(np.uint16)))
+        ep, ow, d = _cpu_ep()
+        results[rank] = _matches_oracle(ep, ow, d, rank, world)
     finally:
         dist.destroy_process_group()
 
@@ -134,6 +152,110 @@ def test_expert_parallel_two_gloo_ranks_match_the_single_block():
         p.join(120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert dict(results) == {0: True, 1: True}
+
+
+def _bad_routing_rank(rank, world, port, results):
+    """Rank 1's router returns an expert id past E on the first forward only."""
+    import torch.distributed as dist
+    from robustgemq_b200.inference.expert_parallel import ExpertParallelError
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        calls = {"n": 0}
+
+        def hook(idx):
+            calls["n"] += 1
+            if rank == 1 and calls["n"] == 1:
+                idx = idx.copy()
+                idx[0, 0] = 1000
+            return idx
+
+        ep, ow, d = _cpu_ep(route_hook=hook)
+        mine = torch.from_numpy(np.ascontiguousarray(d["x"].astype(F16)[rank::world]))
+        try:
+            ep.forward_tokens(mine)
+            raised = ""
+        except ExpertParallelError as exc:
+            raised = str(exc)
+        # every rank learned of rank 1's table in the counts exchange, and the group
+        # is still usable: the next forward runs and matches the oracle
+        results[rank] = ("rank(s) [1]" in raised, _matches_oracle(ep, ow, d, rank, world))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_invalid_routing_on_one_rank_fails_every_rank_and_keeps_the_group():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_bad_routing_rank, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(results) == {0: (True, True), 1: (True, True)}
+
+
+def _absent_peer_rank(rank, world, port, results, release):
+    """Rank 1 joins the group but never runs a forward; rank 0's exchange must fail
+    within the group's short timeout instead of waiting for ever."""
+    import time
+    from datetime import timedelta
+
+    import torch.distributed as dist
+    from robustgemq_b200.inference.expert_parallel import ExpertParallelError
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=3))
+    try:
+        if rank == 1:
+            release.wait(90)
+            results[rank] = True
+            return
+        ep, ow, d = _cpu_ep()
+        mine = torch.from_numpy(np.ascontiguousarray(d["x"].astype(F16)[0::world]))
+        t0 = time.monotonic()
+        first = second = ""
+        try:
+            ep.forward_tokens(mine)
+        except ExpertParallelError as exc:
+            first = str(exc)
+        waited = time.monotonic() - t0
+        try:
+            ep.forward_tokens(mine)  # refused on the host: no collective after a failed one
+        except ExpertParallelError as exc:
+            second = str(exc)
+        results[rank] = ("counts" in first, waited < 60, "earlier exchange failed" in second)
+        release.set()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_absent_peer_ends_the_exchange_with_an_error():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    release = manager.Event()
+    port = _free_port()
+    procs = [ctx.Process(target=_absent_peer_rank, args=(r, 2, port, results, release)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(150)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert procs[0].exitcode == 0, [p.exitcode for p in procs]
+    assert results.get(0) == (True, True, True), dict(results)
 
 
 @pytest.mark.gpu
