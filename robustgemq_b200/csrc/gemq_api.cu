@@ -8,6 +8,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "gemq_common.cuh"
 #include "gemq_internal.h"
 
@@ -15,7 +17,17 @@ namespace gemq {
 
 namespace {
 thread_local std::string t_last_error;
-}
+
+// Host-side NVTX range over one C-ABI call, named after the entry point, so a
+// profiler timeline (nsys, ncu's NVTX filter) shows which call launched which
+// kernels. NVTX records nothing unless a tool is attached.
+struct TraceRange {
+  explicit TraceRange(const char* name) { nvtxRangePushA(name); }
+  ~TraceRange() { nvtxRangePop(); }
+  TraceRange(const TraceRange&) = delete;
+  TraceRange& operator=(const TraceRange&) = delete;
+};
+}  // namespace
 
 void set_error(const std::string& msg) { t_last_error = msg; }
 
@@ -205,6 +217,7 @@ int gemq_get_device_error(uint32_t* code_out) {
 
 int gemq_pack_weights_over_cols(const uint8_t* codes, int64_t rows, int64_t cols, int32_t nbits, int32_t* out,
                                 void* stream) {
+  TraceRange trace("gemq_pack_weights_over_cols");
   if (nbits < 1 || nbits > 4) return fail(GEMQ_ERR_INVALID_ARGUMENT, "Untested quantization bitwidth (utils.py:83)");
   if (rows < 0 || cols < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative size");
   if (rows * cols > 0 && (codes == nullptr || out == nullptr)) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
@@ -214,6 +227,7 @@ int gemq_pack_weights_over_cols(const uint8_t* codes, int64_t rows, int64_t cols
 
 int gemq_unpack_over_cols(const int32_t* packed, int64_t rows, int64_t packed_cols, int64_t out_cols, int32_t nbits,
                           uint8_t* out, void* stream) {
+  TraceRange trace("gemq_unpack_over_cols");
   if (nbits < 1 || nbits > 4) return fail(GEMQ_ERR_INVALID_ARGUMENT, "Untested quantization bitwidth (utils.py:83)");
   if (rows < 0 || out_cols < 0 || packed_cols < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative size");
   const int eps = 32 / nbits;
@@ -225,6 +239,7 @@ int gemq_unpack_over_cols(const int32_t* packed, int64_t rows, int64_t packed_co
 }
 
 int gemq_dequant_expert(const gemq_proj_t* proj, int32_t expert, uint16_t* out, void* stream) {
+  TraceRange trace("gemq_dequant_expert");
   if (int rc = check_proj(proj, "proj")) return rc;
   if (expert < 0 || expert >= proj->num_experts) return fail(GEMQ_ERR_INVALID_ARGUMENT, "expert out of range");
   if (out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null output");
@@ -242,6 +257,7 @@ size_t gemq_group_gemm_workspace_size(int32_t num_indices) {
 int gemq_dequant_group_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t m, const int32_t* indices,
                             int32_t num_indices, uint16_t* out, void* workspace, size_t workspace_bytes,
                             void* stream) {
+  TraceRange trace("gemq_dequant_group_gemm");
   if (int rc = check_proj(proj, "proj")) return rc;
   if (num_indices <= 0 || num_indices > 1023) return fail(GEMQ_ERR_INVALID_ARGUMENT, "num_indices must be in [1, 1023]");
   if (m < 0 || m > INT32_MAX / 2) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad m");
@@ -274,6 +290,7 @@ int gemq_dequant_group_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t 
 
 int gemq_dequant_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t m, uint16_t* out, void* workspace,
                       size_t workspace_bytes, void* stream) {
+  TraceRange trace("gemq_dequant_gemm");
   if (int rc = check_proj(proj, "proj")) return rc;
   if (proj->num_experts != 1) return fail(GEMQ_ERR_INVALID_ARGUMENT, "dequant_gemm takes a single weight");
   if (m <= 0) return m == 0 ? GEMQ_OK : fail(GEMQ_ERR_INVALID_ARGUMENT, "bad m");
@@ -313,6 +330,7 @@ size_t gemq_gemv_workspace_size(const gemq_proj_t* proj, int32_t num_rows) {
 
 int gemq_dequant_gemv(const gemq_proj_t* proj, const uint16_t* x, uint16_t* out, void* workspace,
                       size_t workspace_bytes, void* stream) {
+  TraceRange trace("gemq_dequant_gemv");
   if (int rc = check_proj(proj, "proj")) return rc;
   if (proj->num_experts != 1) return fail(GEMQ_ERR_INVALID_ARGUMENT, "dequant_gemv takes a single weight");
   if (x == nullptr || out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
@@ -331,6 +349,7 @@ int gemq_dequant_gemv(const gemq_proj_t* proj, const uint16_t* x, uint16_t* out,
 int gemq_fused_up_proj(const gemq_proj_t* w1, const gemq_proj_t* w3, const uint16_t* x, const int32_t* idx,
                        int32_t num_idx, uint16_t* x1, uint16_t* x3, void* workspace, size_t workspace_bytes,
                        void* stream) {
+  TraceRange trace("gemq_fused_up_proj");
   if (int rc = check_proj(w1, "w1")) return rc;
   if (int rc = check_proj(w3, "w3")) return rc;
   if (w1->k != w3->k || w1->n != w3->n || w1->num_experts != w3->num_experts || w1->group_size != w3->group_size)
@@ -356,6 +375,7 @@ int gemq_fused_up_proj(const gemq_proj_t* w1, const gemq_proj_t* w3, const uint1
 
 int gemq_fused_down_proj(const gemq_proj_t* w2, const uint16_t* x1, const uint16_t* x3, const int32_t* idx,
                          int32_t num_idx, uint16_t* x2, void* workspace, size_t workspace_bytes, void* stream) {
+  TraceRange trace("gemq_fused_down_proj");
   if (int rc = check_proj(w2, "w2")) return rc;
   if (num_idx <= 0 || x1 == nullptr || x3 == nullptr || idx == nullptr || x2 == nullptr)
     return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad arguments");
@@ -374,6 +394,7 @@ int gemq_fused_down_proj(const gemq_proj_t* w2, const uint16_t* x1, const uint16
 
 // ------------------------------------------------------------------ layer
 int gemq_layer_create(const gemq_layer_desc_t* desc, gemq_layer_t** out) {
+  TraceRange trace("gemq_layer_create");
   if (desc == nullptr || out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
   const gemq_layer_desc_t& d = *desc;
   if (d.hidden <= 0 || d.inter <= 0 || d.num_experts <= 0 || d.top_k <= 0 || d.group_size <= 0)
@@ -707,6 +728,7 @@ size_t gemq_moe_workspace_size(const gemq_layer_t* layer, int64_t num_tokens, ui
 
 int gemq_moe_route(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, void* logits, int32_t* topk_idx,
                    uint16_t* topk_w, uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
+  TraceRange trace("gemq_moe_route");
   if (layer == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null layer");
   if (num_tokens < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative token count");
   if (num_tokens == 0) return GEMQ_OK;
@@ -724,6 +746,7 @@ int gemq_moe_route(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, v
 int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, uint16_t* out, void* router_logits,
                      const int32_t* topk_idx, const uint16_t* topk_w, uint32_t flags, void* workspace,
                      size_t workspace_bytes, void* stream) {
+  TraceRange trace("gemq_moe_forward");
   if (layer == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null layer");
   if (num_tokens < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative token count");
   if (num_tokens == 0) return GEMQ_OK;  // empty batch: nothing to read or write (pointers may be null)
@@ -764,6 +787,7 @@ int gemq_route(const uint16_t* x, int64_t num_tokens, int32_t hidden, const uint
                int32_t num_experts, int32_t top_k, int32_t router, int32_t norm_topk_prob, uint32_t flags,
                void* logits, int32_t* topk_idx, uint16_t* topk_w, void* workspace, size_t workspace_bytes,
                void* stream) {
+  TraceRange trace("gemq_route");
   if (num_tokens < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative token count");
   if (num_tokens == 0) return GEMQ_OK;
   if (x == nullptr || gate_weight == nullptr || logits == nullptr || topk_idx == nullptr || topk_w == nullptr)
@@ -794,6 +818,7 @@ int gemq_route(const uint16_t* x, int64_t num_tokens, int32_t hidden, const uint
 int gemq_moe_combine(const uint16_t* y, const int32_t* slot_row, const int32_t* topk_idx, int64_t num_tokens,
                      int32_t top_k, int32_t hidden, uint32_t flags, const uint16_t* residual, uint16_t* out,
                      void* stream) {
+  TraceRange trace("gemq_moe_combine");
   if (num_tokens < 0 || top_k <= 0 || top_k > 16) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad token or top_k count");
   if (num_tokens == 0) return GEMQ_OK;
   if (y == nullptr || slot_row == nullptr || topk_idx == nullptr || out == nullptr)
