@@ -95,8 +95,9 @@ class Clocks:
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
-        except Exception:
+        except subprocess.TimeoutExpired:
             self.proc.kill()
+            self.proc.wait()
         self.f.close()
         rows = []
         for line in self.path.read_text().splitlines():
