@@ -405,6 +405,13 @@ class QuantFusedDeepseekV2MoEBlock(_QuantFusedMoEBlock):
                                 self.hidden_dim, g)
         d.shared_w2 = make_proj(self.shared_w2_wq, self.shared_w2_scales, self.shared_w2_zeros, nb, zero, zero, fs, g)
 
+    def forward_single_expert(self, expert_idx: Tensor, hidden_states: Tensor, is_shared: bool = False) -> Tensor:
+        """Routed expert ``expert_idx``, or the shared experts when ``is_shared``
+        (moe_block.py:508-538)."""
+        if is_shared:
+            return self.forward_shared(hidden_states)
+        return super().forward_single_expert(expert_idx, hidden_states)
+
     def forward_shared(self, hidden_states: Tensor) -> Tensor:
         """Shared experts alone through dequant_gemm (moe_block.py:511-522)."""
         x = hidden_states

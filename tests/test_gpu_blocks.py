@@ -107,6 +107,22 @@ def test_tensor_core_and_cuda_core_paths_agree(family):
     assert rel_l2(y_tc.cpu().numpy(), y_simt.cpu().numpy()) <= 5e-4
 
 
+@pytest.mark.parametrize("family", FAMILIES)
+def test_forward_single_expert_matches_oracle(family):
+    """``forward_single_expert`` (moe_block.py:763-779; DeepSeek's ``is_shared``
+    branch, 508-522): three dequant GEMMs around the fp16 ``silu(x1) * x3``."""
+    blk, d = block_from_golden(family)
+    ob = block_weights(d, family)
+    x = cuda(d["x"])[:13].contiguous()
+    for e in (0, 5):
+        y = blk.forward_single_expert(torch.tensor([e], dtype=torch.int32, device="cuda"), x)
+        yo = O.expert_ffn_n_tokens(ob, e, d["x"][:13])
+        assert rel_l2(y.cpu().numpy(), yo) <= ORACLE_TOL, e
+    if family == "deepseek":
+        ys = blk.forward_single_expert(None, x, is_shared=True)
+        assert rel_l2(ys.cpu().numpy(), O.shared_ffn(ob, d["x"][:13])) <= ORACLE_TOL
+
+
 def _poison(nbytes=256 * 1024 * 1024):
     junk = torch.full((nbytes // 2,), float("nan"), dtype=torch.float16, device="cuda")
     del junk
