@@ -5,8 +5,10 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 #include <string>
 #include <utility>
 
@@ -30,6 +32,31 @@ inline cudaError_t launch_dep(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Devices whose raised shared-memory limits are remembered (a process on a larger
+// machine still works: beyond this the limit is set on every call).
+constexpr int kMaxDevices = 64;
+
+// Raises `kernel`'s dynamic shared-memory limit to at least `bytes` on the current
+// device. A limit set with cudaFuncSetAttribute belongs to the device that is current
+// when it is set, so the largest size set so far is kept per device in `done`, and a
+// process that drives several GPUs raises the limit on each of them. Sets are
+// serialised, so the limit only grows. Call outside stream capture; once a device's
+// limit covers `bytes` the call only reads an atomic.
+template <typename... KArgs>
+inline cudaError_t raise_smem_limit(void (*kernel)(KArgs...), size_t bytes, std::atomic<size_t> (&done)[kMaxDevices]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const bool tracked = dev >= 0 && dev < kMaxDevices;
+  if (tracked && done[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
+  static std::mutex m;
+  std::lock_guard<std::mutex> lock(m);
+  if (tracked && done[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess && tracked) done[dev].store(bytes, std::memory_order_release);
+  return e;
 }
 
 // A contiguous run of activation rows that all use one expert:

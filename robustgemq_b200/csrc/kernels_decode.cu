@@ -457,12 +457,10 @@ cudaError_t launch_gemv_t(const ProjDev& w0, const ProjDev* w1, const int32_t* i
   // plus the scale and zero rows of the groups it touches
   const int xbytes = (XF16 ? 2 : 4) * gemv_x_elems(w0.k, splits);
   const size_t smem = ((xbytes + 15) & ~15) + 2 * 2 * 128 * static_cast<size_t>(gemv_groups(w0.k, splits, w0.group_size));
-  static int smem_set = 48 * 1024;
-  if (static_cast<int>(smem) > smem_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(k_gemv<XF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static std::atomic<size_t> smem_done[kMaxDevices];  // per device: the attribute is per device
+  if (smem > 48 * 1024) {
+    cudaError_t e = raise_smem_limit(k_gemv<XF16>, smem, smem_done);
     if (e != cudaSuccess) return e;
-    smem_set = static_cast<int>(smem);
   }
   dim3 grid((w0.n + kGemvCols - 1) / kGemvCols, splits, nmat * rows_a);
   return launch_dep(k_gemv<XF16>, grid, dim3(kGemvThreads), smem, s, w0, w1 != nullptr ? *w1 : w0, idx, rows_a, src,

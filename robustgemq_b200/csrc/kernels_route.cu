@@ -553,12 +553,10 @@ cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16
                                void* logits, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
   const size_t smem = static_cast<size_t>(kLogitTokens) * D * 2;
-  static size_t smem_set = 48 * 1024;
-  if (smem > smem_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_gate_logits, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+  static std::atomic<size_t> smem_done[kMaxDevices];  // per device: the attribute is per device
+  if (smem > 48 * 1024) {
+    cudaError_t e = raise_smem_limit(k_gate_logits, smem, smem_done);
     if (e != cudaSuccess) return e;
-    smem_set = smem;
   }
   const dim3 grid((E + kLogitExperts - 1) / kLogitExperts, static_cast<unsigned>((T + kLogitTokens - 1) / kLogitTokens));
   return launch_dep(k_gate_logits, grid, dim3(32 * kLogitExperts), smem, stream, reinterpret_cast<const __half*>(x), T,
@@ -577,15 +575,11 @@ cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, con
   // permuted copies stage each warp's row in shared memory (8 warps per block)
   const size_t row_smem = perm_nbits != nullptr ? static_cast<size_t>(8) * D * sizeof(__half) : 0;
   if (row_smem > 0) {
-    static size_t attr_set = 0;  // raised once per larger row size (outside graph capture)
-    if (row_smem > attr_set) {
-      cudaError_t e = cudaFuncSetAttribute(k_dispatch_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(row_smem));
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(row_smem));
-      if (e != cudaSuccess) return e;
-      attr_set = row_smem;
-    }
+    // raised per device and per larger row size (outside graph capture)
+    static std::atomic<size_t> small_done[kMaxDevices], scatter_done[kMaxDevices];
+    cudaError_t e = raise_smem_limit(k_dispatch_small, row_smem, small_done);
+    if (e == cudaSuccess) e = raise_smem_limit(k_scatter, row_smem, scatter_done);
+    if (e != cudaSuccess) return e;
   }
   cudaError_t err;
   if (small_dispatch_ok(P, E)) {

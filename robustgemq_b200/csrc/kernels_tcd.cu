@@ -795,12 +795,10 @@ cudaError_t launch_d(const GemmArgs& a, cudaStream_t stream) {
   p.row_weight = reinterpret_cast<const __half*>(a.row_weight);
   p.perm_out_nbits = a.perm_out_nbits;
   auto kern = k_moe_tcd<NT, MODE>;
-  static bool attr_set = false;  // set once per instantiation (outside any graph capture)
-  if (!attr_set) {
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    if (err != cudaSuccess) return err;
-    attr_set = true;
-  }
+  // set once per instantiation and device (outside any graph capture)
+  static std::atomic<size_t> smem_done[kMaxDevices];
+  if (cudaError_t err = raise_smem_limit(kern, static_cast<size_t>(C::kSmemBytes), smem_done); err != cudaSuccess)
+    return err;
   return launch_dep(kern, dim3(a.num_sms), dim3(kThreadsD), C::kSmemBytes, stream, p, m_act, words, m_s0, m_z0, m_s1,
                     m_z1);
 }
