@@ -7,6 +7,8 @@ every call raises. ``load()`` builds it in-tree first if the sources are newer.
 from __future__ import annotations
 
 import ctypes
+import functools
+import inspect
 import threading
 from pathlib import Path
 from typing import Optional
@@ -153,6 +155,31 @@ def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 def stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def off_current_device(t: torch.Tensor) -> bool:
+    """True when ``t`` is a CUDA tensor on a device other than the current one.
+
+    The library launches on the current CUDA device, with the stream of the
+    tensors' device. A model spread over several GPUs in one process (layers placed
+    with a device map) moves each layer's inputs to that layer's GPU but does not
+    make it the current device, so callers switch devices when this is true."""
+    return t.is_cuda and t.device.index != torch.cuda.current_device()
+
+
+def on_input_device(fn):
+    """Decorator: run ``fn`` with the device of its first parameter (a tensor) current."""
+    first = next(iter(inspect.signature(fn).parameters))
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        t = args[0] if args else kwargs.get(first)
+        if isinstance(t, torch.Tensor) and off_current_device(t):
+            with torch.cuda.device(t.device):
+                return fn(*args, **kwargs)
+        return fn(*args, **kwargs)
+
+    return wrapper
 
 
 def device_error() -> int:

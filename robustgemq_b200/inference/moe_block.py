@@ -229,6 +229,9 @@ class _QuantFusedMoEBlock(nn.Module):
             raise ValueError("QuantFused blocks run on CUDA only (no CPU path)")
         if x.dtype != torch.float16:
             raise ValueError("hidden_states must be float16 (the reference computes in fp16)")
+        if _lib.off_current_device(x):
+            with torch.cuda.device(x.device):
+                return self._run(x, flags, want_logits, topk_idx, topk_w, logits_in)
         x = x.contiguous()
         T = x.shape[0]
         handle = self.layer_handle()
@@ -299,6 +302,9 @@ class _QuantFusedMoEBlock(nn.Module):
 
     def route(self, hidden_states: Tensor):
         """Router only: ``(logits, topk_idx int32, topk_w fp16)``."""
+        if _lib.off_current_device(hidden_states):
+            with torch.cuda.device(hidden_states.device):
+                return self.route(hidden_states)
         x = hidden_states.reshape(-1, self.hidden_dim).contiguous()
         T = x.shape[0]
         logits = torch.empty((T, self.num_experts), device=x.device,

@@ -27,7 +27,7 @@ from typing import Tuple
 import torch
 
 from . import _lib
-from ._lib import ProjT, check, ptr, stream_ptr
+from ._lib import ProjT, check, on_input_device, ptr, stream_ptr
 
 
 def _cuda(t: torch.Tensor, name: str) -> None:
@@ -60,6 +60,7 @@ def make_proj(wq: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor, nbits
 
 
 # ------------------------------------------------------------------ packing
+@on_input_device
 def pack_weights_over_cols(W_q: torch.Tensor, W_nbits: int, packing_bitwidth: int = 32,
                            transpose: bool = True) -> Tuple[torch.Tensor, int]:
     """uint8 codes ``[N, K]`` -> int32 words; returns ``(words, 32 // W_nbits)`` where
@@ -78,6 +79,7 @@ def pack_weights_over_cols(W_q: torch.Tensor, W_nbits: int, packing_bitwidth: in
     return (out.t() if transpose else out), eps
 
 
+@on_input_device
 def unpack_over_cols(W_q_packed: torch.Tensor, W_nbits: int, packing_bitwidth: int, num_output_cols: int,
                      dtype: torch.dtype = torch.uint8) -> torch.Tensor:
     """Inverse of the packer on the ``[N, cdiv(K, eps)]`` buffer (utils.py:149-189)."""
@@ -91,6 +93,7 @@ def unpack_over_cols(W_q_packed: torch.Tensor, W_nbits: int, packing_bitwidth: i
     return out if dtype == torch.uint8 else out.to(dtype)
 
 
+@on_input_device
 def dequantize_expert(wq, scales, zeros, nbits, wq_strides, zs_strides, K: int, group_size: int,
                       expert: int) -> torch.Tensor:
     """Dequantised ``[K, N]`` fp16 weight of one expert: the reference's ``dequantize``
@@ -102,6 +105,7 @@ def dequantize_expert(wq, scales, zeros, nbits, wq_strides, zs_strides, K: int, 
 
 
 # ------------------------------------------------------------------ GEMMs
+@on_input_device
 def dequant_group_gemm(x: torch.Tensor, indices: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor,
                        zeros: torch.Tensor, nbits: torch.Tensor, group_sizes: torch.Tensor, wq_strides: torch.Tensor,
                        zs_strides: torch.Tensor, compute_dtype=torch.float16) -> torch.Tensor:
@@ -140,6 +144,7 @@ class _SingleMeta:
         return cls.cache[key]
 
 
+@on_input_device
 def dequant_gemm(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor, nbits: int,
                  group_size: int) -> torch.Tensor:
     """``x @ dequantize(w_q)`` for one packed weight (dequant_gemm.py:150-193)."""
@@ -155,6 +160,7 @@ def dequant_gemm(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, zeros
     return out
 
 
+@on_input_device
 def dequant_splitk_gemv(x: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor, nbits: int,
                         group_size: int) -> torch.Tensor:
     """Batch-1 ``x @ dequantize(w_q)`` (dequant_gemv.py:118-156). The split-K partial
@@ -179,6 +185,7 @@ def _stacked_zs(E: int, K: int, group_size: int, N: int, device) -> torch.Tensor
     return torch.arange(E, dtype=torch.int32, device=device) * ((K // group_size) * N)
 
 
+@on_input_device
 def fused_dequant_up_proj(x: torch.Tensor, idx: torch.Tensor, w1: torch.Tensor, w3: torch.Tensor,
                           w1_scales: torch.Tensor, w1_zeros: torch.Tensor, w3_scales: torch.Tensor,
                           w3_zeros: torch.Tensor, nbits: torch.Tensor, w_strides: torch.Tensor, group_size: int):
@@ -203,6 +210,7 @@ def fused_dequant_up_proj(x: torch.Tensor, idx: torch.Tensor, w1: torch.Tensor, 
     return x1, x3
 
 
+@on_input_device
 def fused_dequant_down_proj(x1: torch.Tensor, x3: torch.Tensor, idx: torch.Tensor, w2: torch.Tensor,
                             w2_scales: torch.Tensor, w2_zeros: torch.Tensor, nbits: torch.Tensor,
                             w_strides: torch.Tensor, group_size: int) -> torch.Tensor:

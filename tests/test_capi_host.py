@@ -214,3 +214,52 @@ def test_stacking_matches_reference_layout():
     bad[1].group_size = 128
     with pytest.raises(AssertionError, match="Group sizes"):
         QuantFusedOlmoeMoEBlock.from_packed(cfg, torch.zeros((3, K), dtype=torch.float16), bad, bad, w2)
+
+
+class _FakeCudaTensor:
+    """Stands for a CUDA tensor on device ``index`` (this machine has no GPU)."""
+
+    is_cuda = True
+
+    def __init__(self, index):
+        self.device = SimpleNamespace(type="cuda", index=index)
+
+
+def test_calls_switch_to_the_inputs_device(monkeypatch):
+    """A model spread over several GPUs in one process calls each layer with its
+    inputs on that layer's GPU while another device is current; the Python entry
+    points make the input's device current for the call, and only then."""
+    import contextlib
+
+    import torch
+    from robustgemq_b200 import _lib
+
+    current = {"dev": 0}
+    entered = []
+
+    @contextlib.contextmanager
+    def fake_device(d):
+        entered.append(d.index)
+        prev, current["dev"] = current["dev"], d.index
+        try:
+            yield
+        finally:
+            current["dev"] = prev
+
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: current["dev"])
+    monkeypatch.setattr(torch.cuda, "device", fake_device)
+    monkeypatch.setattr(torch, "Tensor", _FakeCudaTensor)  # isinstance check in the decorator
+
+    seen = []
+
+    @_lib.on_input_device
+    def op(x, scale=1):
+        seen.append(current["dev"])
+        return scale
+
+    assert op(_FakeCudaTensor(0)) == 1 and entered == [] and seen == [0]
+    assert op(_FakeCudaTensor(1), scale=2) == 2 and entered == [1] and seen == [0, 1]
+    assert op(x=_FakeCudaTensor(1)) == 1 and entered == [1, 1] and seen == [0, 1, 1]
+    assert current["dev"] == 0  # restored after each call
+    assert not _lib.off_current_device(_FakeCudaTensor(0))
+    assert _lib.off_current_device(_FakeCudaTensor(3))
