@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -70,11 +71,19 @@ class Clocks:
 
     def __init__(self):
         self.proc = None
-        self.path = ROOT / "gpurun_out" / "bench_clocks.csv"
+        # the samples go to GEMQ_BENCH_CLOCKS_CSV when it is set (to keep them), else
+        # to a fresh temporary file
+        keep = os.environ.get("GEMQ_BENCH_CLOCKS_CSV")
+        if keep:
+            self.path = Path(keep)
+        else:
+            fd, name = tempfile.mkstemp(prefix="gemq_bench_clocks_", suffix=".csv")
+            os.close(fd)
+            self.path = Path(name)
 
     def start(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
+            self.path.parent.mkdir(parents=True, exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
