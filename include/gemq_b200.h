@@ -141,7 +141,10 @@ int gemq_dequant_group_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t 
  * array's address (cudaGetSymbolAddress), so make it before any stream capture.
  * Every call shares the one array: calls that overlap on the GPU (other streams,
  * other host threads) race and must be serialised by the caller. Each call
- * rewrites the entries it reads, so no clearing is needed between calls. */
+ * rewrites the entries it reads, so no clearing is needed between calls. The
+ * looked-up address is kept for the life of the process: do not call
+ * cudaDeviceReset on a device once this entry point has run there.
+ * Both group GEMM entry points reject num_indices * m above 2^31 - 1 rows. */
 #define GEMQ_NOALLOC_MAX_INDICES 1023
 int gemq_dequant_group_gemm_noalloc(const gemq_proj_t* proj, const uint16_t* x, int64_t m, const int32_t* indices,
                                     int32_t num_indices, uint16_t* out, void* stream);

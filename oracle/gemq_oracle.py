@@ -141,24 +141,33 @@ def dequantize_expert(proj: PackedProj, e: int, fma: str = "single") -> np.ndarr
     start at element ``wq_strides[e]`` with row stride N; code ``(k, n)`` sits in
     word row ``k // eps`` at shift ``(k % eps) * nbits``; scale/zero row ``k // g``
     starting at element ``zs_strides[e]``.
+
+    ``single`` (the GPU's ``fma.rn.f16``): every fp16 value is an integer multiple
+    of 2**-24 below 2**16, and the code is below 2**4, so ``q*s + z`` spans at
+    most 45 bits and is exact in float64; the one rounding is the float64 -> fp16
+    conversion (round to nearest even), the same result as ``fma_f16``.
     """
     nb = int(proj.nbits[e])
     g = int(proj.group_sizes[e])
     eps = elements_per_word(nb)
     K, N = proj.K, proj.N
-    wflat = proj.wq.reshape(-1)
     rows = packed_rows(K, nb)
     w0 = int(proj.wq_strides[e])
-    words = wflat[w0: w0 + rows * N].reshape(rows, N).view(np.uint32)
-    k = np.arange(K)
-    q = (words[k // eps, :] >> ((k % eps) * nb).astype(np.uint32)[:, None]) & np.uint32((1 << nb) - 1)
-    z0 = int(proj.zs_strides[e])
-    sflat = proj.scales.reshape(-1)
-    zflat = proj.zeros.reshape(-1)
+    words = proj.wq.reshape(-1)[w0: w0 + rows * N].reshape(rows, N).view(np.uint32)
+    shifts = (np.arange(eps, dtype=np.uint32) * np.uint32(nb))[None, :, None]
+    # code k = r*eps + j of word row r sits at bit j*nb (utils.py:134-142)
+    q = ((words[:, None, :] >> shifts) & np.uint32((1 << nb) - 1)).reshape(rows * eps, N)[:K]
     ng = K // g
-    s = sflat[z0: z0 + ng * N].reshape(ng, N)[k // g, :]
-    z = zflat[z0: z0 + ng * N].reshape(ng, N)[k // g, :]
-    return fma_f16(q, s, z, fma)
+    z0 = int(proj.zs_strides[e])
+    s = proj.scales.reshape(-1)[z0: z0 + ng * N].reshape(ng, 1, N)
+    z = proj.zeros.reshape(-1)[z0: z0 + ng * N].reshape(ng, 1, N)
+    qg = q.reshape(ng, g, N)
+    if fma == "double":
+        return fma_f16(qg, s, z, fma).reshape(K, N)
+    if fma != "single":
+        raise ValueError(fma)
+    w = qg.astype(F64) * s.astype(F64) + z.astype(F64)
+    return w.reshape(K, N).astype(F16)
 
 
 def matmul_f16_out(a: np.ndarray, b: np.ndarray) -> np.ndarray:

@@ -261,6 +261,9 @@ int gemq_dequant_group_gemm(const gemq_proj_t* proj, const uint16_t* x, int64_t 
   if (int rc = check_proj(proj, "proj")) return rc;
   if (num_indices <= 0 || num_indices > 1023) return fail(GEMQ_ERR_INVALID_ARGUMENT, "num_indices must be in [1, 1023]");
   if (m < 0 || m > INT32_MAX / 2) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad m");
+  // output rows of index a start at a * m, held as a 32-bit row offset in the segment table
+  if (static_cast<int64_t>(num_indices) * m > INT32_MAX)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "num_indices * m exceeds 2^31 - 1 output rows");
   if (m == 0) return GEMQ_OK;
   if (x == nullptr || out == nullptr || indices == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
   if (workspace_bytes < gemq_group_gemm_workspace_size(num_indices) || workspace == nullptr)
@@ -889,6 +892,7 @@ int noalloc_scratch(void** out) {
 extern "C" int gemq_dequant_group_gemm_noalloc(const gemq_proj_t* proj, const uint16_t* x, int64_t m,
                                                const int32_t* indices, int32_t num_indices, uint16_t* out,
                                                void* stream) {
+  TraceRange trace("gemq_dequant_group_gemm_noalloc");
   if (int rc = check_proj(proj, "proj")) return rc;
   if (num_indices > GEMQ_NOALLOC_MAX_INDICES)
     return fail(GEMQ_ERR_INVALID_ARGUMENT, "num_indices " + std::to_string(num_indices) +
@@ -897,6 +901,8 @@ extern "C" int gemq_dequant_group_gemm_noalloc(const gemq_proj_t* proj, const ui
                                                "), the capacity of the library's static segment table");
   if (num_indices <= 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "num_indices must be positive");
   if (m < 0 || m > INT32_MAX / 2) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad m");
+  if (static_cast<int64_t>(num_indices) * m > INT32_MAX)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "num_indices * m exceeds 2^31 - 1 output rows");
   if (m == 0) return GEMQ_OK;
   if (x == nullptr || out == nullptr || indices == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
   void* scratch = nullptr;

@@ -68,6 +68,31 @@ def test_argument_errors_are_statuses_not_aborts():
     assert rc == _lib.GEMQ_ERR_INVALID_ARGUMENT  # no indices
     rc, _ = _status(lib.gemq_dequant_group_gemm(ctypes.byref(p), 0x3000, 4, 0x4000, 1, 0x5000, 0x6000, 8, None))
     assert rc == _lib.GEMQ_ERR_WORKSPACE
+    # index a's output rows start at a * m, a 32-bit row offset: 600 x 2^22 rows is too many
+    rc, msg = _status(lib.gemq_dequant_group_gemm(ctypes.byref(p), 0x3000, 1 << 22, 0x4000, 600, 0x5000, 0x6000,
+                                                  1 << 20, None))
+    assert rc == _lib.GEMQ_ERR_INVALID_ARGUMENT and "2^31" in msg
+
+
+@pytest.mark.parametrize("num_indices,m,x,out,indices,text", [
+    (1024, 4, 0x3000, 0x5000, 0x4000, "GEMQ_NOALLOC_MAX_INDICES"),
+    (0, 4, 0x3000, 0x5000, 0x4000, "positive"),
+    (-1, 4, 0x3000, 0x5000, 0x4000, "positive"),
+    (600, 1 << 22, 0x3000, 0x5000, 0x4000, "2^31"),
+    (4, 4, None, 0x5000, 0x4000, "null"),
+    (4, 4, 0x3000, None, 0x4000, "null"),
+    (4, 4, 0x3000, 0x5000, None, "null"),
+])
+def test_noalloc_group_gemm_rejects_arguments_before_device_access(num_indices, m, x, out, indices, text):
+    """The allocation-free entry point checks its arguments on the host: these
+    calls get GEMQ_ERR_INVALID_ARGUMENT without a CUDA call (no GPU here)."""
+    from robustgemq_b200 import _lib
+
+    lib = _lib.load()
+    p = _fake_proj()
+    rc, msg = _status(lib.gemq_dequant_group_gemm_noalloc(ctypes.byref(p), x, m, indices, num_indices, out, None))
+    assert rc == _lib.GEMQ_ERR_INVALID_ARGUMENT
+    assert text in msg
 
 
 def _desc(**kw):

@@ -78,6 +78,39 @@ def test_no_alloc_group_gemm_matches_workspace_version():
     assert _lib.device_error() == 0
 
 
+def test_no_alloc_group_gemm_beyond_256_indices():
+    """257-1023 indices run the CUDA-core grouped GEMM (the tensor-core kernel
+    takes up to 256 segments); two calls in a row, 300 then 1023 indices."""
+    from conftest import proj_from
+    from gpu_helpers import proj_tensors
+    from oracle import gemq_oracle as O
+    from robustgemq_b200 import _lib
+
+    lib = _lib.load()
+    d = load_golden("group_gemm.npz")
+    sub = {k[len("g64_"):]: v for k, v in d.items() if k.startswith("g64_")}
+    t = proj_tensors(sub, "w")
+    K, N = int(sub["w_K"]), int(t["wq"].shape[1])
+    p = _proj(t, K, 64)
+    E = t["nbits"].shape[0]
+    rng = np.random.default_rng(11)
+    for A, M in ((300, 3), (1023, 2)):
+        xc = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float16)).cuda()
+        idx = torch.from_numpy(rng.integers(0, E, size=A).astype(np.int32)).cuda()
+        ref = _with_workspace(lib, p, xc, idx, N)
+        out = torch.full((A, M, N), float("nan"), dtype=torch.float16, device="cuda")
+        got = _no_alloc(lib, p, xc, idx, out)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref)
+        # and against the per-index products of the oracle for a few indices
+        op = proj_from(sub, "w")
+        for a in (0, A // 2, A - 1):
+            e = int(idx[a])
+            yo = O.dequant_group_gemm(xc.cpu().numpy(), [e], op)[0]
+            assert rel_l2(got[a].cpu().numpy(), yo) < PRODUCT_REL_TOL
+    assert _lib.device_error() == 0
+
+
 def test_no_alloc_rejects_more_indices_than_the_static_table():
     from robustgemq_b200 import _lib
     from gpu_helpers import proj_tensors
