@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--no-ep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-configs", action="store_true", help="skip the config 0 / config 3 sub-objects")
+    ap.add_argument("--reference-gpu", default="prefill", choices=["none", "prefill", "all"],
+                    help="time the reference's own Triton path beside ours (N=1, when baseline/_ref is installed)")
     return ap.parse_args()
 
 
@@ -318,9 +321,16 @@ def run_ours(args, rank, world, local_rank):
     ep = None
     if not args.no_ep:
         ep = run_ep(args, rank, world, device, bf16_sus)
-    cpu = None
+    configs = None
+    if not args.no_configs:
+        configs = run_configs(blocks[0], device, hbm_peak, bf16_peak)
+    cpu = cpu0 = None
     if rank == 0 and not args.no_cpu:
         cpu = cpu_baseline(blocks[0], inputs, args.cpu_seconds)
+        cpu0 = cpu_config0(blocks[0])
+    ref_gpu = None
+    if world == 1 and args.reference_gpu != "none":
+        ref_gpu = run_reference_gpu(args, blocks[0], device)
     launches = kernel_launches(blocks, batches)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -357,6 +367,12 @@ def run_ours(args, rank, world, local_rank):
         line["expert_parallel"] = ep
     if cpu:
         line["cpu_baseline"] = cpu
+    if configs:
+        line.update(configs)
+    if cpu0:
+        line["cpu_config0"] = cpu0
+    if ref_gpu:
+        line["reference_gpu"] = ref_gpu
     return line
 
 
@@ -369,19 +385,16 @@ def kernel_launches(blocks, batches):
 
 
 def profiled_traffic(kernel: str, batch: int):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary
-    (profiles/k_moe_tcd_olmoe_b64.md), or None when no capture covers it."""
-    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "k_moe_tcd_olmoe_b64.md")
-    key = f"{kernel}_b{batch}"
+    """DRAM bytes per launch of the dominant kernel from one ncu capture, kept as data in
+    profiles/ncu_traffic.json (the capture and its command are summarised beside it),
+    or None when no capture covers it."""
+    path = ROOT / "profiles" / "ncu_traffic.json"
     try:
-        for line in open(path):
-            if line.startswith("traffic_bytes:"):
-                name, val = line.split(":", 1)[1].split()
-                if name == key:
-                    return int(val)
-    except OSError:
+        table = json.loads(path.read_text())["dram_bytes_per_launch"]
+    except (OSError, ValueError, KeyError):
         return None
-    return None
+    v = table.get(f"{kernel}_b{batch}")
+    return int(v) if v is not None else None
 
 
 def run_prefill(args, device, bf16_peak, bf16_sus):
@@ -429,8 +442,9 @@ def run_prefill(args, device, bf16_peak, bf16_sus):
     return {"workload": "qwen3-30b-a3b-shaped prefill, 48 layers, 4096 tokens, Zipf(1.1) router logits (config 2)",
             "layers": L, "tokens": T, "ms_per_pass": round(ms, 3), "tokens_per_s": round(T / (ms * 1e-3), 1),
             "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
-            "frac_bf16_peak": round(flops / (ms * 1e-3) / 1e12 / bf16_sus, 3),
-            "peak_tflops_used": bf16_sus,
+            "frac_bf16_peak": round(flops / (ms * 1e-3) / 1e12 / bf16_peak, 3),
+            "peak_tflops_used": bf16_peak,
+            "frac_bf16_sustained": round(flops / (ms * 1e-3) / 1e12 / bf16_sus, 3),
             "stage_ms_layer0": [round(v, 4) for v in st],
             "up_tflops": round(up_flops / (st[2] * 1e-3) / 1e12, 1) if st[2] > 0 else None,
             "down_tflops": round(dn_flops / (st[3] * 1e-3) / 1e12, 1) if st[3] > 0 else None}
@@ -450,10 +464,15 @@ def run_ep(args, rank, world, device, bf16_sus):
     cfg, shp = synth.mixtral_config()
     L, T = args.ep_layers, args.ep_tokens
     layers = []
+    full0 = None
     for l in range(L):
         blk = synth.random_block(QuantFusedMixtralMoEBlock, cfg, shp["hidden"], shp["inter"], shp["num_experts"],
                                  shp["mean_bits"], shp["group_size"], 7000 + l, device)
         layers.append(ExpertParallelMoE(blk))
+        if l == 0:
+            full0 = blk  # the whole layer, kept to check the sharded forward against
+        else:
+            del blk
     gen = torch.Generator(device=device).manual_seed(900 + rank)
     x = torch.randn((T, shp["hidden"]), generator=gen, device=device).half()
 
@@ -477,16 +496,146 @@ def run_ep(args, rank, world, device, bf16_sus):
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
+    # parity (untimed): the sharded forward of layer 0 against the whole layer run
+    # locally on 256 of this rank's tokens; every rank takes the same collective steps
+    xp = x[:256].contiguous()
+    y_ep, _ = layers[0].forward_tokens(xp)
+    y_full = full0(xp[None])[0][0]
+    err = ((y_ep.double() - y_full.double()).norm() / y_full.double().norm()).reshape(1)
+    if world > 1:
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    del full0
     D, F, k = shp["hidden"], shp["inter"], cfg.num_experts_per_tok
     flops = world * T * L * k * 6 * D * F
     return {"workload": f"mixtral-8x7b-shaped prefill, {L} layers, {T} tokens per rank, experts sharded over "
                         f"{world} rank(s), NCCL all-to-all dispatch/combine (config 4)",
             "layers": L, "tokens_per_rank": T, "n_ranks": world, "ms_per_pass": round(ms, 3),
             "tokens_per_s": round(world * T / (ms * 1e-3), 1), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
-            "frac_bf16_peak_per_gpu": round(flops / world / (ms * 1e-3) / 1e12 / bf16_sus, 3)}
+            "frac_bf16_peak_per_gpu": round(flops / world / (ms * 1e-3) / 1e12 / bf16_sus, 3),
+            "peak_tflops_used": bf16_sus,
+            "parity_rel_l2": float(f"{float(err.item()):.3e}"),
+            "parity": "layer 0, 256 tokens per rank: sharded forward vs the whole layer on one GPU, max over ranks"}
+
+
+def _time_ms(fn, reps):
+    import torch
+
+    fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def run_configs(olmoe_blk, device, hbm_peak, bf16_peak):
+    """Configs 0 and 3 on one GPU, eager through the block API (router included).
+
+    config 0: one OLMoE-shaped layer (a layer of the decode stack), prefill of 512 tokens;
+    config 3: one DeepSeek-V2-Lite-shaped layer (64 routed experts top-6 + 2 shared,
+    F 1408, g 64, mean 2.75 bits, shared 4-bit), prefill of 2048 tokens and decode of 16."""
+    import torch
+
+    from robustgemq_b200 import synth
+    from robustgemq_b200.inference import QuantFusedDeepseekV2MoEBlock
+
+    out = {}
+    g = torch.Generator(device=device).manual_seed(4242)
+    D = olmoe_blk.hidden_dim
+    x0 = torch.randn((1, 512, D), generator=g, device=device).half()
+    ms = _time_ms(lambda: olmoe_blk(x0), 10)
+    F, E, k = olmoe_blk.ffn_dim, olmoe_blk.num_experts, olmoe_blk.top_k
+    flops = 512 * k * 6 * D * F + 2 * 512 * D * E
+    out["config0"] = {"workload": "olmoe-shaped MoE block, prefill of 512 tokens, device router (config 0)",
+                      "ms": round(ms, 4), "tokens_per_s": round(512 / (ms * 1e-3), 1),
+                      "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                      "frac_bf16_peak": round(flops / (ms * 1e-3) / 1e12 / bf16_peak, 3)}
+    cfg, s = synth.deepseek_config()
+    blk = synth.random_block(QuantFusedDeepseekV2MoEBlock, cfg, s["hidden"], s["inter"], s["num_experts"],
+                             s["mean_bits"], s["group_size"], 303, device, shared_inter=s["shared_inter"])
+    D, F, E, k, Fs = s["hidden"], s["inter"], s["num_experts"], cfg.num_experts_per_tok, s["shared_inter"]
+    xp = torch.randn((1, 2048, D), generator=g, device=device).half()
+    ms_p = _time_ms(lambda: blk(xp), 10)
+    flops_p = 2048 * (k * 6 * D * F + 6 * D * Fs + 2 * D * E)
+    xd = torch.randn((16, D), generator=g, device=device).half()
+    ms_d = _time_ms(lambda: blk(xd[None]), 20)
+    eb = synth.layer_expert_bytes(blk)
+    _, idx, _ = blk.route(xd)
+    shared_bytes = sum(getattr(blk, f"shared_{n}_wq").numel() * 4 + 2 * 2 * getattr(blk, f"shared_{n}_scales").numel()
+                       for n in ("w1", "w3", "w2"))
+    bytes_d = sum(eb[e] for e in torch.unique(idx).tolist()) + shared_bytes + E * D * 2 + 2 * 16 * D * 2
+    out["config3"] = {"workload": "deepseek-v2-lite-shaped MoE layer with 2 shared experts (config 3)",
+                      "prefill_tokens": 2048, "prefill_ms": round(ms_p, 4),
+                      "prefill_tokens_per_s": round(2048 / (ms_p * 1e-3), 1),
+                      "prefill_tflops": round(flops_p / (ms_p * 1e-3) / 1e12, 1),
+                      "prefill_frac_bf16_peak": round(flops_p / (ms_p * 1e-3) / 1e12 / bf16_peak, 3),
+                      "decode_batch": 16, "decode_ms": round(ms_d, 4),
+                      "decode_gbs": round(bytes_d / (ms_d * 1e-3) / 1e9, 1),
+                      "decode_frac_hbm": round(bytes_d / (ms_d * 1e-3) / 1e9 / hbm_peak, 3),
+                      "decode_path": "eager block call (no CUDA graph)"}
+    del blk
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_reference_gpu(args, blk, device):
+    """The reference's own GPU path (its Triton kernels JIT-compiled for this B200 with
+    its own autotune, from the unmodified package in baseline/_ref) beside ours on the
+    same OLMoE-shaped layer and inputs: prefill of 512 tokens (config 0), and with
+    ``--reference-gpu all`` the one-token decode path (config 1, batch 1)."""
+    import torch
+
+    from baseline import reference_gpu as RG
+
+    if not RG.available():
+        return {"unavailable": "the reference is not installed in baseline/_ref (or triton is missing)"}
+    ref = RG.reference_block(blk)
+    g = torch.Generator(device=device).manual_seed(512)
+    res = {"source": "baseline/_ref (unmodified gemq package), Triton JIT + autotune on this GPU"}
+    cases = [("prefill_512", 512)] + ([("decode_b1", 1)] if args.reference_gpu == "all" else [])
+    for name, T in cases:
+        x = torch.randn((1, T, blk.hidden_dim), generator=g, device=device).half()
+        t0 = time.time()
+        with torch.no_grad():
+            RG.output(ref(x))
+        torch.cuda.synchronize()
+        first_s = time.time() - t0
+        with torch.no_grad():
+            ms_ref = _time_ms(lambda: RG.output(ref(x)), 5)
+            y_ref = RG.output(ref(x)).reshape(T, -1).double()
+        ms_ours = _time_ms(lambda: RG.output(blk(x)), 20)
+        y = RG.output(blk(x)).reshape(T, -1).double()
+        res[name] = {"tokens": T, "reference_ms": round(ms_ref, 4), "ours_ms": round(ms_ours, 4),
+                     "speedup": round(ms_ref / ms_ours, 1),
+                     "reference_tokens_per_s": round(T / (ms_ref * 1e-3), 1),
+                     "ours_tokens_per_s": round(T / (ms_ours * 1e-3), 1),
+                     "rel_l2_ours_vs_reference": float(f"{float((y - y_ref).norm() / y_ref.norm()):.3e}"),
+                     "reference_first_call_s": round(first_s, 1)}
+    return res
 
 
 # ----------------------------------------------------------------------------- CPU baseline
+def cpu_config0(blk):
+    """Config 0 on the host cores: the reference's fake-quant block (dequantise to fp32 +
+    torch matmul, the forward_n_tokens control flow) over 512 tokens, both with the
+    dequant inside the timed pass and with pre-dequantised weights (matmul only)."""
+    import numpy as np
+    import torch
+
+    from oracle import cpu_baseline as cb
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    layer = cb.layer_from_block(blk)
+    x = np.random.default_rng(512).standard_normal((512, layer.D)).astype(np.float16)
+    r = cb.time_block_prefill(layer, x, reps=3)
+    r.update({"workload": "olmoe-shaped MoE block, prefill of 512 tokens, fp32 (config 0)", "kind": "port",
+              "cores": torch.get_num_threads(), "cpu_model": cb.cpu_model()})
+    return r
+
+
 def cpu_baseline(blk, inputs, seconds):
     """The reference's CPU fake-quant path (dequantise + torch fp32 matmul) on one OLMoE
     layer, timed on this host's cores; sample: one layer at each batch size."""
@@ -495,10 +644,12 @@ def cpu_baseline(blk, inputs, seconds):
 
     from oracle import cpu_baseline as cb
 
+    torch.set_num_threads(os.cpu_count() or 1)  # torchrun sets OMP_NUM_THREADS=1
     layer = cb.layer_from_block(blk)
     xs = {B: v[0][0].float().cpu().numpy() for B, v in inputs.items()}
     r = cb.time_decode(layer, xs, seconds)
     r["cores"] = torch.get_num_threads()
+    r["cpu_model"] = cb.cpu_model()
     return r
 
 
@@ -530,7 +681,8 @@ def run_reference(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "olmoe-16-layer-moe-stack-decode (BASELINE config 1), CPU sample"},
-            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample,
+                             "cpu_model": cb.cpu_model()},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 

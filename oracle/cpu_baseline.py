@@ -94,6 +94,87 @@ def dequant_fp32(p: O.PackedProj, e: int) -> np.ndarray:
     return (q.reshape(ng, p.group_size, p.N) * s + z).reshape(p.K, p.N)
 
 
+def dequant_fp32_torch(p: O.PackedProj, e: int) -> torch.Tensor:
+    """``dequant_fp32`` with torch CPU ops (which use all the host threads torch is given)."""
+    nb = int(p.nbits[e])
+    eps = O.elements_per_word(nb)
+    rows = O.packed_rows(p.K, nb)
+    w0 = int(p.wq_strides[e])
+    words = torch.from_numpy(p.wq.reshape(-1)[w0: w0 + rows * p.N].reshape(rows, p.N).view(np.int32).astype(np.int64))
+    words = words & 0xFFFFFFFF
+    shifts = torch.arange(eps, dtype=torch.int64).view(1, eps, 1) * nb
+    q = ((words.view(rows, 1, p.N) >> shifts) & ((1 << nb) - 1)).reshape(rows * eps, p.N)[: p.K].float()
+    ng = p.K // p.group_size
+    z0 = int(p.zs_strides[e])
+    s = torch.from_numpy(p.scales.reshape(-1)[z0: z0 + ng * p.N].reshape(ng, 1, p.N).astype(np.float32))
+    z = torch.from_numpy(p.zeros.reshape(-1)[z0: z0 + ng * p.N].reshape(ng, 1, p.N).astype(np.float32))
+    return (q.view(ng, p.group_size, p.N) * s + z).reshape(p.K, p.N)
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def block_prefill(layer: CpuLayer, x: torch.Tensor, weights=None) -> torch.Tensor:
+    """``forward_n_tokens`` (moe_block.py:781-815) in fp32 on the CPU: router, then per hit
+    expert (ascending id) SwiGLU with ``F.linear``-equivalent matmuls and ``index_add_``.
+    ``weights`` maps expert -> (W1, W3, W2) fp32 already dequantised (the matmul-only
+    leg); without it every hit expert is dequantised inside the call."""
+    logits = x @ torch.from_numpy(layer.gate.astype(np.float32)).T
+    p = torch.softmax(logits, dim=-1)
+    w, idx = torch.topk(p, layer.k, dim=-1)
+    if layer.norm:
+        w = w / w.sum(dim=-1, keepdim=True)
+    out = torch.zeros_like(x)
+    for e in torch.unique(idx).tolist():
+        tok, slot = torch.nonzero(idx == e, as_tuple=True)
+        if weights is not None:
+            W1, W3, W2 = weights[e]
+        else:
+            W1, W3, W2 = (dequant_fp32_torch(layer.w1, e), dequant_fp32_torch(layer.w3, e),
+                          dequant_fp32_torch(layer.w2, e))
+        xe = x[tok]
+        h = F.silu(xe @ W1) * (xe @ W3)
+        out.index_add_(0, tok, (h @ W2) * w[tok, slot, None])
+    return out
+
+
+def time_block_prefill(layer: CpuLayer, x: np.ndarray, reps: int = 3) -> dict:
+    """Config 0 on the host: one OLMoE-shaped block over ``x`` [T, D] in fp32, timed
+    twice: dequantise + matmul (weights dequantised inside every pass) and matmul only
+    (weights dequantised once beforehand). Median of ``reps`` passes after a warm-up."""
+    xt = torch.from_numpy(np.asarray(x, dtype=np.float32))
+    T = xt.shape[0]
+    flops = T * layer.k * 6 * layer.D * layer.F + 2 * T * layer.D * layer.E
+    res = {}
+    block_prefill(layer, xt)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        block_prefill(layer, xt)
+        ts.append(time.perf_counter() - t0)
+    res["dequant_matmul_ms"] = round(1e3 * float(np.median(ts)), 1)
+    weights = {e: (dequant_fp32_torch(layer.w1, e), dequant_fp32_torch(layer.w3, e), dequant_fp32_torch(layer.w2, e))
+               for e in range(layer.E)}
+    block_prefill(layer, xt, weights)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        block_prefill(layer, xt, weights)
+        ts.append(time.perf_counter() - t0)
+    res["matmul_only_ms"] = round(1e3 * float(np.median(ts)), 1)
+    res["dequant_matmul_tokens_per_s"] = round(T / (res["dequant_matmul_ms"] * 1e-3), 1)
+    res["matmul_only_tokens_per_s"] = round(T / (res["matmul_only_ms"] * 1e-3), 1)
+    res["matmul_only_gflops"] = round(flops / (res["matmul_only_ms"] * 1e-3) / 1e9, 1)
+    return res
+
+
 def decode_layer(layer: CpuLayer, x: np.ndarray) -> int:
     """One fake-quant forward of the layer on x [B, D]; returns the algorithmic bytes."""
     xt = torch.from_numpy(np.asarray(x, dtype=np.float32))
@@ -106,9 +187,9 @@ def decode_layer(layer: CpuLayer, x: np.ndarray) -> int:
     hit = torch.unique(idx).tolist()
     for e in hit:
         tok, slot = torch.nonzero(idx == e, as_tuple=True)
-        W1 = torch.from_numpy(dequant_fp32(layer.w1, e))
-        W3 = torch.from_numpy(dequant_fp32(layer.w3, e))
-        W2 = torch.from_numpy(dequant_fp32(layer.w2, e))
+        W1 = dequant_fp32_torch(layer.w1, e)
+        W3 = dequant_fp32_torch(layer.w3, e)
+        W2 = dequant_fp32_torch(layer.w2, e)
         xe = xt[tok]
         h = F.silu(xe @ W1) * (xe @ W3)
         out.index_add_(0, tok, (h @ W2) * w[tok, slot, None])
