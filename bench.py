@@ -452,27 +452,30 @@ def run_prefill(args, device, bf16_peak, bf16_sus):
 
 def run_ep(args, rank, world, device, bf16_sus):
     """Mixtral-shaped prefill with expert parallelism over all ranks:
-    each rank owns E / world experts and its own ``ep_tokens`` tokens (weak scaling);
-    tokens reach their experts' ranks and return by NCCL all-to-all."""
+    each rank builds and holds only its E / world experts (``ExpertParallelMoE.from_shard``)
+    and routes its own ``ep_tokens`` tokens (weak scaling); tokens reach their experts'
+    ranks and return by NCCL all-to-all. Also reported: the per-step breakdown (max over
+    ranks) and the sharded forward's parity with the whole layer run on one GPU."""
+    from types import SimpleNamespace
+
     import torch
     import torch.distributed as dist
 
     from robustgemq_b200 import synth
     from robustgemq_b200.inference import QuantFusedMixtralMoEBlock
-    from robustgemq_b200.inference.expert_parallel import ExpertParallelMoE
+    from robustgemq_b200.inference.expert_parallel import STAGES, ExpertParallelMoE
 
     cfg, shp = synth.mixtral_config()
     L, T = args.ep_layers, args.ep_tokens
+    E = shp["num_experts"]
+    epr = E // world
+    mine = range(rank * epr, (rank + 1) * epr)
+    local_cfg = SimpleNamespace(**{**vars(cfg), "num_local_experts": epr})
     layers = []
-    full0 = None
     for l in range(L):
-        blk = synth.random_block(QuantFusedMixtralMoEBlock, cfg, shp["hidden"], shp["inter"], shp["num_experts"],
-                                 shp["mean_bits"], shp["group_size"], 7000 + l, device)
-        layers.append(ExpertParallelMoE(blk))
-        if l == 0:
-            full0 = blk  # the whole layer, kept to check the sharded forward against
-        else:
-            del blk
+        blk, gate = synth.random_block_experts(QuantFusedMixtralMoEBlock, local_cfg, shp["hidden"], shp["inter"], E,
+                                               shp["mean_bits"], shp["group_size"], 7000 + l, device, experts=mine)
+        layers.append(ExpertParallelMoE.from_shard(blk, gate, E, time_stages=True))
     gen = torch.Generator(device=device).manual_seed(900 + rank)
     x = torch.randn((T, shp["hidden"]), generator=gen, device=device).half()
 
@@ -493,11 +496,19 @@ def run_ep(args, rank, world, device, bf16_sus):
     e.record()
     torch.cuda.synchronize()
     ms = torch.tensor([s.elapsed_time(e) / reps], device=device)
+    # per-step breakdown of the last layer of the last pass, max over ranks
+    st = layers[-1].stage_times()
+    brk = torch.tensor([st[n] for n in STAGES], device=device)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(brk, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
-    # parity (untimed): the sharded forward of layer 0 against the whole layer run
-    # locally on 256 of this rank's tokens; every rank takes the same collective steps
+    # parity (untimed): layer 0 sharded against the whole layer 0 built on this GPU
+    # (every expert from its own generator, so identical to the union of the shards),
+    # on 256 of this rank's tokens; every rank takes the same collective steps
+    full_cfg = cfg
+    full0, _ = synth.random_block_experts(QuantFusedMixtralMoEBlock, full_cfg, shp["hidden"], shp["inter"], E,
+                                          shp["mean_bits"], shp["group_size"], 7000, device)
     xp = x[:256].contiguous()
     y_ep, _ = layers[0].forward_tokens(xp)
     y_full = full0(xp[None])[0][0]
@@ -505,6 +516,7 @@ def run_ep(args, rank, world, device, bf16_sus):
     if world > 1:
         dist.all_reduce(err, op=dist.ReduceOp.MAX)
     del full0
+    torch.cuda.empty_cache()
     D, F, k = shp["hidden"], shp["inter"], cfg.num_experts_per_tok
     flops = world * T * L * k * 6 * D * F
     return {"workload": f"mixtral-8x7b-shaped prefill, {L} layers, {T} tokens per rank, experts sharded over "
@@ -513,6 +525,7 @@ def run_ep(args, rank, world, device, bf16_sus):
             "tokens_per_s": round(world * T / (ms * 1e-3), 1), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
             "frac_bf16_peak_per_gpu": round(flops / world / (ms * 1e-3) / 1e12 / bf16_sus, 3),
             "peak_tflops_used": bf16_sus,
+            "stage_ms_per_layer_max_over_ranks": {n: round(float(v), 4) for n, v in zip(STAGES, brk.tolist())},
             "parity_rel_l2": float(f"{float(err.item()):.3e}"),
             "parity": "layer 0, 256 tokens per rank: sharded forward vs the whole layer on one GPU, max over ranks"}
 

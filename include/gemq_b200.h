@@ -206,6 +206,32 @@ int gemq_moe_combine(const uint16_t* y, const int32_t* slot_row, const int32_t* 
                      int32_t top_k, int32_t hidden, uint32_t flags, const uint16_t* residual, uint16_t* out,
                      void* stream);
 
+/* Dispatch of forward_n_tokens (moe_block.py:804-810: one_hot / nonzero / where /
+ * gather), exposed for expert parallelism: the T*k token-expert slots grouped by
+ * expert id, ascending. expert_counts int32 [num_experts] (rows per expert, in row
+ * order); slot_row int32 [T*k] (row of slot t*k + j, -1 for an expert id outside
+ * [0, num_experts), which is also recorded in the device error word); w_rows fp16
+ * [T*k] (routing weight of each row); x_rows fp16 [T*k, hidden] (the token's
+ * activation row). Rows of one expert come in no particular order. */
+size_t gemq_dispatch_workspace_size(int64_t num_tokens, int32_t top_k, int32_t num_experts);
+int gemq_moe_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t num_tokens,
+                      int32_t top_k, int32_t num_experts, int32_t hidden, int32_t* expert_counts, int32_t* slot_row,
+                      uint16_t* w_rows, uint16_t* x_rows, void* workspace, size_t workspace_bytes, void* stream);
+
+/* forward_single_expert (moe_block.py:763-779) for every expert of the layer at once,
+ * on rows already grouped by expert: rows fp16 [num_rows, hidden] ordered as
+ * [group 0: expert 0 rows, expert 1 rows, ... | group 1: ...], with
+ * group_counts int32 [num_groups * num_experts] (device) giving the row counts in
+ * that order (an expert-parallel rank: one group per source rank). out fp16
+ * [num_rows, hidden] in the same row order; each row fp16(fp16(y) * row_weight)
+ * (moe_block.py:811) when row_weight (fp16 [num_rows]) is given, else fp16(y).
+ * sm_budget > 0 caps the SMs the GEMMs use (leaves room for a concurrent
+ * collective); 0 = all. num_groups * num_experts <= 1024. */
+size_t gemq_moe_experts_workspace_size(const gemq_layer_t* layer, int64_t num_rows, int32_t num_groups);
+int gemq_moe_experts(gemq_layer_t* layer, const uint16_t* rows, int64_t num_rows, const int32_t* group_counts,
+                     int32_t num_groups, const uint16_t* row_weight, uint16_t* out, int32_t sm_budget,
+                     uint32_t flags, void* workspace, size_t workspace_bytes, void* stream);
+
 /* The whole block: replaces QuantFused*MoEBlock.forward -> forward_n_tokens /
  * forward_one_token (moe_block.py:781-858, 234-309, 540-628, 1011-1088).
  *   x fp16 [T, D] -> out fp16 [T, D]

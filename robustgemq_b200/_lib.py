@@ -47,6 +47,7 @@ EXPORTED = [
     "gemq_gemv_workspace_size", "gemq_dequant_gemv", "gemq_fused_up_proj", "gemq_fused_down_proj",
     "gemq_layer_create", "gemq_layer_destroy", "gemq_moe_workspace_size", "gemq_moe_route",
     "gemq_moe_forward", "gemq_layer_stage_times", "gemq_route", "gemq_moe_combine",
+    "gemq_dispatch_workspace_size", "gemq_moe_dispatch", "gemq_moe_experts_workspace_size", "gemq_moe_experts",
 ]
 
 
@@ -113,6 +114,10 @@ def _declare(lib: ctypes.CDLL) -> None:
         "gemq_layer_stage_times": (ctypes.c_int, [vp, P(ctypes.c_float)]),
         "gemq_route": (ctypes.c_int, [vp, i64, i32, vp, i32, i32, i32, i32, u32, vp, vp, vp, vp, sz, vp]),
         "gemq_moe_combine": (ctypes.c_int, [vp, vp, vp, i64, i32, i32, u32, vp, vp, vp]),
+        "gemq_dispatch_workspace_size": (sz, [i64, i32, i32]),
+        "gemq_moe_dispatch": (ctypes.c_int, [vp, vp, vp, i64, i32, i32, i32, vp, vp, vp, vp, vp, sz, vp]),
+        "gemq_moe_experts_workspace_size": (sz, [vp, i64, i32]),
+        "gemq_moe_experts": (ctypes.c_int, [vp, vp, i64, vp, i32, vp, vp, i32, u32, vp, sz, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

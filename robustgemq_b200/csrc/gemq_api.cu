@@ -835,6 +835,111 @@ int gemq_moe_combine(const uint16_t* y, const int32_t* slot_row, const int32_t* 
   return GEMQ_OK;
 }
 
+size_t gemq_dispatch_workspace_size(int64_t num_tokens, int32_t top_k, int32_t num_experts) {
+  (void)num_tokens;
+  (void)top_k;
+  if (num_experts <= 0) return 0;
+  Carver c(nullptr);
+  c.take<int32_t>(num_experts);  // cursor
+  c.take<Seg>(num_experts);
+  c.take<int32_t>(num_experts + 1);
+  return c.off + 256;
+}
+
+int gemq_moe_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t num_tokens,
+                      int32_t top_k, int32_t num_experts, int32_t hidden, int32_t* expert_counts, int32_t* slot_row,
+                      uint16_t* w_rows, uint16_t* x_rows, void* workspace, size_t workspace_bytes, void* stream) {
+  TraceRange trace("gemq_moe_dispatch");
+  if (num_tokens < 0 || top_k <= 0 || top_k > 16) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad token or top_k count");
+  if (num_experts <= 0 || num_experts > 256) return fail(GEMQ_ERR_UNSUPPORTED, "num_experts must be in [1, 256]");
+  if (hidden <= 0 || hidden % 8 != 0) return fail(GEMQ_ERR_UNSUPPORTED, "hidden size must be a positive multiple of 8");
+  if (num_tokens * top_k > INT32_MAX / 2) return fail(GEMQ_ERR_UNSUPPORTED, "too many tokens");
+  if (expert_counts == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (num_tokens == 0) {
+    GEMQ_CUDA(cudaMemsetAsync(expert_counts, 0, sizeof(int32_t) * num_experts, s), "zero counts");
+    return GEMQ_OK;
+  }
+  if (topk_idx == nullptr || topk_w == nullptr || x == nullptr || slot_row == nullptr || w_rows == nullptr ||
+      x_rows == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(x_rows)) & 15u)
+    return fail(GEMQ_ERR_UNSUPPORTED, "x and x_rows must be 16-byte aligned");
+  if (workspace == nullptr || workspace_bytes < gemq_dispatch_workspace_size(num_tokens, top_k, num_experts))
+    return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
+  Carver c(workspace);
+  int32_t* cursor = c.take<int32_t>(num_experts);
+  Seg* segs = c.take<Seg>(num_experts);
+  int32_t* tp = c.take<int32_t>(num_experts + 1);
+  GEMQ_CUDA(launch_dispatch(topk_idx, topk_w, x, num_tokens, top_k, num_experts, hidden, kNtLarge, expert_counts,
+                            cursor, segs, tp, slot_row, w_rows, x_rows, nullptr, nullptr, s),
+            "dispatch");
+  return GEMQ_OK;
+}
+
+size_t gemq_moe_experts_workspace_size(const gemq_layer_t* layer, int64_t num_rows, int32_t num_groups) {
+  if (layer == nullptr || num_rows < 0 || num_groups <= 0) return 0;
+  const int n = num_groups * layer->d.num_experts;
+  Carver c(nullptr);
+  c.take<Seg>(n);
+  c.take<int32_t>(n + 1);
+  c.take<uint16_t>(static_cast<size_t>(num_rows > 0 ? num_rows : 1) * layer->d.inter);
+  return c.off + 256;
+}
+
+int gemq_moe_experts(gemq_layer_t* layer, const uint16_t* rows, int64_t num_rows, const int32_t* group_counts,
+                     int32_t num_groups, const uint16_t* row_weight, uint16_t* out, int32_t sm_budget,
+                     uint32_t flags, void* workspace, size_t workspace_bytes, void* stream) {
+  TraceRange trace("gemq_moe_experts");
+  if (layer == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null layer");
+  if (num_rows < 0 || num_groups <= 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad row or group count");
+  if (num_rows == 0) return GEMQ_OK;
+  if (num_rows > INT32_MAX / 2) return fail(GEMQ_ERR_UNSUPPORTED, "too many rows");
+  const gemq_layer_desc_t& d = layer->d;
+  const int E = d.num_experts;
+  if (static_cast<int64_t>(num_groups) * E > 1024) return fail(GEMQ_ERR_UNSUPPORTED, "num_groups * experts > 1024");
+  if (rows == nullptr || group_counts == nullptr || out == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  if ((reinterpret_cast<uintptr_t>(rows) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(GEMQ_ERR_UNSUPPORTED, "rows and out must be 16-byte aligned");
+  if (workspace == nullptr || workspace_bytes < gemq_moe_experts_workspace_size(layer, num_rows, num_groups))
+    return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int n = num_groups * E;
+  Carver c(workspace);
+  Seg* segs = c.take<Seg>(n);
+  int32_t* tp = c.take<int32_t>(n + 1);
+  uint16_t* h = c.take<uint16_t>(static_cast<size_t>(num_rows) * d.inter);
+  const bool force_simt = (flags & GEMQ_FWD_FORCE_SIMT) != 0;
+  GemmArgs up{};
+  up.mode = GemmMode::kSwiGLU;
+  up.w0 = layer->w1;
+  up.w1 = layer->w3;
+  up.act = rows;
+  up.act_rows = num_rows;
+  up.segs = segs;
+  up.tile_prefix = tp;
+  up.num_segs = n;
+  up.out = h;
+  up.out_ld = d.inter;
+  up.out_cols = d.inter;
+  up.num_sms = (sm_budget > 0 && sm_budget < layer->num_sms) ? sm_budget : layer->num_sms;
+  up.nt = choose_nt(num_rows / n);
+  GemmArgs dn = up;
+  dn.mode = row_weight != nullptr ? GemmMode::kRouteWeight : GemmMode::kStoreF16;
+  dn.w0 = dn.w1 = layer->w2;
+  dn.act = h;
+  dn.out = out;
+  dn.out_ld = d.hidden;
+  dn.out_cols = d.hidden;
+  dn.row_weight = row_weight;
+  const bool tc = !force_simt && tc_gemm_supported(up) && tc_gemm_supported(dn);
+  if (!tc) up.nt = dn.nt = 32;
+  GEMQ_CUDA(launch_group_segs(group_counts, n, E, up.nt, segs, tp, s), "segments");
+  if (int rc = run_gemm(up, !tc, s, "up projection")) return rc;
+  return run_gemm(dn, !tc, s, "down projection");
+}
+
 int gemq_layer_stage_times(gemq_layer_t* layer, float* ms_out) {
   if (layer == nullptr || ms_out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
   for (int st = 0; st < GEMQ_NUM_STAGES; ++st) ms_out[st] = 0.f;

@@ -132,6 +132,9 @@ cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16
 cudaError_t launch_topk(const void* logits, bool logits_fp32, int64_t T, int E, int k, bool norm, bool fp16_softmax,
                         int32_t* topk_idx, uint16_t* topk_w, cudaStream_t stream);
 bool small_dispatch_ok(int64_t P, int E);
+// Segments of rows grouped as [group][expert] (n = groups * E counts, n <= 1024).
+cudaError_t launch_group_segs(const int32_t* counts, int n, int E, int nt, Seg* segs, int32_t* tile_prefix,
+                              cudaStream_t stream);
 cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t T, int k,
                             int E, int D, int nt, int32_t* counts, int32_t* cursor, Seg* segs, int32_t* tile_prefix,
                             int32_t* slot_pos, uint16_t* w_perm, uint16_t* x_perm, const int32_t* perm_nbits,

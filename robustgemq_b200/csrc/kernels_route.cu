@@ -564,6 +564,47 @@ cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16
 }
 
 
+// ------------------------------------------------------------------ grouped segments
+// Rows arrive grouped as [group 0: expert 0 rows, expert 1 rows, ... | group 1: ...]
+// (expert parallelism: one group per source rank, each sorted by local expert).
+// Segment g * E + e covers the rows of expert e in group g; one block scans the
+// G * E counts (at most 1024) into row starts and token-tile starts.
+__global__ void k_group_segs(const int32_t* __restrict__ counts, int n, int E, int nt, Seg* __restrict__ segs,
+                             int32_t* __restrict__ tile_prefix) {
+  grid_dep_wait();
+  __shared__ int s_rows[1024];
+  __shared__ int s_tiles[1024];
+  const int i = threadIdx.x;
+  int c = (i < n) ? counts[i] : 0;
+  if (c < 0) {
+    set_device_error(kDevBadExpert);
+    c = 0;
+  }
+  s_rows[i] = c;
+  s_tiles[i] = (c + nt - 1) / nt;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int a = (i >= off) ? s_rows[i - off] : 0;
+    const int b = (i >= off) ? s_tiles[i - off] : 0;
+    __syncthreads();
+    s_rows[i] += a;
+    s_tiles[i] += b;
+    __syncthreads();
+  }
+  if (i < n) {
+    const int start = s_rows[i] - c;
+    segs[i] = make_int4(i % E, start, start, c);
+    tile_prefix[i] = s_tiles[i] - (c + nt - 1) / nt;
+    if (i == n - 1) tile_prefix[n] = s_tiles[i];
+  }
+}
+
+cudaError_t launch_group_segs(const int32_t* counts, int n, int E, int nt, Seg* segs, int32_t* tile_prefix,
+                              cudaStream_t stream) {
+  if (n <= 0 || n > 1024 || E <= 0) return cudaErrorInvalidValue;
+  return launch_dep(k_group_segs, dim3(1), dim3(1024), 0, stream, counts, n, E, nt, segs, tile_prefix);
+}
+
 bool small_dispatch_ok(int64_t P, int E) { return P <= kSmallDispatchMaxSlots && E <= kMaxExperts; }
 
 cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t T, int k,

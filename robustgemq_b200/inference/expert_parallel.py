@@ -2,17 +2,24 @@
 
 Rank ``r`` of ``P`` holds experts ``[r * E / P, (r + 1) * E / P)`` of every
 projection (the stacked packed layout of ``from_hf``, sliced by expert with its
-strides rebased). A forward on a rank's own tokens:
+strides rebased, or built from the rank's experts alone with ``from_shard``). A
+forward on a rank's own tokens:
 
 1. routes them over all ``E`` experts (``gemq_route``; the gate is replicated);
-2. orders the ``T * k`` token-expert slots by the rank owning the expert and sends
-   each slot's activation row, local expert id and routing weight there with
-   ``all_to_all_single`` (counts first);
-3. the owner runs its local experts on the rows it received, one expert per row
-   (``gemq_moe_forward`` with given routing and ``top_k = 1``, whose output row is
-   exactly ``fp16(fp16(y) * w)``: the down projection's route-weight epilogue);
-4. sends the rows back with the reverse ``all_to_all_single``;
-5. combines each token's ``k`` rows in ascending expert id with fp16 rounding after
+2. groups the ``T * k`` token-expert slots by expert id on the device
+   (``gemq_moe_dispatch``: histogram, scan, scatter of the activation rows and
+   routing weights). Experts are contiguous per rank, so the rows come out grouped
+   by destination rank and, inside each destination, by its local expert;
+3. exchanges the per-expert row counts (with this rank's routing status) in one
+   ``all_to_all_single`` and reads them to the host: the one host synchronisation
+   of the forward, which sizes the exchanges that follow;
+4. sends the activation rows and their routing weights to their owners;
+5. the owner runs its experts on the rows it received, grouped as [source rank]
+   [local expert] (``gemq_moe_experts``: the segment table built on the device from
+   the received counts, then the gate/up and down GEMMs; each output row is exactly
+   ``fp16(fp16(y) * w)``, the down projection's route-weight epilogue);
+6. sends the rows back with the reverse ``all_to_all_single``;
+7. combines each token's ``k`` rows in ascending expert id with fp16 rounding after
    every add (``gemq_moe_combine``): the fp16 ``index_add_`` order of
    ``forward_n_tokens`` (moe_block.py:799-812), so a rank's output equals the 1-GPU
    block's on the same tokens whenever the per-row GEMM results do.
@@ -20,10 +27,13 @@ strides rebased). A forward on a rank's own tokens:
 DeepSeek's shared experts are replicated and run on the token's own rank; their
 output is added in fp16 after the combine (moe_block.py:575).
 
+``time_stages=True`` records CUDA events around steps 1-7 (route, dispatch, counts,
+rows out, experts, rows back, combine); ``stage_times()`` returns their durations.
+
 Failures end in ``ExpertParallelError`` on every rank, never in a hang:
 
 * an invalid routing table on one rank (an expert id outside ``[0, E)``) travels
-  with the counts of step 2 as a per-peer status, so every rank learns of it in
+  with the counts of step 3 as a per-peer status, so every rank learns of it in
   the same exchange and raises before any row is sent; all ranks took the same
   collective steps, so the group stays usable for the next forward;
 * a rank that is gone or never joins ends the others' pending exchange through
@@ -31,15 +41,15 @@ Failures end in ``ExpertParallelError`` on every rank, never in a hang:
   step, and the wrapper refuses further forwards, since the group's state is no
   longer known (rebuild the group and the wrapper).
 
-With NCCL the exchange runs over NVLink; with gloo (CPU tests) the local expert
-compute, the router and the combine can be replaced by callables (``route_fn``,
-``experts_fn``, ``combine_fn``) so the dispatch / combine bookkeeping is tested
-without a GPU. The defaults are the CUDA kernels; there is no CPU fallback.
+With NCCL the exchange runs over NVLink; with gloo (CPU tests) the router, the
+dispatch, the local expert compute and the combine can be replaced by callables
+(``route_fn``, ``dispatch_fn``, ``experts_fn``, ``combine_fn``) so the exchange
+bookkeeping is tested without a GPU. The defaults are the CUDA kernels; there is
+no CPU fallback.
 """
 
 from __future__ import annotations
 
-import ctypes
 from typing import Callable, Optional, Tuple
 
 import torch
@@ -53,19 +63,6 @@ from .moe_block import _QuantFusedMoEBlock
 
 class ExpertParallelError(RuntimeError):
     """An expert-parallel forward failed: invalid routing on some rank, or a failed exchange."""
-
-
-def plan_dispatch(topk_idx: Tensor, experts_per_rank: int, world: int) -> Tuple[Tensor, Tensor, Tensor]:
-    """Send order of the ``T * k`` slots (stable, grouped by destination rank), the
-    per-rank slot counts, and each sent slot's expert id local to its destination."""
-    flat = topk_idx.reshape(-1).to(torch.int64)
-    dest = torch.div(flat, experts_per_rank, rounding_mode="floor")
-    if bool(((dest < 0) | (dest >= world)).any()):
-        raise ValueError("expert id out of range for the expert-parallel layout")
-    order = torch.argsort(dest, stable=True)
-    counts = torch.bincount(dest, minlength=world)
-    local = (flat - dest * experts_per_rank)[order]
-    return order, counts, local
 
 
 def slice_projection(block: _QuantFusedMoEBlock, name: str, e0: int, e1: int, k: int) -> dict:
@@ -99,34 +96,68 @@ class _LocalExperts(_QuantFusedMoEBlock):
         self._init_common(hidden, ffn, num_experts, 1, False)
 
 
+STAGES = ("route", "dispatch", "counts", "rows_out", "experts", "rows_back", "combine")
+
+
 class ExpertParallelMoE(nn.Module):
     """Expert-parallel wrapper of a ``QuantFused*MoEBlock`` (see the module docstring)."""
 
-    def __init__(self, block: _QuantFusedMoEBlock, group=None, route_fn: Optional[Callable] = None,
-                 experts_fn: Optional[Callable] = None, combine_fn: Optional[Callable] = None):
+    def __init__(self, block: Optional[_QuantFusedMoEBlock], group=None, route_fn: Optional[Callable] = None,
+                 experts_fn: Optional[Callable] = None, combine_fn: Optional[Callable] = None,
+                 dispatch_fn: Optional[Callable] = None, time_stages: bool = False, sm_budget: int = 0,
+                 _shard: Optional[tuple] = None):
         super().__init__()
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
-        E = block.num_experts
+        if _shard is not None:
+            local_block, gate_weight, E = _shard
+            src = local_block
+        else:
+            src = block
+            E = block.num_experts
+            gate_weight = block.gate.weight
         if E % self.world != 0:
             raise ValueError(f"{E} experts do not split evenly over {self.world} ranks")
-        self.num_experts, self.top_k = E, block.top_k
-        self.hidden_dim, self.ffn_dim = block.hidden_dim, block.ffn_dim
+        self.num_experts, self.top_k = E, src.top_k
+        self.hidden_dim, self.ffn_dim = src.hidden_dim, src.ffn_dim
         self.experts_per_rank = E // self.world
         self.e0 = self.rank * self.experts_per_rank
-        self.router_fp32 = block.router_fp32
-        self.norm = bool(block.norm_topk_prob or block.always_normalize)
-        self.returns_logits = block.returns_logits
-        self.gate_weight = block.gate.weight.detach().to(torch.float16).contiguous()
-        self.shared = block if getattr(block, "has_shared", False) else None
-        self.local = _LocalExperts(block.hidden_dim, block.ffn_dim, self.experts_per_rank)
-        if block.w1_wq is not None:
-            self._load_local(block)
+        self.router_fp32 = src.router_fp32
+        self.norm = bool(src.norm_topk_prob or src.always_normalize)
+        self.returns_logits = src.returns_logits
+        self.gate_weight = gate_weight.detach().to(torch.float16).contiguous()
+        self.shared = src if getattr(src, "has_shared", False) else None
+        if _shard is not None:
+            if local_block.num_experts != self.experts_per_rank:
+                raise ValueError(f"a shard holds {self.experts_per_rank} experts, got {local_block.num_experts}")
+            self.local = _LocalExperts(src.hidden_dim, src.ffn_dim, self.experts_per_rank)
+            for name in ("w1", "w2", "w3"):
+                for key in ("wq", "scales", "zeros", "nbits", "group_sizes", "wq_strides", "zs_strides"):
+                    setattr(self.local, f"{name}_{key}", getattr(local_block, f"{name}_{key}"))
+            self.local.block_group_size = local_block.block_group_size
+            self.local.invalidate()
+        else:
+            self.local = _LocalExperts(block.hidden_dim, block.ffn_dim, self.experts_per_rank)
+            if block.w1_wq is not None:
+                self._load_local(block)
         self.route_fn = route_fn or self._route
+        self.dispatch_fn = dispatch_fn or self._dispatch
         self.experts_fn = experts_fn or self._experts
         self.combine_fn = combine_fn or self._combine
+        self.time_stages = time_stages
+        self.sm_budget = int(sm_budget)
+        self._events = None
         self._broken: Optional[str] = None  # set when an exchange failed
+
+    @classmethod
+    def from_shard(cls, local_block: _QuantFusedMoEBlock, gate_weight: Tensor, num_experts: int, group=None,
+                   **kw) -> "ExpertParallelMoE":
+        """Build from this rank's experts alone: ``local_block`` holds experts
+        ``[rank * E / P, (rank + 1) * E / P)`` (its own gate is not used), and
+        ``gate_weight`` is the full ``[E, hidden]`` router weight. No rank ever holds
+        the whole layer."""
+        return cls(None, group=group, _shard=(local_block, gate_weight, num_experts), **kw)
 
     def _load_local(self, block: _QuantFusedMoEBlock):
         e1 = self.e0 + self.experts_per_rank
@@ -151,10 +182,32 @@ class ExpertParallelMoE(nn.Module):
                                      stream_ptr(x.device)))
         return logits, idx, w
 
-    def _experts(self, rows: Tensor, local_ids: Tensor, weights: Tensor) -> Tensor:
+    def _dispatch(self, idx: Tensor, w: Tensor, x: Tensor):
+        T, k, E, D = x.shape[0], self.top_k, self.num_experts, self.hidden_dim
+        P = T * k
+        counts = torch.empty(E, dtype=torch.int32, device=x.device)
+        slot_row = torch.empty(max(P, 1), dtype=torch.int32, device=x.device)
+        w_rows = torch.empty(max(P, 1), dtype=torch.float16, device=x.device)
+        x_rows = torch.empty((max(P, 1), D), dtype=torch.float16, device=x.device)
+        lib = _lib.load()
+        ws = torch.empty(lib.gemq_dispatch_workspace_size(T, k, E), dtype=torch.uint8, device=x.device)
+        check(lib.gemq_moe_dispatch(ptr(idx), ptr(w), ptr(x), T, k, E, D, ptr(counts), ptr(slot_row), ptr(w_rows),
+                                    ptr(x_rows), ptr(ws), ws.numel(), stream_ptr(x.device)))
+        return counts, slot_row[:P], w_rows[:P], x_rows[:P]
+
+    def _experts(self, rows: Tensor, group_counts: Tensor, weights: Tensor) -> Tensor:
         if rows.shape[0] == 0:
             return rows.clone()
-        return self.local.forward_routed(rows, local_ids.reshape(-1, 1), weights.reshape(-1, 1))
+        lib = _lib.load()
+        handle = self.local.layer_handle()
+        G = group_counts.shape[0]
+        out = torch.empty_like(rows)
+        gc = group_counts.to(device=rows.device, dtype=torch.int32).contiguous()
+        ws = torch.empty(lib.gemq_moe_experts_workspace_size(handle, rows.shape[0], G), dtype=torch.uint8,
+                         device=rows.device)
+        check(lib.gemq_moe_experts(handle, ptr(rows), rows.shape[0], ptr(gc), G, ptr(weights.contiguous()), ptr(out),
+                                   self.sm_budget, 0, ptr(ws), ws.numel(), stream_ptr(rows.device)))
+        return out
 
     def _combine(self, y: Tensor, slot_row: Tensor, topk_idx: Tensor, residual: Optional[Tensor]) -> Tensor:
         T = topk_idx.shape[0]
@@ -179,45 +232,59 @@ class ExpertParallelMoE(nn.Module):
             raise ExpertParallelError(self._broken) from exc
         return recv
 
+    def _mark(self, i: int, device) -> None:
+        if not self.time_stages or device.type != "cuda":
+            return
+        if self._events is None:
+            self._events = [torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)]
+        self._events[i].record()
+
+    def stage_times(self) -> dict:
+        """Durations (ms) of the last forward's steps (``time_stages=True``, CUDA only)."""
+        if self._events is None:
+            return {}
+        self._events[-1].synchronize()
+        return {name: self._events[i].elapsed_time(self._events[i + 1]) for i, name in enumerate(STAGES)}
+
     def forward_tokens(self, x: Tensor) -> Tuple[Tensor, Tensor]:
         """``x [T, D]`` fp16 on this rank -> ``(out [T, D], router_logits [T, E])``."""
         if self._broken is not None:
             raise ExpertParallelError(f"an earlier exchange failed ({self._broken}); rebuild the process group")
         x = x.contiguous()
-        T, k = x.shape[0], self.top_k
+        dev = x.device
+        epr, W = self.experts_per_rank, self.world
+        self._mark(0, dev)
         logits, idx, w = self.route_fn(x)
+        self._mark(1, dev)
         flat = idx.reshape(-1)
-        valid = not bool(((flat < 0) | (flat >= self.num_experts)).any())
-        if valid:
-            order, send_counts, local_ids = plan_dispatch(idx, self.experts_per_rank, self.world)
-        else:  # send no rows; the status below tells every peer
-            order = torch.arange(T * k, device=x.device)
-            send_counts = torch.zeros(self.world, dtype=torch.int64)
-            local_ids = torch.zeros(T * k, dtype=torch.int64)
-        order = order.to(x.device)
-        # counts first, so every rank can size its receive buffers, each sent with
-        # this rank's routing status
-        sc = send_counts.to(device=x.device, dtype=torch.int64)
-        msg = torch.stack([sc, torch.full_like(sc, 0 if valid else 1)], dim=1).reshape(-1)
-        rmsg = self._a2a(msg, [2] * self.world, [2] * self.world, "counts").reshape(self.world, 2)
-        bad = [r for r in range(self.world) if int(rmsg[r, 1]) != 0]
-        if bad:
+        bad = ((flat < 0) | (flat >= self.num_experts)).any().to(torch.int32).reshape(1)
+        counts, slot_row, w_rows, x_rows = self.dispatch_fn(idx, w, x)
+        self._mark(2, dev)
+        # counts first, each destination's block with this rank's routing status, so
+        # every rank can size its receives; the only host synchronisation
+        msg = torch.cat([counts.to(torch.int32).reshape(W, epr), bad.to(counts.device).expand(W, 1)], dim=1)
+        rmsg = self._a2a(msg.reshape(-1), [epr + 1] * W, [epr + 1] * W, "counts").reshape(W, epr + 1)
+        both = torch.stack([msg, rmsg]).cpu()
+        self._mark(3, dev)
+        bad_ranks = [r for r in range(W) if int(both[1, r, epr]) != 0]
+        if bad_ranks:
             raise ExpertParallelError(
-                f"invalid routing table (expert id outside [0, {self.num_experts})) on rank(s) {bad}; "
+                f"invalid routing table (expert id outside [0, {self.num_experts})) on rank(s) {bad_ranks}; "
                 "no rows were exchanged")
-        send_counts, recv_counts = sc.tolist(), rmsg[:, 0].tolist()
-        tok = torch.div(order, k, rounding_mode="floor")
-        rows = self._a2a(x.index_select(0, tok), send_counts, recv_counts, "activation rows")
-        ids = self._a2a(local_ids.to(device=x.device, dtype=torch.int32), send_counts, recv_counts, "expert ids")
-        wts = self._a2a(w.reshape(-1).index_select(0, order), send_counts, recv_counts, "routing weights")
-        y = self.experts_fn(rows, ids, wts)
+        send_counts = both[0, :, :epr].sum(dim=1).tolist()
+        recv_counts = both[1, :, :epr].sum(dim=1).tolist()
+        rows = self._a2a(x_rows, send_counts, recv_counts, "activation rows")
+        wts = self._a2a(w_rows, send_counts, recv_counts, "routing weights")
+        self._mark(4, dev)
+        y = self.experts_fn(rows, rmsg[:, :epr], wts)
+        self._mark(5, dev)
         back = self._a2a(y, recv_counts, send_counts, "expert outputs")
-        slot_row = torch.empty(T * k, dtype=torch.int32, device=x.device)
-        slot_row[order] = torch.arange(T * k, dtype=torch.int32, device=x.device)
+        self._mark(6, dev)
         residual = None
         if self.shared is not None:
             residual = self.shared.forward_shared(x)
         out = self.combine_fn(back, slot_row, idx.to(torch.int32).contiguous(), residual)
+        self._mark(7, dev)
         return out, logits
 
     def forward(self, hidden_states: Tensor):

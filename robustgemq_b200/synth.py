@@ -61,6 +61,29 @@ def random_block(family_cls, config, hidden: int, inter: int, num_experts: int, 
     return blk
 
 
+def random_block_experts(family_cls, config, hidden: int, inter: int, num_experts: int, mean_bits: float,
+                         group_size: int, seed: int, device, experts=None):
+    """A block holding only ``experts`` (default: all) of a synthetic layer whose experts
+    are each drawn from their own generator (seed, expert), so any subset, on any rank,
+    equals the same experts of the whole layer. The config's expert count must match
+    ``len(experts)``; the gate ``[num_experts, hidden]`` of the whole layer is returned
+    beside the block."""
+    experts = list(range(num_experts)) if experts is None else list(experts)
+    bits = bit_mix(num_experts, mean_bits, seed)
+    w1, w3, w2 = [], [], []
+    for e in experts:
+        gen = torch.Generator(device=device).manual_seed(seed * 100003 + e)
+        w1.append(random_packed_linear(inter, hidden, bits[e], group_size, gen, device))
+        w3.append(random_packed_linear(inter, hidden, bits[e], group_size, gen, device))
+        w2.append(random_packed_linear(hidden, inter, bits[e], group_size, gen, device))
+    g = torch.Generator(device=device).manual_seed(seed * 100003 + num_experts)
+    gate = (torch.randn((num_experts, hidden), generator=g, device=device) * 0.02).half()
+    blk = family_cls.from_packed(config, gate[experts[0]:experts[0] + len(experts)], w1, w3, w2)
+    blk.gate.to(device)
+    blk.bits = [bits[e] for e in experts]
+    return blk, gate
+
+
 # ----------------------------------------------------------------------------- configs
 def olmoe_config():
     """OLMoE-1B-7B-shaped block (BASELINE configs 0/1)."""

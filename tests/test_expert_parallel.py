@@ -45,16 +45,30 @@ def _oracle_weights(d):
                           top_k=int(d["top_k"]), norm_topk_prob=bool(d["norm_topk_prob"]))
 
 
-def test_plan_dispatch_orders_slots_by_owner():
-    from robustgemq_b200.inference.expert_parallel import plan_dispatch
+def cpu_dispatch(idx, w, x, num_experts):
+    """Slots grouped by expert id (stable), as gemq_moe_dispatch groups them; an id
+    outside [0, E) gets no row and slot_row -1."""
+    k = idx.shape[1]
+    flat = idx.reshape(-1).to(torch.int64)
+    valid = (flat >= 0) & (flat < num_experts)
+    order = torch.argsort(torch.where(valid, flat, num_experts), stable=True)
+    nvalid = int(valid.sum())
+    counts = torch.bincount(flat[valid], minlength=num_experts).to(torch.int32)
+    slot_row = torch.full((flat.numel(),), -1, dtype=torch.int32)
+    slot_row[order[:nvalid]] = torch.arange(nvalid, dtype=torch.int32)
+    sel = order[:nvalid]
+    return counts, slot_row, w.reshape(-1)[sel], x[torch.div(sel, k, rounding_mode="floor")]
 
-    idx = torch.tensor([[5, 0], [2, 7], [3, 4]])
-    order, counts, local = plan_dispatch(idx, experts_per_rank=4, world=2)
-    assert counts.tolist() == [3, 3]
-    assert order.tolist() == [1, 2, 4, 0, 3, 5]  # stable inside each destination
-    assert local.tolist() == [0, 2, 3, 1, 3, 0]
-    with pytest.raises(ValueError):
-        plan_dispatch(torch.tensor([[8]]), experts_per_rank=4, world=2)
+
+def test_cpu_dispatch_groups_slots_by_expert():
+    idx = torch.tensor([[5, 0], [2, 7], [3, 4], [0, 9]], dtype=torch.int32)
+    w = torch.arange(8, dtype=torch.float16).reshape(4, 2)
+    x = torch.arange(4, dtype=torch.float16).reshape(4, 1).expand(4, 8).contiguous()
+    counts, slot_row, w_rows, x_rows = cpu_dispatch(idx, w, x, 8)
+    assert counts.tolist() == [2, 0, 1, 1, 1, 1, 0, 1]
+    assert slot_row.tolist() == [5, 0, 2, 6, 3, 4, 1, -1]
+    assert w_rows.tolist() == [1, 6, 2, 4, 5, 0, 3]
+    assert x_rows[:, 0].tolist() == [0, 3, 1, 2, 2, 0, 1]
 
 
 def test_slice_projection_keeps_each_experts_dequant():
@@ -96,13 +110,21 @@ def _cpu_ep(route_hook=None):
             idx = route_hook(idx)
         return torch.from_numpy(r.logits), torch.from_numpy(idx), torch.from_numpy(r.topk_w)
 
-    def experts_fn(rows, ids, wts):
-        rows_np, ids_np, w_np = rows.numpy(), ids.numpy(), wts.numpy()
+    def dispatch_fn(idx, w, x):
+        return cpu_dispatch(idx, w, x, ow.w1.num_experts)
+
+    def experts_fn(rows, group_counts, wts):
+        # rows arrive grouped as [source rank][local expert]
+        rows_np, gc, w_np = rows.numpy(), group_counts.numpy(), wts.numpy()
         y = np.zeros_like(rows_np)
-        for e in np.unique(ids_np):
-            sel = np.nonzero(ids_np == e)[0]
-            ye = O.expert_ffn_n_tokens(ow, ep.e0 + int(e), rows_np[sel])
-            y[sel] = (ye.astype(F32) * w_np[sel].astype(F32)[:, None]).astype(F16)
+        off = 0
+        for g in range(gc.shape[0]):
+            for e in range(gc.shape[1]):
+                c = int(gc[g, e])
+                if c:
+                    ye = O.expert_ffn_n_tokens(ow, ep.e0 + e, rows_np[off:off + c])
+                    y[off:off + c] = (ye.astype(F32) * w_np[off:off + c].astype(F32)[:, None]).astype(F16)
+                off += c
         return torch.from_numpy(y)
 
     def combine_fn(y, slot_row, idx, residual):
@@ -114,7 +136,8 @@ def _cpu_ep(route_hook=None):
                 out[t] = (out[t].astype(F32) + y_np[sr[t * k + j]].astype(F32)).astype(F16)
         return torch.from_numpy(out)
 
-    ep = ExpertParallelMoE(blk, route_fn=route_fn, experts_fn=experts_fn, combine_fn=combine_fn)
+    ep = ExpertParallelMoE(blk, route_fn=route_fn, experts_fn=experts_fn, combine_fn=combine_fn,
+                           dispatch_fn=dispatch_fn)
     return ep, ow, d
 
 
@@ -266,12 +289,30 @@ def test_expert_parallel_one_rank_matches_block_on_gpu():
     blk, d = _golden_block("cuda")
     x = torch.from_numpy(d["x"].astype(F16)).cuda()
     ref, ref_logits = blk.forward_n_tokens(x.unsqueeze(0))
-    ep = ExpertParallelMoE(blk)
+    ep = ExpertParallelMoE(blk, time_stages=True)
     out, logits = ep.forward_tokens(x)
     torch.cuda.synchronize()
+    # the received rows go through the grouped GEMM (the block's decode-batch GEMM
+    # reads K in another order): equal up to fp32 summation order
     assert rel_l2(out.cpu().numpy(), ref[0].cpu().numpy()) < 1e-3
-    assert torch.equal(out, ref[0])  # same kernels per row, same combine order
     assert torch.equal(logits, ref_logits)
+    st = ep.stage_times()
+    assert set(st) == {"route", "dispatch", "counts", "rows_out", "experts", "rows_back", "combine"}
+    assert all(v >= 0 for v in st.values())
+    # a shard built from this rank's experts alone gives the same result
+    from robustgemq_b200.inference.expert_parallel import slice_projection
+    from gpu_helpers import family_config
+    from robustgemq_b200.inference import QuantFusedOlmoeMoEBlock
+
+    cfg = family_config("olmoe", d)
+    loc = QuantFusedOlmoeMoEBlock(cfg)
+    for name, kk in (("w1", blk.hidden_dim), ("w3", blk.hidden_dim), ("w2", blk.ffn_dim)):
+        for key, t in slice_projection(blk, name, 0, blk.num_experts, kk).items():
+            setattr(loc, f"{name}_{key}", t)
+    loc.block_group_size = blk.block_group_size
+    ep2 = ExpertParallelMoE.from_shard(loc, blk.gate.weight, blk.num_experts)
+    out2, _ = ep2.forward_tokens(x)
+    assert torch.equal(out2, out)
     assert _lib.device_error() == 0
 
 
