@@ -45,7 +45,7 @@ extern "C" {
 #define GEMQ_FWD_FORCE_SIMT 32u      /* use the CUDA-core grouped GEMM (cross-checking) */
 #define GEMQ_FWD_RESIDUAL 64u        /* out = fp16(x + block(x)): the decoder layer's residual add, fused */
 #define GEMQ_FWD_TIME_STAGES 128u    /* record CUDA events around each stage (read with gemq_layer_stage_times) */
-#define GEMQ_FWD_SMEM_DEQUANT 256u   /* decode batches: use the shared-memory dequant GEMM (cross-checking) */
+#define GEMQ_FWD_SMEM_DEQUANT 256u   /* use the shared-memory dequant GEMM instead of the tensor-memory one (cross-checking) */
 
 /* Stage indices reported by gemq_layer_stage_times. */
 #define GEMQ_STAGE_ROUTE 0    /* gate GEMM + softmax/top-k */

@@ -647,14 +647,23 @@ int forward_n_tokens(gemq_layer_t* L, const uint16_t* x, int64_t T, uint16_t* ou
   dn.row_weight = b.w_perm;
   const bool tc = !force_simt && tc_gemm_supported(up) && tc_gemm_supported(dn);
   if (!tc) up.nt = dn.nt = 32;
-  // decode batches: the tensor-memory dequant GEMM, with activations in its K order
-  const bool dec = tc && (flags & GEMQ_FWD_SMEM_DEQUANT) == 0 && tcd_gemm_supported(up) && tcd_gemm_supported(dn);
+  // the tensor-memory dequant GEMM, with activations in its K order, wherever it
+  // takes the shapes: 16 / 32-token tiles for decode batches, 64 for prefill
+  bool dec = false;
+  if (tc && (flags & GEMQ_FWD_SMEM_DEQUANT) == 0) {
+    GemmArgs u2 = up, d2 = dn;
+    if (up.nt == kNtLarge) u2.nt = d2.nt = kNtMid;
+    if (tcd_gemm_supported(u2) && tcd_gemm_supported(d2)) {
+      dec = true;
+      up.nt = dn.nt = u2.nt;
+    }
+  }
   if (dec) up.perm_out_nbits = L->w2.nbits;
   // Token tiles of 16 halve the MMA width. With at most 16 tokens no expert gets more
   // than 16 rows (a token picks an expert once); up to about 10 rows per expert on
   // average the few experts that need a second tile (and stream their weights twice)
   // cost less than the wider MMAs of 32-row tiles, measured on B200.
-  if (dec && (T <= kNtTiny || P <= 10 * static_cast<int64_t>(E))) up.nt = dn.nt = kNtTiny;
+  if (dec && up.nt == kNtSmall && (T <= kNtTiny || P <= 10 * static_cast<int64_t>(E))) up.nt = dn.nt = kNtTiny;
   // Few slots per expert (well under three waves of work items): order the segments
   // by dequant cost so the decode GEMM's last wave holds its cheapest items. With
   // more waves a mix of bit-widths on the SMs at any time measured faster.

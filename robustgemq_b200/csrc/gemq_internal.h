@@ -66,6 +66,7 @@ using Seg = int4;
 // Token-tile widths the tensor-core GEMM is instantiated for (UMMA N).
 constexpr int kNtTiny = 16;  // decode GEMM, batches of at most 16 tokens (16 rows per expert at most)
 constexpr int kNtSmall = 32;
+constexpr int kNtMid = 64;   // tensor-memory dequant GEMM, prefill (more than 48 rows per expert)
 constexpr int kNtLarge = 128;
 
 enum class GemmMode : int {
@@ -113,8 +114,8 @@ bool tc_gemm_supported(const GemmArgs& a);
 cudaError_t launch_tc_gemm(const GemmArgs& a, cudaStream_t stream);
 cudaError_t launch_simt_gemm(const GemmArgs& a, cudaStream_t stream);
 
-// Decode-batch tensor-core GEMM (token tiles of 32, dequantised weights in tensor
-// memory; kernels_tcd.cu). Its activations are stored in the slot order of
+// Tensor-core GEMM with the dequantised weights in tensor memory (token tiles of
+// 16 / 32 for decode batches, 64 for prefill; kernels_tcd.cu). Its activations are stored in the slot order of
 // kperm.cuh for the expert's bit-width: dispatch with perm_nbits, and the gate/up
 // launch's perm_out_nbits for the down projection.
 bool tcd_gemm_supported(const GemmArgs& a);
