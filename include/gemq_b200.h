@@ -46,6 +46,7 @@ extern "C" {
 #define GEMQ_FWD_RESIDUAL 64u        /* out = fp16(x + block(x)): the decoder layer's residual add, fused */
 #define GEMQ_FWD_TIME_STAGES 128u    /* record CUDA events around each stage (read with gemq_layer_stage_times) */
 #define GEMQ_FWD_SMEM_DEQUANT 256u   /* use the shared-memory dequant GEMM instead of the tensor-memory one (cross-checking) */
+#define GEMQ_FWD_PERMUTED_ROWS 512u  /* gemq_moe_experts: rows are in the tensor-memory GEMM's K order (see there) */
 
 /* Stage indices reported by gemq_layer_stage_times. */
 #define GEMQ_STAGE_ROUTE 0    /* gate GEMM + softmax/top-k */
@@ -215,8 +216,16 @@ int gemq_moe_combine(const uint16_t* y, const int32_t* slot_row, const int32_t* 
  * activation row). Rows of one expert come in no particular order. */
 size_t gemq_dispatch_workspace_size(int64_t num_tokens, int32_t top_k, int32_t num_experts);
 int gemq_moe_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t num_tokens,
-                      int32_t top_k, int32_t num_experts, int32_t hidden, int32_t* expert_counts, int32_t* slot_row,
-                      uint16_t* w_rows, uint16_t* x_rows, void* workspace, size_t workspace_bytes, void* stream);
+                      int32_t top_k, int32_t num_experts, int32_t hidden, const int32_t* perm_nbits,
+                      int32_t* expert_counts, int32_t* slot_row, uint16_t* w_rows, uint16_t* x_rows, void* workspace,
+                      size_t workspace_bytes, void* stream);
+/* perm_nbits (device int32 [num_experts], or NULL): write each row in the K order the
+ * tensor-memory GEMM reads for its expert's gate/up bit-width, for owners whose
+ * gemq_moe_experts_row_order is 1 (the rows then go in with GEMQ_FWD_PERMUTED_ROWS).
+ * Returns 1 when gemq_moe_experts runs this layer on the tensor-memory GEMM, whose
+ * input rows must then be permuted (dispatch with perm_nbits = the gate/up bit-widths
+ * of all experts) and flagged GEMQ_FWD_PERMUTED_ROWS; 0 when rows go in unpermuted. */
+int gemq_moe_experts_row_order(const gemq_layer_t* layer);
 
 /* forward_single_expert (moe_block.py:763-779) for every expert of the layer at once,
  * on rows already grouped by expert: rows fp16 [num_rows, hidden] ordered as

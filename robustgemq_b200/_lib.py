@@ -35,6 +35,7 @@ FWD_FORCE_SIMT = 32
 FWD_RESIDUAL = 64
 FWD_TIME_STAGES = 128
 FWD_SMEM_DEQUANT = 256
+FWD_PERMUTED_ROWS = 512
 ROUTE_WORKSPACE_BYTES = 1024
 STAGES = ("route", "dispatch", "up", "down", "shared", "combine")
 
@@ -48,6 +49,7 @@ EXPORTED = [
     "gemq_layer_create", "gemq_layer_destroy", "gemq_moe_workspace_size", "gemq_moe_route",
     "gemq_moe_forward", "gemq_layer_stage_times", "gemq_route", "gemq_moe_combine",
     "gemq_dispatch_workspace_size", "gemq_moe_dispatch", "gemq_moe_experts_workspace_size", "gemq_moe_experts",
+    "gemq_moe_experts_row_order",
 ]
 
 
@@ -115,7 +117,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "gemq_route": (ctypes.c_int, [vp, i64, i32, vp, i32, i32, i32, i32, u32, vp, vp, vp, vp, sz, vp]),
         "gemq_moe_combine": (ctypes.c_int, [vp, vp, vp, i64, i32, i32, u32, vp, vp, vp]),
         "gemq_dispatch_workspace_size": (sz, [i64, i32, i32]),
-        "gemq_moe_dispatch": (ctypes.c_int, [vp, vp, vp, i64, i32, i32, i32, vp, vp, vp, vp, vp, sz, vp]),
+        "gemq_moe_dispatch": (ctypes.c_int, [vp, vp, vp, i64, i32, i32, i32, vp, vp, vp, vp, vp, vp, sz, vp]),
+        "gemq_moe_experts_row_order": (ctypes.c_int, [vp]),
         "gemq_moe_experts_workspace_size": (sz, [vp, i64, i32]),
         "gemq_moe_experts": (ctypes.c_int, [vp, vp, i64, vp, i32, vp, vp, i32, u32, vp, sz, vp]),
     }

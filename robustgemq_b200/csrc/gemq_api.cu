@@ -856,8 +856,9 @@ size_t gemq_dispatch_workspace_size(int64_t num_tokens, int32_t top_k, int32_t n
 }
 
 int gemq_moe_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t num_tokens,
-                      int32_t top_k, int32_t num_experts, int32_t hidden, int32_t* expert_counts, int32_t* slot_row,
-                      uint16_t* w_rows, uint16_t* x_rows, void* workspace, size_t workspace_bytes, void* stream) {
+                      int32_t top_k, int32_t num_experts, int32_t hidden, const int32_t* perm_nbits,
+                      int32_t* expert_counts, int32_t* slot_row, uint16_t* w_rows, uint16_t* x_rows, void* workspace,
+                      size_t workspace_bytes, void* stream) {
   TraceRange trace("gemq_moe_dispatch");
   if (num_tokens < 0 || top_k <= 0 || top_k > 16) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad token or top_k count");
   if (num_experts <= 0 || num_experts > 256) return fail(GEMQ_ERR_UNSUPPORTED, "num_experts must be in [1, 256]");
@@ -874,6 +875,8 @@ int gemq_moe_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uin
     return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(x_rows)) & 15u)
     return fail(GEMQ_ERR_UNSUPPORTED, "x and x_rows must be 16-byte aligned");
+  if (perm_nbits != nullptr && hidden % 128 != 0)
+    return fail(GEMQ_ERR_UNSUPPORTED, "permuted rows need a hidden size that is a multiple of 128");
   if (workspace == nullptr || workspace_bytes < gemq_dispatch_workspace_size(num_tokens, top_k, num_experts))
     return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
   Carver c(workspace);
@@ -881,7 +884,7 @@ int gemq_moe_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uin
   Seg* segs = c.take<Seg>(num_experts);
   int32_t* tp = c.take<int32_t>(num_experts + 1);
   GEMQ_CUDA(launch_dispatch(topk_idx, topk_w, x, num_tokens, top_k, num_experts, hidden, kNtLarge, expert_counts,
-                            cursor, segs, tp, slot_row, w_rows, x_rows, nullptr, nullptr, s),
+                            cursor, segs, tp, slot_row, w_rows, x_rows, perm_nbits, nullptr, s),
             "dispatch");
   return GEMQ_OK;
 }
@@ -894,6 +897,48 @@ size_t gemq_moe_experts_workspace_size(const gemq_layer_t* layer, int64_t num_ro
   c.take<int32_t>(n + 1);
   c.take<uint16_t>(static_cast<size_t>(num_rows > 0 ? num_rows : 1) * layer->d.inter);
   return c.off + 256;
+}
+
+}  // extern "C"
+
+namespace gemq {
+namespace {
+// The two GEMMs of gemq_moe_experts for a layer, tile width and row order chosen the
+// same way whatever the row counts, so that the row order a sender must use
+// (gemq_moe_experts_row_order) depends on the layer alone.
+void experts_args(const gemq_layer_t* layer, int32_t sm_budget, GemmArgs& up, GemmArgs& dn, bool& tc, bool& tmem) {
+  const gemq_layer_desc_t& d = layer->d;
+  up = GemmArgs{};
+  up.mode = GemmMode::kSwiGLU;
+  up.w0 = layer->w1;
+  up.w1 = layer->w3;
+  up.out_ld = d.inter;
+  up.out_cols = d.inter;
+  up.num_sms = (sm_budget > 0 && sm_budget < layer->num_sms) ? sm_budget : layer->num_sms;
+  up.num_segs = 1;
+  up.nt = kNtLarge;
+  dn = up;
+  dn.mode = GemmMode::kRouteWeight;
+  dn.w0 = dn.w1 = layer->w2;
+  dn.out_ld = d.hidden;
+  dn.out_cols = d.hidden;
+  up.act = dn.act = reinterpret_cast<const uint16_t*>(uintptr_t{256});  // alignment check only
+  tc = tc_gemm_supported(up) && tc_gemm_supported(dn);
+  GemmArgs u2 = up, d2 = dn;
+  u2.nt = d2.nt = kNtMid;
+  tmem = tc && tcd_gemm_supported(u2) && tcd_gemm_supported(d2);
+}
+}  // namespace
+}  // namespace gemq
+
+extern "C" {
+
+int gemq_moe_experts_row_order(const gemq_layer_t* layer) {
+  if (layer == nullptr) return 0;
+  GemmArgs up, dn;
+  bool tc = false, tmem = false;
+  experts_args(layer, 0, up, dn, tc, tmem);
+  return tmem ? 1 : 0;
 }
 
 int gemq_moe_experts(gemq_layer_t* layer, const uint16_t* rows, int64_t num_rows, const int32_t* group_counts,
@@ -919,32 +964,45 @@ int gemq_moe_experts(gemq_layer_t* layer, const uint16_t* rows, int64_t num_rows
   Seg* segs = c.take<Seg>(n);
   int32_t* tp = c.take<int32_t>(n + 1);
   uint16_t* h = c.take<uint16_t>(static_cast<size_t>(num_rows) * d.inter);
-  const bool force_simt = (flags & GEMQ_FWD_FORCE_SIMT) != 0;
-  GemmArgs up{};
-  up.mode = GemmMode::kSwiGLU;
-  up.w0 = layer->w1;
-  up.w1 = layer->w3;
+  GemmArgs up, dn;
+  bool tc = false, tmem = false;
+  experts_args(layer, sm_budget, up, dn, tc, tmem);
+  const bool permuted = (flags & GEMQ_FWD_PERMUTED_ROWS) != 0;
+  if (permuted != tmem)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, tmem ? "this layer takes rows in the tensor-memory GEMM's K order "
+                                                  "(dispatch with perm_nbits, flag GEMQ_FWD_PERMUTED_ROWS)"
+                                                : "this layer takes unpermuted rows");
+  if (row_weight == nullptr && tmem) return fail(GEMQ_ERR_UNSUPPORTED, "the tensor-memory GEMM needs row weights");
   up.act = rows;
   up.act_rows = num_rows;
   up.segs = segs;
   up.tile_prefix = tp;
   up.num_segs = n;
   up.out = h;
-  up.out_ld = d.inter;
-  up.out_cols = d.inter;
-  up.num_sms = (sm_budget > 0 && sm_budget < layer->num_sms) ? sm_budget : layer->num_sms;
-  up.nt = choose_nt(num_rows / n);
-  GemmArgs dn = up;
   dn.mode = row_weight != nullptr ? GemmMode::kRouteWeight : GemmMode::kStoreF16;
-  dn.w0 = dn.w1 = layer->w2;
   dn.act = h;
+  dn.act_rows = num_rows;
+  dn.segs = segs;
+  dn.tile_prefix = tp;
+  dn.num_segs = n;
   dn.out = out;
-  dn.out_ld = d.hidden;
-  dn.out_cols = d.hidden;
   dn.row_weight = row_weight;
-  const bool tc = !force_simt && tc_gemm_supported(up) && tc_gemm_supported(dn);
-  if (!tc) up.nt = dn.nt = 32;
+  if (tmem) {
+    // 16 / 32 / 64-token tiles by rows per segment, h written in w2's K order
+    const int64_t per = num_rows / n;
+    up.nt = per > 48 ? kNtMid : (per > 10 ? kNtSmall : kNtTiny);
+    up.perm_out_nbits = layer->w2.nbits;
+  } else {
+    up.nt = tc ? choose_nt(num_rows / n) : 32;
+  }
+  dn.nt = up.nt;
   GEMQ_CUDA(launch_group_segs(group_counts, n, E, up.nt, segs, tp, s), "segments");
+  if (tmem) {
+    if (!tcd_gemm_supported(up) || !tcd_gemm_supported(dn)) return fail(GEMQ_ERR_UNSUPPORTED, "expert GEMM shape");
+    GEMQ_CUDA(launch_tcd_gemm(up, s), "up projection");
+    GEMQ_CUDA(launch_tcd_gemm(dn, s), "down projection");
+    return GEMQ_OK;
+  }
   if (int rc = run_gemm(up, !tc, s, "up projection")) return rc;
   return run_gemm(dn, !tc, s, "down projection");
 }

@@ -9,7 +9,10 @@ forward on a rank's own tokens:
 2. groups the ``T * k`` token-expert slots by expert id on the device
    (``gemq_moe_dispatch``: histogram, scan, scatter of the activation rows and
    routing weights). Experts are contiguous per rank, so the rows come out grouped
-   by destination rank and, inside each destination, by its local expert;
+   by destination rank and, inside each destination, by its local expert. Each row
+   is written in the K order the owner's tensor-memory GEMM reads for that expert's
+   bit-width (``gemq_moe_experts_row_order``; every rank knows all experts' gate/up
+   bit-widths, gathered once by ``from_shard``);
 3. exchanges the per-expert row counts (with this rank's routing status) in one
    ``all_to_all_single`` and reads them to the host: the one host synchronisation
    of the forward, which sizes the exchanges that follow;
@@ -141,6 +144,18 @@ class ExpertParallelMoE(nn.Module):
             self.local = _LocalExperts(block.hidden_dim, block.ffn_dim, self.experts_per_rank)
             if block.w1_wq is not None:
                 self._load_local(block)
+        # gate/up bit-widths of all E experts (the dispatch writes each row in the K
+        # order its owner's tensor-memory GEMM reads); a shard gathers them once
+        if _shard is None:
+            self.w1_nbits_all = block.w1_nbits
+        elif self.world > 1:
+            nb = local_block.w1_nbits.to(torch.int32).contiguous()
+            allnb = nb.new_empty(E)
+            dist.all_gather_into_tensor(allnb, nb, group=group)
+            self.w1_nbits_all = allnb
+        else:
+            self.w1_nbits_all = local_block.w1_nbits
+        self._rows_permuted = None  # decided by the local layer on the first forward
         self.route_fn = route_fn or self._route
         self.dispatch_fn = dispatch_fn or self._dispatch
         self.experts_fn = experts_fn or self._experts
@@ -182,6 +197,13 @@ class ExpertParallelMoE(nn.Module):
                                      stream_ptr(x.device)))
         return logits, idx, w
 
+    def rows_permuted(self) -> bool:
+        """Whether the local experts' GEMM takes rows in the tensor-memory GEMM's K order
+        (the same answer on every rank: it depends on the layer's shapes alone)."""
+        if self._rows_permuted is None:
+            self._rows_permuted = bool(_lib.load().gemq_moe_experts_row_order(self.local.layer_handle()))
+        return self._rows_permuted
+
     def _dispatch(self, idx: Tensor, w: Tensor, x: Tensor):
         T, k, E, D = x.shape[0], self.top_k, self.num_experts, self.hidden_dim
         P = T * k
@@ -191,8 +213,11 @@ class ExpertParallelMoE(nn.Module):
         x_rows = torch.empty((max(P, 1), D), dtype=torch.float16, device=x.device)
         lib = _lib.load()
         ws = torch.empty(lib.gemq_dispatch_workspace_size(T, k, E), dtype=torch.uint8, device=x.device)
-        check(lib.gemq_moe_dispatch(ptr(idx), ptr(w), ptr(x), T, k, E, D, ptr(counts), ptr(slot_row), ptr(w_rows),
-                                    ptr(x_rows), ptr(ws), ws.numel(), stream_ptr(x.device)))
+        perm = None
+        if self.rows_permuted():
+            perm = self.w1_nbits_all.to(device=x.device, dtype=torch.int32).contiguous()
+        check(lib.gemq_moe_dispatch(ptr(idx), ptr(w), ptr(x), T, k, E, D, ptr(perm), ptr(counts), ptr(slot_row),
+                                    ptr(w_rows), ptr(x_rows), ptr(ws), ws.numel(), stream_ptr(x.device)))
         return counts, slot_row[:P], w_rows[:P], x_rows[:P]
 
     def _experts(self, rows: Tensor, group_counts: Tensor, weights: Tensor) -> Tensor:
@@ -205,8 +230,9 @@ class ExpertParallelMoE(nn.Module):
         gc = group_counts.to(device=rows.device, dtype=torch.int32).contiguous()
         ws = torch.empty(lib.gemq_moe_experts_workspace_size(handle, rows.shape[0], G), dtype=torch.uint8,
                          device=rows.device)
+        flags = _lib.FWD_PERMUTED_ROWS if self.rows_permuted() else 0
         check(lib.gemq_moe_experts(handle, ptr(rows), rows.shape[0], ptr(gc), G, ptr(weights.contiguous()), ptr(out),
-                                   self.sm_budget, 0, ptr(ws), ws.numel(), stream_ptr(rows.device)))
+                                   self.sm_budget, flags, ptr(ws), ws.numel(), stream_ptr(rows.device)))
         return out
 
     def _combine(self, y: Tensor, slot_row: Tensor, topk_idx: Tensor, residual: Optional[Tensor]) -> Tensor:
