@@ -303,6 +303,60 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// The eight K=16 steps of one 128-wide K stage, D[tmem] (+)= A[tmem] * B[smem]^T,
+// issued from one asm block: step j reads A at column a_tmem + 8j and B through the
+// descriptor advanced by 2j (j < 4) or BHI + 2(j - 4) (j >= 4) descriptor units of 16
+// bytes (B is two 64-wide SW128 sub-tiles, the second BHI units on). Step 0
+// accumulates when `accumulate` is non-zero, the others always. With no compiler
+// barrier between the steps their operands are formed back to back: issued one asm
+// statement (and one memory clobber) per MMA, each MMA cost about 28 cycles of issue,
+// several times its execution at a 16-token tile, and the MMA warp paced the kernel.
+// The descriptor's start field (bits 0-13, address >> 4) cannot carry: shared memory
+// addresses stay below 2^18.
+template <int BHI>
+__device__ __forceinline__ void umma_f16_ts_k128(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      ".reg .b32 a1, a2, a3, a4, a5, a6, a7;\n\t"
+      ".reg .b64 b1, b2, b3, b4, b5, b6, b7;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.u32 q, 0, 0;\n\t"
+      "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\tadd.u32 a4, %1, 32;\n\t"
+      "add.u32 a5, %1, 40;\n\tadd.u32 a6, %1, 48;\n\tadd.u32 a7, %1, 56;\n\t"
+      "add.u64 b1, %2, 2;\n\tadd.u64 b2, %2, 4;\n\tadd.u64 b3, %2, 6;\n\tadd.u64 b4, %2, %5;\n\t"
+      "add.u64 b5, %2, %6;\n\tadd.u64 b6, %2, %7;\n\tadd.u64 b7, %2, %8;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a4], b4, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a5], b5, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a6], b6, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a7], b7, %3, q;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "n"(BHI), "n"(BHI + 2), "n"(BHI + 4), "n"(BHI + 6)
+      : "memory");
+}
+
+// The four K=16 steps of one 64-wide K stage, D[tmem] (+)= A[smem] * B[smem]^T, both
+// operands SW128 K-major: step j advances both descriptors by 2j units (32 bytes).
+__device__ __forceinline__ void umma_f16_k64(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      ".reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.u32 q, 0, 0;\n\t"
+      "add.u64 a1, %1, 2;\n\tadd.u64 a2, %1, 4;\n\tadd.u64 a3, %1, 6;\n\t"
+      "add.u64 b1, %2, 2;\n\tadd.u64 b2, %2, 4;\n\tadd.u64 b3, %2, 6;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, q;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor, K-major operand in the canonical 128-byte
 // swizzle: rows of 64 fp16 (128 B), 8-row atoms of 1024 B stacked along M/N.
 // Fields per the sm100 UMMA descriptor: start>>4 [0,14), LBO>>4 [16,30) (unused

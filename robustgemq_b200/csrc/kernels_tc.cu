@@ -323,11 +323,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int m = 0; m < kMats; ++m) {
             const uint32_t a_addr = kDense ? act_addr + C::kActBytes
                                            : smem_u32(smem + C::kARingOff + (as * kMats + m) * C::kATile);
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-              umma_f16(d_base + static_cast<uint32_t>(m * NT), sdesc_sw128(a_addr + kk * 32),
-                       sdesc_sw128(act_addr + kk * 32), C::kIdesc, (kt | kk) != 0 ? 1u : 0u);
-            }
+            // the 4 K=16 steps of the stage from one asm block (+32 B per step)
+            umma_f16_k64(d_base + static_cast<uint32_t>(m * NT), sdesc_sw128(a_addr), sdesc_sw128(act_addr),
+                         C::kIdesc, kt != 0 ? 1u : 0u);
           }
           umma_commit(&empty[s]);
           if constexpr (!kDense) umma_commit(&aempty[as]);

@@ -590,16 +590,12 @@ __global__ void __launch_bounds__(kThreadsD, 1)
           const uint64_t b0 = sdesc_sw128(act);
           const uint32_t a0 = tmem + static_cast<uint32_t>(C::kACol0 + as * C::kACols);
           if (elect_one()) {
+            // per matrix, the 8 K=16 steps of the stage: +32 B per step inside a
+            // 128-byte row, the second 64-k sub-tile kActSub bytes on
 #pragma unroll
-            for (int m = 0; m < kMats; ++m) {
-#pragma unroll
-              for (int kk = 0; kk < kSK / 16; ++kk) {
-                // +32 B per 16-k step inside a 128-byte row, +NT rows per 64-k sub-tile
-                const uint64_t bd = b0 + static_cast<uint64_t>(((kk >> 2) * C::kActSub + (kk & 3) * 32) >> 4);
-                umma_f16_ts(d_base + static_cast<uint32_t>(m * NT), a0 + static_cast<uint32_t>(m * 64 + kk * 8), bd,
-                            C::kIdesc, (kt | kk) != 0 ? 1u : 0u);
-              }
-            }
+            for (int m = 0; m < kMats; ++m)
+              umma_f16_ts_k128<C::kActSub / 16>(d_base + static_cast<uint32_t>(m * NT),
+                                                a0 + static_cast<uint32_t>(m * 64), b0, C::kIdesc, kt != 0 ? 1u : 0u);
             umma_commit(&empty[s]);
             umma_commit(&aempty[as]);
           }
