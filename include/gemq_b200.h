@@ -47,7 +47,6 @@ extern "C" {
 #define GEMQ_FWD_TIME_STAGES 128u    /* record CUDA events around each stage (read with gemq_layer_stage_times) */
 #define GEMQ_FWD_SMEM_DEQUANT 256u   /* use the shared-memory dequant GEMM instead of the tensor-memory one (cross-checking) */
 #define GEMQ_FWD_PERMUTED_ROWS 512u  /* gemq_moe_experts: rows are in the tensor-memory GEMM's K order (see there) */
-#define GEMQ_FWD_SPLIT_KERNELS 1024u /* one-token path: one kernel per stage instead of the single cooperative kernel */
 
 /* Stage indices reported by gemq_layer_stage_times. */
 #define GEMQ_STAGE_ROUTE 0    /* gate GEMM + softmax/top-k */

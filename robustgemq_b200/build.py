@@ -22,7 +22,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libgemq_b200.so"
 SOURCES = ["gemq_api.cu", "kernels_misc.cu", "kernels_route.cu", "kernels_decode.cu", "kernels_tc.cu",
            "kernels_tcd.cu", "kernels_simt.cu"]
-HEADERS = ["gemq_common.cuh", "gemq_internal.h", "tc_work.cuh", "kperm.cuh", "route_topk.cuh"]
+HEADERS = ["gemq_common.cuh", "gemq_internal.h", "tc_work.cuh", "kperm.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

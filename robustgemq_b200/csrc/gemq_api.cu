@@ -487,7 +487,6 @@ struct FwdBufs {
   uint16_t *w_perm = nullptr, *x_perm = nullptr, *h_perm = nullptr, *y_perm = nullptr;
   uint16_t *s_h = nullptr, *s_out = nullptr;
   float *part_up = nullptr, *part_dn = nullptr, *part_s = nullptr, *part_s2 = nullptr;
-  unsigned* barrier = nullptr;  // one-token layer kernel's grid barrier counter
   size_t bytes = 0;
   int splits_up = 1, splits_dn = 1, splits_s = 1, splits_s2 = 1;
 };
@@ -509,7 +508,6 @@ FwdBufs carve(const gemq_layer_t* L, int64_t T, uint32_t flags, void* base, cons
   b.one_seg = c.take<Seg>(1);
   b.one_tp = c.take<int32_t>(2);
   if (flags & GEMQ_FWD_ONE_TOKEN) {
-    b.barrier = c.take<unsigned>(4);
     b.splits_up = gemv_default_splits(D, F, k, L->num_sms, 2);
     b.splits_dn = gemv_default_splits(F, D, k, L->num_sms);
     b.part_up = c.take<float>(2ull * b.splits_up * k * F);  // [w1, w3][split][a][F]
@@ -584,50 +582,6 @@ int run_router(const gemq_layer_desc_t& d, int num_sms, const uint16_t* x, int64
   GEMQ_CUDA(launch_topk(logits_out, fp32_logits, T, d.num_experts, d.top_k, norm, fp16_softmax, idx, w, s), "topk");
   if (tm) tm->end(GEMQ_STAGE_ROUTE);
   return GEMQ_OK;
-}
-
-// The whole one-token layer as one cooperative kernel (router included unless the
-// routing is given). Returns cudaErrorNotSupported when the device cannot hold its
-// grid; the caller then runs the per-stage kernels.
-cudaError_t forward_one_token_fused(gemq_layer_t* L, const uint16_t* x, uint16_t* out, const int32_t* given_idx,
-                                    const uint16_t* given_w, uint32_t flags, FwdBufs& b, cudaStream_t s) {
-  const gemq_layer_desc_t& d = L->d;
-  OneTokenArgs a{};
-  a.w1 = L->w1;
-  a.w3 = L->w3_as_w1;
-  a.w2 = L->w2;
-  a.has_shared = d.has_shared;
-  if (d.has_shared) {
-    a.sw1 = L->sw1;
-    a.sw3 = L->sw3;
-    a.sw2 = L->sw2;
-  }
-  a.x = reinterpret_cast<const __half*>(x);
-  a.gate = reinterpret_cast<const __half*>(d.gate_weight);
-  a.E = d.num_experts;
-  a.k = d.top_k;
-  a.D = d.hidden;
-  a.F = d.inter;
-  a.Fs = L->shared_inter;
-  a.router_fp32 = d.router == GEMQ_ROUTER_FP32;
-  a.norm = d.norm_topk_prob != 0;
-  a.fp16_softmax = (flags & GEMQ_FWD_FP16_SOFTMAX) != 0;
-  a.given_idx = given_idx;
-  a.given_w = reinterpret_cast<const __half*>(given_w);
-  a.idx_out = given_idx != nullptr ? nullptr : b.topk_idx;
-  a.w_out = given_idx != nullptr ? nullptr : reinterpret_cast<__half*>(b.topk_w);
-  a.part_up = b.part_up;
-  a.part_dn = b.part_dn;
-  a.part_s = b.part_s;
-  a.part_s2 = b.part_s2;
-  a.splits_up = b.splits_up;
-  a.splits_dn = b.splits_dn;
-  a.splits_s = b.splits_s;
-  a.splits_s2 = b.splits_s2;
-  a.residual = (flags & GEMQ_FWD_RESIDUAL) ? reinterpret_cast<const __half*>(x) : nullptr;
-  a.out = reinterpret_cast<__half*>(out);
-  a.barrier = b.barrier;
-  return launch_one_token_layer(a, L->num_sms, s);
 }
 
 int forward_one_token(gemq_layer_t* L, const uint16_t* x, uint16_t* out, const int32_t* idx, const uint16_t* w,
@@ -826,16 +780,6 @@ int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens,
   if (workspace == nullptr || workspace_bytes < b.bytes) return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   StageTimer tm(layer, s, flags);
-  // one token: the single cooperative kernel, unless the caller wants the logits,
-  // gives them, times the stages or asks for the per-stage kernels
-  if (one && !given_logits && router_logits == nullptr &&
-      (flags & (GEMQ_FWD_TIME_STAGES | GEMQ_FWD_SPLIT_KERNELS)) == 0) {
-    const cudaError_t e = forward_one_token_fused(layer, x, out, given_routing ? topk_idx : nullptr,
-                                                  given_routing ? topk_w : nullptr, flags, b, s);
-    if (e == cudaSuccess) return GEMQ_OK;
-    if (e != cudaErrorNotSupported) return cuda_fail(e, "one-token layer");
-    (void)cudaGetLastError();
-  }
   const int32_t* idx = topk_idx;
   const uint16_t* w = topk_w;
   if (!given_routing) {

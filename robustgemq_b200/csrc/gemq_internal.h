@@ -170,31 +170,6 @@ cudaError_t launch_gemv(const ProjDev& w0, const ProjDev* w1, const int32_t* idx
 // out[a][n] = fp16(sum_s part[s][a][n])
 cudaError_t launch_gemv_reduce(const float* part, int splits, int rows_a, int n, uint16_t* out, cudaStream_t s);
 // out[n] = fp16(sum_a w[a] * fp16(sum_s part[s][a][n])) (+ fp16 shared, + residual)
-// The whole one-token layer in one cooperative launch (kernels_decode.cu): router
-// (unless routing is given), gate/up GEMV units, a grid barrier, down GEMV units, a
-// grid barrier, combine. The same arithmetic, in the same order, as gate logits ->
-// top-k -> launch_gemv x2 -> launch_decode_combine.
-struct OneTokenArgs {
-  ProjDev w1, w3, w2;     // w3 read with w1's nbits / strides (fused_dequant_bmm.py:98)
-  ProjDev sw1, sw3, sw2;  // DeepSeek shared experts (has_shared)
-  int has_shared;
-  const __half* x;        // [D]
-  const __half* gate;     // [E, D] (router), unused with given routing
-  int E, k, D, F, Fs;
-  int router_fp32, norm, fp16_softmax;
-  const int32_t* given_idx;  // [k] or null
-  const __half* given_w;     // [k] or null
-  int32_t* idx_out;          // [k] routing written by CTA 0 (may be null)
-  __half* w_out;
-  float *part_up, *part_dn, *part_s, *part_s2;
-  int splits_up, splits_dn, splits_s, splits_s2;
-  const __half* residual;  // [D] or null
-  __half* out;             // [D]
-  unsigned* barrier;       // zeroed by the launcher
-};
-// Returns cudaErrorNotSupported when the device cannot hold the whole grid at once
-// (the caller then uses the per-stage kernels).
-cudaError_t launch_one_token_layer(const OneTokenArgs& a, int num_sms, cudaStream_t s);
 cudaError_t launch_decode_combine(const float* part, int splits, int A, int n, const uint16_t* w,
                                   const float* shared_part, int shared_splits, const uint16_t* residual, uint16_t* out,
                                   cudaStream_t s);

@@ -23,12 +23,8 @@
 //                 ``F.silu(x1) * x3`` of the shared experts, moe_block.py:619)
 #include <cuda_fp16.h>
 
-#include <algorithm>
-#include <atomic>
-
 #include "gemq_common.cuh"
 #include "gemq_internal.h"
-#include "route_topk.cuh"
 
 namespace gemq {
 
@@ -255,15 +251,15 @@ __device__ __forceinline__ void gemv_rows(const int32_t* wbase, int K, int N, in
 __host__ __device__ inline int gemv_x_elems(int k, int splits) { return (k + splits - 1) / splits + 128; }
 __host__ __device__ inline int gemv_groups(int k, int splits, int g) { return gemv_x_elems(k, splits) / g + 2; }
 
-// One work unit of the split-K GEMV: 128 output features (slab), one K split s, one
-// (matrix, row a) pair z = mat * rows_a + a, computed by the whole CTA (256 threads)
-// with its shared memory; part[mat][s][a][n] gets the unit's fp32 sums. The CTA's
-// threads all return together (every early exit depends on the unit only).
 template <bool XF16>
-__device__ __forceinline__ void gemv_unit(const ProjDev& w0, const ProjDev& w1, const int32_t* idx, int rows_a,
-                                          const GemvSrc& src, float* __restrict__ part, int splits, int slab, int s,
-                                          int z, unsigned char* s_raw, float (*s_red)[kGemvCols]) {
-  const int mat = z / rows_a, a = z - mat * rows_a;
+__global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1, const int32_t* __restrict__ idx,
+                                                          int rows_a, GemvSrc src, float* __restrict__ part,
+                                                          int splits) {
+  grid_dep_wait();
+  extern __shared__ __align__(16) unsigned char s_raw[];
+  __shared__ float s_red[8][kGemvCols];
+  const int slab = blockIdx.x, s = blockIdx.y;
+  const int mat = blockIdx.z / rows_a, a = blockIdx.z - mat * rows_a;
   const ProjDev& w = (mat == 0) ? w0 : w1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = (idx != nullptr) ? idx[a] : a;
@@ -410,16 +406,6 @@ __device__ __forceinline__ void gemv_unit(const ProjDev& w0, const ProjDev& w1, 
   }
 }
 
-template <bool XF16>
-__global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1, const int32_t* __restrict__ idx,
-                                                          int rows_a, GemvSrc src, float* __restrict__ part,
-                                                          int splits) {
-  grid_dep_wait();
-  extern __shared__ __align__(16) unsigned char s_raw[];
-  __shared__ float s_red[8][kGemvCols];
-  gemv_unit<XF16>(w0, w1, idx, rows_a, src, part, splits, blockIdx.x, blockIdx.y, blockIdx.z, s_raw, s_red);
-}
-
 __global__ void k_gemv_reduce(const float* __restrict__ part, int splits, int64_t count, __half* __restrict__ out) {
   grid_dep_wait();
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -433,22 +419,12 @@ __global__ void k_gemv_reduce(const float* __restrict__ part, int splits, int64_
 // out[n] = fp16(sum_a w[a] * x2[a][n]) with x2 = fp16(sum_s part[s][a][n]): the fp32
 // einsum combine of forward_one_token (moe_block.py:849-850); then the shared
 // experts' fp16 output (moe_block.py:620) and an optional residual, each in fp16.
-__device__ __forceinline__ __half decode_combine_elem(const float* __restrict__ part, int splits, int A, int n, int i,
-                                                     const __half* w, const float* __restrict__ shared_part,
-                                                     int shared_splits, const __half* __restrict__ residual);
-
 __global__ void k_decode_combine(const float* __restrict__ part, int splits, int A, int n, const __half* __restrict__ w,
                                  const float* __restrict__ shared_part, int shared_splits,
                                  const __half* __restrict__ residual, __half* __restrict__ out) {
   grid_dep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  out[i] = decode_combine_elem(part, splits, A, n, i, w, shared_part, shared_splits, residual);
-}
-
-__device__ __forceinline__ __half decode_combine_elem(const float* __restrict__ part, int splits, int A, int n, int i,
-                                                     const __half* w, const float* __restrict__ shared_part,
-                                                     int shared_splits, const __half* __restrict__ residual) {
   // split-major, so the partials of all rows a of one split load together; each
   // x2[a] is still summed in split order
   float x2[16];
@@ -470,7 +446,7 @@ __device__ __forceinline__ __half decode_combine_elem(const float* __restrict__ 
     r = __float2half_rn(__half2float(r) + __half2float(__float2half_rn(v)));
   }
   if (residual != nullptr) r = __float2half_rn(__half2float(r) + __half2float(residual[i]));
-  return r;
+  out[i] = r;
 }
 
 template <bool XF16>
@@ -491,162 +467,7 @@ cudaError_t launch_gemv_t(const ProjDev& w0, const ProjDev* w1, const int32_t* i
                     part, splits);
 }
 
-// ------------------------------------------------------------------ one-token layer
-// Grid barrier of the cooperative one-token kernel: every CTA adds one to the counter
-// and waits until it reaches `target` (calls k of a launch use target k * gridDim.x).
-// The wait is bounded (kWaitLimitNs); on expiry the kernel records a timeout and the
-// CTA returns false.
-__device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned target) {
-  __shared__ int s_ok;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int ok = 1;
-    __threadfence();
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
-    const uint64_t t0 = globaltimer_ns();
-    for (;;) {
-      unsigned v;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
-      if (v >= target) break;
-      if (device_error_set() || globaltimer_ns() - t0 > kWaitLimitNs) {
-        set_device_abort(kDevTimeoutDrain);
-        ok = 0;
-        break;
-      }
-      __nanosleep(32);
-    }
-    s_ok = ok;
-  }
-  __syncthreads();
-  return s_ok != 0;
-}
-
-__device__ __forceinline__ void unit_coords(int u, int slabs, int splits, int& slab, int& s, int& z) {
-  slab = u % slabs;
-  const int t = u / slabs;
-  s = t % splits;
-  z = t / splits;
-}
-
-__global__ void __launch_bounds__(kGemvThreads, 2) k_one_token(const OneTokenArgs a) {
-  extern __shared__ __align__(16) unsigned char s_raw[];
-  __shared__ float s_red[8][kGemvCols];
-  __shared__ float s_logit[kMaxExperts];
-  __shared__ int32_t s_idx[16];
-  __shared__ __half s_w[16];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // ---- routing: every CTA computes the same logits and top-k (the arithmetic of
-  // k_gate_logits + k_topk), so no CTA waits for another before the up GEMV
-  if (a.given_idx != nullptr) {
-    if (threadIdx.x < a.k) {
-      s_idx[threadIdx.x] = a.given_idx[threadIdx.x];
-      s_w[threadIdx.x] = a.given_w[threadIdx.x];
-    }
-  } else {
-    uint4* xs = reinterpret_cast<uint4*>(s_raw);
-    const int d8 = a.D / 8;
-    for (int c = threadIdx.x; c < d8; c += blockDim.x) xs[c] = reinterpret_cast<const uint4*>(a.x)[c];
-    __syncthreads();
-    for (int e = warp; e < a.E; e += blockDim.x / 32) {
-      const float v = gate_logit_warp(xs, a.gate + static_cast<int64_t>(e) * a.D, d8, lane);
-      if (lane == 0) s_logit[e] = a.router_fp32 ? v : __half2float(__float2half_rn(v));
-    }
-    __syncthreads();
-    if (warp == 0)
-      topk_warp([&](int e) { return s_logit[e]; }, a.E, a.k, a.norm, a.fp16_softmax, s_idx, s_w);
-  }
-  __syncthreads();
-  if (blockIdx.x == 0 && a.idx_out != nullptr && threadIdx.x < a.k) {
-    a.idx_out[threadIdx.x] = s_idx[threadIdx.x];
-    a.w_out[threadIdx.x] = s_w[threadIdx.x];
-  }
-  // ---- gate/up (w1 and w3 of the k experts) and the shared experts' gate/up
-  const int slabs_up = (a.F + kGemvCols - 1) / kGemvCols;
-  const int u_up = slabs_up * a.splits_up * 2 * a.k;
-  const int slabs_su = a.has_shared ? (a.Fs + kGemvCols - 1) / kGemvCols : 0;
-  const int u_su = slabs_su * a.splits_s * 2;
-  const GemvSrc xs_src{kGemvX, a.x, nullptr, 0, nullptr, 0, 0, 0};
-  for (int u = blockIdx.x; u < u_up + u_su; u += gridDim.x) {
-    int slab, sp, z;
-    if (u < u_up) {
-      unit_coords(u, slabs_up, a.splits_up, slab, sp, z);
-      gemv_unit<true>(a.w1, a.w3, s_idx, a.k, xs_src, a.part_up, a.splits_up, slab, sp, z, s_raw, s_red);
-    } else {
-      unit_coords(u - u_up, slabs_su, a.splits_s, slab, sp, z);
-      gemv_unit<true>(a.sw1, a.sw3, nullptr, 1, xs_src, a.part_s, a.splits_s, slab, sp, z, s_raw, s_red);
-    }
-    __syncthreads();
-  }
-  if (!grid_barrier(a.barrier, gridDim.x)) return;
-  // ---- down (reduces the up partials, fp32 SiLU*mul) and the shared experts' down
-  const int slabs_dn = (a.D + kGemvCols - 1) / kGemvCols;
-  const int u_dn = slabs_dn * a.splits_dn * a.k;
-  const int u_sd = a.has_shared ? slabs_dn * a.splits_s2 : 0;
-  const GemvSrc hs{kGemvPartF32, nullptr, nullptr, 0, a.part_up, a.splits_up, a.k, a.F};
-  const GemvSrc ss{kGemvPartF16, nullptr, nullptr, 0, a.part_s, a.splits_s, 1, a.Fs};
-  for (int u = blockIdx.x; u < u_dn + u_sd; u += gridDim.x) {
-    int slab, sp, z;
-    if (u < u_dn) {
-      unit_coords(u, slabs_dn, a.splits_dn, slab, sp, z);
-      gemv_unit<false>(a.w2, a.w2, s_idx, a.k, hs, a.part_dn, a.splits_dn, slab, sp, z, s_raw, s_red);
-    } else {
-      unit_coords(u - u_dn, slabs_dn, a.splits_s2, slab, sp, z);
-      gemv_unit<false>(a.sw2, a.sw2, nullptr, 1, ss, a.part_s2, a.splits_s2, slab, sp, z, s_raw, s_red);
-    }
-    __syncthreads();
-  }
-  if (!grid_barrier(a.barrier, 2 * gridDim.x)) return;
-  // ---- combine: out = fp16(sum_a w_a * x2_a) (+ shared, + residual)
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.D; i += gridDim.x * blockDim.x)
-    a.out[i] = decode_combine_elem(a.part_dn, a.splits_dn, a.k, a.D, i, s_w, a.has_shared ? a.part_s2 : nullptr,
-                                   a.splits_s2, a.residual);
-}
-
 }  // namespace
-
-cudaError_t launch_one_token_layer(const OneTokenArgs& a, int num_sms, cudaStream_t s) {
-  if (a.k > 16 || a.E > kMaxExperts || a.D % 8 != 0) return cudaErrorNotSupported;
-  if (a.w1.group_size % 32 != 0 || a.w2.group_size % 32 != 0) return cudaErrorNotSupported;
-  if (a.has_shared && (a.sw1.group_size % 32 != 0 || a.sw2.group_size % 32 != 0)) return cudaErrorNotSupported;
-  // shared memory: the largest GEMV unit's x span and scale rows, and the router row
-  auto unit_smem = [](const ProjDev& w, int splits, bool xf16) {
-    const int xbytes = (xf16 ? 2 : 4) * gemv_x_elems(w.k, splits);
-    return ((xbytes + 15) & ~15) + 2 * 2 * 128 * static_cast<size_t>(gemv_groups(w.k, splits, w.group_size));
-  };
-  size_t smem = static_cast<size_t>(a.D) * 2;
-  smem = std::max(smem, unit_smem(a.w1, a.splits_up, true));
-  smem = std::max(smem, unit_smem(a.w2, a.splits_dn, false));
-  if (a.has_shared) {
-    smem = std::max(smem, unit_smem(a.sw1, a.splits_s, true));
-    smem = std::max(smem, unit_smem(a.sw2, a.splits_s2, false));
-  }
-  static std::atomic<size_t> smem_done[kMaxDevices];
-  if (smem > 48 * 1024) {
-    cudaError_t e = raise_smem_limit(k_one_token, smem, smem_done);
-    if (e != cudaSuccess) return e;
-  }
-  int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_one_token, kGemvThreads, smem);
-  if (e != cudaSuccess) return e;
-  const int units_up = ((a.F + kGemvCols - 1) / kGemvCols) * a.splits_up * 2 * a.k +
-                       (a.has_shared ? ((a.Fs + kGemvCols - 1) / kGemvCols) * a.splits_s * 2 : 0);
-  const int units_dn = ((a.D + kGemvCols - 1) / kGemvCols) * (a.splits_dn * a.k + (a.has_shared ? a.splits_s2 : 0));
-  const int grid = std::min(per_sm * num_sms, std::max(units_up, units_dn));
-  if (per_sm < 1 || grid < 1) return cudaErrorNotSupported;
-  e = cudaMemsetAsync(a.barrier, 0, sizeof(unsigned), s);
-  if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kGemvThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_one_token, a);
-}
 
 int gemv_default_splits(int k, int n, int rows_a, int num_sms, int nmat) {
   // the largest power-of-two split that keeps the grid within one wave of two CTAs

@@ -144,28 +144,6 @@ def test_outputs_fully_written_and_deterministic(family):
         assert all(torch.equal(outs[0], o) for o in outs[1:])
 
 
-@pytest.mark.parametrize("family", FAMILIES)
-def test_one_token_layer_kernel_matches_per_stage_kernels(family):
-    """The one-token layer as one cooperative kernel (router, gate/up GEMV, grid
-    barrier, down GEMV, grid barrier, combine) against the per-stage kernels it
-    replaces: the same arithmetic in the same order, so the same bits, with the
-    device router and with given routing, plain and with the fused residual."""
-    from robustgemq_b200 import _lib
-
-    blk, d = block_from_golden(family)
-    x = cuda(d["x_one"])
-    base = _lib.FWD_ONE_TOKEN | (_lib.FWD_FP16_SOFTMAX if blk.fp16_softmax_one_token else 0)
-    for extra in (0, _lib.FWD_RESIDUAL):
-        fused, _ = blk._run(x, base | extra, want_logits=False)
-        split, _ = blk._run(x, base | extra | _lib.FWD_SPLIT_KERNELS, want_logits=False)
-        assert torch.equal(fused, split), extra
-    idx, w = cuda(d["route1_idx"]), cuda(d["route1_w"])
-    fused, _ = blk._run(x, base, want_logits=False, topk_idx=idx, topk_w=w)
-    split, _ = blk._run(x, base | _lib.FWD_SPLIT_KERNELS, want_logits=False, topk_idx=idx, topk_w=w)
-    assert torch.equal(fused, split)
-    assert _lib.device_error() == 0
-
-
 def test_empty_and_single_token_inputs():
     blk, d = block_from_golden("olmoe")
     x0 = torch.empty((1, 0, int(d["D"])), dtype=torch.float16, device="cuda")
