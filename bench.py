@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-configs", action="store_true", help="skip the config 0 / config 3 sub-objects")
+    ap.add_argument("--no-generate", action="store_true", help="skip the whole-model decode sub-object")
     ap.add_argument("--reference-gpu", default="prefill", choices=["none", "prefill", "all"],
                     help="time the reference's own Triton path beside ours (N=1, when baseline/_ref is installed)")
     return ap.parse_args()
@@ -330,7 +331,10 @@ def run_ours(args, rank, world, local_rank):
         cpu0 = cpu_config0(blocks[0])
     ref_gpu = None
     if world == 1 and args.reference_gpu != "none":
-        ref_gpu = run_reference_gpu(args, blocks[0], device)
+        ref_gpu = optional(lambda: run_reference_gpu(args, blocks[0], device))
+    gen = None
+    if not args.no_generate:
+        gen = optional(lambda: run_generate(blocks, device))
     launches = kernel_launches(blocks, batches)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -373,6 +377,8 @@ def run_ours(args, rank, world, local_rank):
         line["cpu_config0"] = cpu0
     if ref_gpu:
         line["reference_gpu"] = ref_gpu
+    if gen:
+        line["generate"] = gen
     return line
 
 
@@ -628,6 +634,44 @@ def run_reference_gpu(args, blk, device):
                      "rel_l2_ours_vs_reference": float(f"{float((y - y_ref).norm() / y_ref.norm()):.3e}"),
                      "reference_first_call_s": round(first_s, 1)}
     return res
+
+
+def optional(fn):
+    """Runs an optional sub-measurement; a failure is reported in the line, not raised."""
+    try:
+        return fn()
+    except Exception as exc:  # the headline measurement must not depend on it
+        import torch
+
+        torch.cuda.synchronize()
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+
+
+def run_generate(blocks, device):
+    """Whole-model decode: an OLMoE-1B-7B-shaped transformers model whose 16 MoE blocks
+    are the decode stack's layers, 4-bit attention projections, static KV cache, the
+    decode step replayed as one CUDA graph; the reference's protocol (9-token prompt,
+    64 new tokens, 3 rounds, benchmark_generate.py:160-230), greedy tokens."""
+    import torch
+
+    from robustgemq_b200.inference.generate import StaticDecoder, synthetic_olmoe
+
+    model = synthetic_olmoe(num_layers=len(blocks), device=device, seed=11, blocks=blocks,
+                            max_position_embeddings=256)
+    prompt = torch.randint(0, model.config.vocab_size, (9,), generator=torch.Generator().manual_seed(9)).to(device)
+    dec = StaticDecoder(model, max_cache_len=9 + 64)
+    dec.generate(prompt, 64)  # capture + warm-up round
+    rounds = [dec.generate(prompt, 64)[1] for _ in range(3)]
+    dec_tps = sorted(r["decode_tokens_per_s"] for r in rounds)[1]
+    pre_tps = sorted(r["prefill_tokens_per_s"] for r in rounds)[1]
+    for layer in model.model.layers:  # the blocks stay owned by the decode stack
+        layer.mlp = None
+    del dec, model
+    torch.cuda.empty_cache()
+    return {"workload": "olmoe-1b-7b-shaped model, 16 MoE layers of this library, 4-bit attention, fp16 "
+                        "embeddings / norms / LM head; 9-token prompt, 64 new tokens, greedy; median of 3 rounds",
+            "decode_tokens_per_s": round(dec_tps, 1), "prefill_tokens_per_s": round(pre_tps, 1),
+            "decode_path": "static KV cache, decode step replayed as one CUDA graph"}
 
 
 # ----------------------------------------------------------------------------- CPU baseline
