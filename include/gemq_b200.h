@@ -256,6 +256,14 @@ int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens,
  * No counterpart in the reference (it has no native timing hooks). */
 int gemq_layer_stage_times(gemq_layer_t* layer, float* ms_out /* host */);
 
+/* Dequant form the tensor-memory GEMM uses for w1, w3, w2 (host int32[3]): 1 = the
+ * single-instruction form, taken when every scale of the projection is a normal fp16
+ * number with s * 2^18 finite (2^16 for 1-bit experts, 2^19 for 3-bit: exponent field
+ * at most 12 / 14 / 11); 0 = the general form. Both give bit-identical weights
+ * (utils.py:206-210). Decided once, when the layer is created. No reference
+ * counterpart (a diagnostic). */
+int gemq_layer_dequant_forms(const gemq_layer_t* layer, int32_t* forms_out /* host */);
+
 #ifdef __cplusplus
 }
 #endif

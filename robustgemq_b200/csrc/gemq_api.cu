@@ -69,6 +69,7 @@ ProjDev to_dev(const gemq_proj_t& p) {
   d.k = p.k;
   d.n = p.n;
   d.group_size = p.group_size;
+  d.sub_ok = 0;  // set by a layer's scale check; one-shot GEMM calls keep the general dequant
   return d;
 }
 
@@ -449,6 +450,13 @@ int gemq_layer_create(const gemq_layer_desc_t* desc, gemq_layer_t** out) {
   L->w1 = to_dev(d.w1);
   L->w3 = to_dev(d.w3);
   L->w2 = to_dev(d.w2);
+  for (ProjDev* pd : {&L->w1, &L->w3, &L->w2}) {
+    const cudaError_t e = scale_exponents_ok(*pd, &pd->sub_ok);
+    if (e != cudaSuccess) {
+      delete L;
+      return cuda_fail(e, "scale exponent check");
+    }
+  }
   L->w3_as_w1 = L->w3;
   L->w3_as_w1.nbits = L->w1.nbits;
   L->w3_as_w1.wq_strides = L->w1.wq_strides;
@@ -1016,6 +1024,14 @@ int gemq_layer_stage_times(gemq_layer_t* layer, float* ms_out) {
     GEMQ_CUDA(cudaEventSynchronize(layer->ev[2 * st + 1]), "stage event");
     GEMQ_CUDA(cudaEventElapsedTime(&ms_out[st], layer->ev[2 * st], layer->ev[2 * st + 1]), "stage time");
   }
+  return GEMQ_OK;
+}
+
+int gemq_layer_dequant_forms(const gemq_layer_t* layer, int32_t* forms_out) {
+  if (layer == nullptr || forms_out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  forms_out[0] = layer->w1.sub_ok;
+  forms_out[1] = layer->w3.sub_ok;
+  forms_out[2] = layer->w2.sub_ok;
   return GEMQ_OK;
 }
 

@@ -86,6 +86,7 @@ struct ProjDev {
   const int32_t* zs_strides;
   int64_t wq_rows;
   int num_experts, k, n, group_size;
+  int sub_ok;  // every scale fits the tensor-memory GEMM's subnormal dequant (scale_exponents_ok)
 };
 
 // Everything a grouped-GEMM launch needs besides tensor maps.
@@ -113,6 +114,12 @@ struct GemmArgs {
 bool tc_gemm_supported(const GemmArgs& a);
 cudaError_t launch_tc_gemm(const GemmArgs& a, cudaStream_t stream);
 cudaError_t launch_simt_gemm(const GemmArgs& a, cudaStream_t stream);
+
+// 1 when every scale of the projection is a normal fp16 number small enough that
+// s * 2^(24 - o) stays finite for its expert's bit-width (b = 1: s < 1; 2, 4: s < 1/4;
+// 3: s < 1/8): the condition of the subnormal dequant form. Synchronous (layer
+// creation); uses a device word of the library, serialised by a host mutex.
+cudaError_t scale_exponents_ok(const ProjDev& p, int* ok);
 
 // Tensor-core GEMM with the dequantised weights in tensor memory (token tiles of
 // 16 / 32 for decode batches, 64 for prefill; kernels_tcd.cu). Its activations are stored in the slot order of

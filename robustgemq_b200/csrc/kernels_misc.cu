@@ -5,6 +5,8 @@
 //   dequant       gemq/triton_kernels/utils.py:192-212
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "gemq_common.cuh"
 #include "gemq_internal.h"
 
@@ -81,6 +83,49 @@ cudaError_t launch_dequant_expert(const ProjDev& p, int expert, uint16_t* out, c
   k_dequant_expert<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(p, expert,
                                                                                reinterpret_cast<__half*>(out));
   return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ scale exponents
+// Largest fp16 exponent field a scale may have for each bit-width so that s * 2^(24 - o)
+// (o the smallest code offset the subnormal form uses) stays finite: b = 1 (o = 8):
+// 14; b = 2, 4 (o = 6): 12; b = 3 (o = 5): 11. The field must also be at least 1
+// (a normal number). One CTA per expert; any scale outside the range sets *bad.
+__device__ unsigned g_scale_check;
+
+__global__ void k_scale_exponents(const ProjDev p, unsigned* bad) {
+  const int e = blockIdx.x;
+  const int nb = p.nbits[e];
+  const int lim = nb == 1 ? 14 : (nb == 2 || nb == 4) ? 12 : nb == 3 ? 11 : 0;
+  const int64_t z0 = p.zs_strides[e];
+  const int64_t n = static_cast<int64_t>(p.k / p.group_size) * p.n;
+  const unsigned short* sc = reinterpret_cast<const unsigned short*>(p.scales);
+  bool out = (lim == 0);
+  for (int64_t i = threadIdx.x; i < n && !out; i += blockDim.x) {
+    const int ex = (sc[z0 + i] >> 10) & 31;
+    out = ex < 1 || ex > lim;
+  }
+  if (out) atomicOr(bad, 1u);
+}
+
+cudaError_t scale_exponents_ok(const ProjDev& p, int* ok) {
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  *ok = 0;
+  if (p.num_experts <= 0 || p.group_size <= 0) return cudaSuccess;
+  const unsigned zero = 0;
+  cudaError_t e = cudaMemcpyToSymbol(g_scale_check, &zero, sizeof(zero));
+  if (e != cudaSuccess) return e;
+  unsigned* flag = nullptr;
+  e = cudaGetSymbolAddress(reinterpret_cast<void**>(&flag), g_scale_check);
+  if (e != cudaSuccess) return e;
+  k_scale_exponents<<<static_cast<unsigned>(p.num_experts), 256>>>(p, flag);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  unsigned bad = 1;
+  e = cudaMemcpyFromSymbol(&bad, g_scale_check, sizeof(bad));  // synchronous
+  if (e != cudaSuccess) return e;
+  *ok = bad == 0 ? 1 : 0;
+  return cudaSuccess;
 }
 
 // ------------------------------------------------------------------ index segments

@@ -67,8 +67,9 @@ __constant__ kperm::Perm3 c_perm3 = kperm::make_perm3();
 __host__ __device__ constexpr int cmin_d(int a, int b) { return a < b ? a : b; }
 __host__ __device__ constexpr int round_up_d(int v, int m) { return (v + m - 1) / m * m; }
 
-template <int NT, GemmMode MODE>
+template <int NT, GemmMode MODE, bool SUB>
 struct CfgD {
+  static constexpr bool kSub = SUB;  // subnormal-operand dequant (see dq_col_sub)
   // Two matrices per work item: w1 and w3 for SwiGLU; for the down projection two
   // adjacent 128-feature tiles of w2, so both modes have the same per-stage shape.
   static constexpr int kMats = 2;
@@ -150,6 +151,7 @@ struct ItemWalk {
 // ---------------------------------------------------------------- dequant
 struct ScaleSet {
   __half2 s0, s1, s01, z0, z1, z01;
+  __half2 t0, t1, t01;  // subnormal form: the scales of the second offset class
 };
 
 // Column C (codes of slots 2C, 2C+1) of a stage as the fma.rn.f16 dequant pair.
@@ -187,21 +189,106 @@ __device__ __forceinline__ uint32_t dq_col(const uint32_t (&w)[kMaxWordRows], co
   }
 }
 
-template <int NB, int PH, bool G2, int C0, int NC, int... Cs>
+// The same column in the subnormal-operand form. The pair is moved (one shift per
+// word and shift amount, shared by the pairs that use it) to mantissa offsets where
+// the fp16 halves, with a zero exponent field, read exactly q * 2^(o - 24); the scales
+// carry the inverse power of two in their exponent, s * 2^(24 - o) (exact: a power of
+// two added to the exponent of a normal number that stays finite). One mask and one
+// fma.rn.f16x2 then give fp16(q * s + z) with its single rounding: the value
+// utils.py:206-210 rounds, so the weights are bit-identical to the magic-number form,
+// with one fp16 instruction per pair instead of two. Offsets: b = 2 at 6 and 8,
+// b = 1 at 8 and 9, b = 4 at 6, b = 3 at (6, 5) per half for (j, j + 5) pairs and
+// (6, 6) for the pairs that straddle words. The launcher takes this form only when
+// every scale of the projection is a normal number with s * 2^(24 - o) finite
+// (scale_exponents_ok).
+template <int NB, int PH, bool G2, int C>
+__device__ __forceinline__ uint32_t dq_col_sub(const uint32_t (&w)[kMaxWordRows], const ScaleSet& sc) {
+  if constexpr (NB == 3) {
+    constexpr kperm::Pair3 pr = kperm::pair3(PH, C);
+    constexpr bool ga = G2 && pr.qa >= 64, gb = G2 && pr.qb >= 64;
+    if constexpr (pr.kind == 0) {
+      const __half2 s2 = ga ? sc.s1 : (gb ? sc.s01 : sc.s0);
+      const __half2 z2 = ga ? sc.z1 : (gb ? sc.z01 : sc.z0);
+      constexpr int sh = 6 - 3 * pr.sa;  // code sa: bit 3 sa -> 6; code sa + 5: bit 15 + 3 sa -> 21
+      const uint32_t x = sh >= 0 ? (w[pr.wa] << sh) : (w[pr.wa] >> (-sh));
+      constexpr uint32_t mask = (7u << 6) | (7u << 21);
+      return h2_as_u32(__hfma2(u32_as_h2(x & mask), s2, z2));
+    } else {
+      const __half2 s2 = ga ? sc.t1 : (gb ? sc.t01 : sc.t0);
+      const __half2 z2 = ga ? sc.z1 : (gb ? sc.z01 : sc.z0);
+      const uint32_t lo = ((w[pr.wa] >> (3 * pr.sa)) & 7u) << 6;
+      const uint32_t hi = ((w[pr.wb] >> (3 * pr.sb)) & 7u) << 22;
+      return h2_as_u32(__hfma2(u32_as_h2(lo | hi), s2, z2));
+    }
+  } else {
+    constexpr int eps = 32 / NB;
+    constexpr int qa = kperm::perm_pow2(NB, 2 * C);
+    constexpr int wi = qa / eps, j = qa % eps;
+    constexpr bool alt = (NB != 4) && (j & 1);  // second offset class (b = 1, 2)
+    constexpr int o = NB == 4 ? 6 : (NB == 2 ? 6 : 8) + (alt ? (NB == 2 ? 2 : 1) : 0);
+    constexpr int sh = o - NB * j;
+    const uint32_t x = sh >= 0 ? (w[wi] << sh) : (w[wi] >> (-sh));
+    constexpr uint32_t cm = (1u << NB) - 1u;
+    constexpr uint32_t mask = (cm << o) | (cm << (o + 16));
+    constexpr bool g1 = G2 && qa >= 64;
+    const __half2 s2 = g1 ? (alt ? sc.t1 : sc.s1) : (alt ? sc.t0 : sc.s0);
+    return h2_as_u32(__hfma2(u32_as_h2(x & mask), s2, g1 ? sc.z1 : sc.z0));
+  }
+}
+
+template <bool SUB, int NB, int PH, bool G2, int C0, int NC, int... Cs>
 __device__ __forceinline__ void dq_cols(const uint32_t (&w)[kMaxWordRows], const ScaleSet& sc, uint32_t (&o)[NC],
                                         std::integer_sequence<int, Cs...>) {
-  ((o[Cs] = dq_col<NB, PH, G2, C0 + Cs>(w, sc)), ...);
+  if constexpr (SUB) ((o[Cs] = dq_col_sub<NB, PH, G2, C0 + Cs>(w, sc)), ...);
+  else ((o[Cs] = dq_col<NB, PH, G2, C0 + Cs>(w, sc)), ...);
 }
 
 // Dequantises columns [C0, C0 + NC) of a stage and stores them to TMEM at `taddr`.
 // Stored 16 columns at a time, so that only 16 results are live at once.
-template <int NB, int PH, bool G2, int C0, int NC>
+template <bool SUB, int NB, int PH, bool G2, int C0, int NC>
 __device__ __forceinline__ void dq_store(const uint32_t (&w)[kMaxWordRows], const ScaleSet& sc, uint32_t taddr) {
   static_assert(NC % 16 == 0, "columns are stored 16 at a time");
   uint32_t o[16];
-  dq_cols<NB, PH, G2, C0, 16>(w, sc, o, std::make_integer_sequence<int, 16>{});
+  dq_cols<SUB, NB, PH, G2, C0, 16>(w, sc, o, std::make_integer_sequence<int, 16>{});
   tmem_st16(taddr, o);
-  if constexpr (NC > 16) dq_store<NB, PH, G2, C0 + 16, NC - 16>(w, sc, taddr + 16u);
+  if constexpr (NC > 16) dq_store<SUB, NB, PH, G2, C0 + 16, NC - 16>(w, sc, taddr + 16u);
+}
+
+// fp16 bits of h with k added to the exponent field (h * 2^k for a normal h whose
+// result stays finite), as the low / high halves of a pair
+__device__ __forceinline__ __half2 exp_pair(__half lo, int klo, __half hi, int khi) {
+  const uint32_t a = static_cast<uint32_t>(__half_as_ushort(lo)) + (static_cast<uint32_t>(klo) << 10);
+  const uint32_t b = static_cast<uint32_t>(__half_as_ushort(hi)) + (static_cast<uint32_t>(khi) << 10);
+  return u32_as_h2((a & 0xffffu) | (b << 16));
+}
+
+// Scale / zero registers of a stage for either dequant form.
+template <bool SUB, int NB>
+__device__ __forceinline__ ScaleSet make_scales(__half sa, __half za, __half sb, __half zb) {
+  ScaleSet sc;
+  sc.z0 = __halves2half2(za, za);
+  sc.z1 = __halves2half2(zb, zb);
+  sc.z01 = __halves2half2(za, zb);
+  if constexpr (!SUB) {
+    sc.s0 = __halves2half2(sa, sa);
+    sc.s1 = __halves2half2(sb, sb);
+    sc.s01 = __halves2half2(sa, sb);
+  } else if constexpr (NB == 3) {
+    sc.s0 = exp_pair(sa, 18, sa, 19);
+    sc.s1 = exp_pair(sb, 18, sb, 19);
+    sc.s01 = exp_pair(sa, 18, sb, 19);
+    sc.t0 = exp_pair(sa, 18, sa, 18);
+    sc.t1 = exp_pair(sb, 18, sb, 18);
+    sc.t01 = exp_pair(sa, 18, sb, 18);
+  } else {
+    constexpr int k0 = NB == 1 ? 16 : 18;               // offset 8 (b = 1) / 6 (b = 2, 4)
+    constexpr int k1 = NB == 1 ? 15 : (NB == 2 ? 16 : 18);  // offset 9 / 8
+    sc.s0 = exp_pair(sa, k0, sa, k0);
+    sc.s1 = exp_pair(sb, k0, sb, k0);
+    sc.t0 = exp_pair(sa, k1, sa, k1);
+    sc.t1 = exp_pair(sb, k1, sb, k1);
+  }
+  return sc;
 }
 
 // Ring positions and barriers a dequant warp walks through; advanced in place.
@@ -324,24 +411,19 @@ __device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
       if (!warp_wait_tok(Bar::aempty(e.bars, r.as), r.aph ^ 1u, tok_a, kDevTimeoutAEmpty, kBusySleepNs))
         return false;
       tc_fence_after();
-      ScaleSet sc;
-      sc.s0 = __halves2half2(cur.sa, cur.sa);
-      sc.z0 = __halves2half2(cur.za, cur.za);
-      sc.s1 = __halves2half2(cur.sb, cur.sb);
-      sc.z1 = __halves2half2(cur.zb, cur.zb);
-      sc.s01 = __halves2half2(cur.sa, cur.sb);
-      sc.z01 = __halves2half2(cur.za, cur.zb);
+      constexpr bool kSub = C::kSub;
+      const ScaleSet sc = make_scales<kSub, NB>(cur.sa, cur.za, cur.sb, cur.zb);
       const uint32_t taddr = e.a_col0 + static_cast<uint32_t>(r.as * C::kACols + e.mat * 64 + C0);
       if constexpr (NB == 3) {
         switch (ph3) {
-          case 0: dq_store<3, 0, G2, C0, NC>(cur.w, sc, taddr); break;
-          case 1: dq_store<3, 1, G2, C0, NC>(cur.w, sc, taddr); break;
-          case 2: dq_store<3, 2, G2, C0, NC>(cur.w, sc, taddr); break;
-          case 3: dq_store<3, 3, G2, C0, NC>(cur.w, sc, taddr); break;
-          default: dq_store<3, 4, G2, C0, NC>(cur.w, sc, taddr); break;
+          case 0: dq_store<kSub, 3, 0, G2, C0, NC>(cur.w, sc, taddr); break;
+          case 1: dq_store<kSub, 3, 1, G2, C0, NC>(cur.w, sc, taddr); break;
+          case 2: dq_store<kSub, 3, 2, G2, C0, NC>(cur.w, sc, taddr); break;
+          case 3: dq_store<kSub, 3, 3, G2, C0, NC>(cur.w, sc, taddr); break;
+          default: dq_store<kSub, 3, 4, G2, C0, NC>(cur.w, sc, taddr); break;
         }
       } else {
-        dq_store<NB, 0, G2, C0, NC>(cur.w, sc, taddr);
+        dq_store<kSub, NB, 0, G2, C0, NC>(cur.w, sc, taddr);
       }
       // first poll of the A slot of this warp's next stage (two positions on), in
       // flight with the stores. No false positive from an older phase: this warp's
@@ -402,12 +484,12 @@ __device__ __forceinline__ int perm_dst(int nb, int f) {
 __device__ __forceinline__ float silu_ref_d(float x) { return x / (1.f + expf(-x)); }
 
 // ---------------------------------------------------------------- the kernel
-template <int NT, GemmMode MODE>
+template <int NT, GemmMode MODE, bool SUB>
 __global__ void __launch_bounds__(kThreadsD, 1)
     k_moe_tcd(const KArgsD p, const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ WordMapsD tm_words,
               const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ CUtensorMap tm_z0,
               const __grid_constant__ CUtensorMap tm_s1, const __grid_constant__ CUtensorMap tm_z1) {
-  using C = CfgD<NT, MODE>;
+  using C = CfgD<NT, MODE, SUB>;
   constexpr int kMats = C::kMats;
   constexpr int kStages = C::kStages;
   constexpr int kAStages = C::kAStages;
@@ -745,9 +827,9 @@ bool make_word_maps_d(CUtensorMap (&maps)[4], const ProjDev& w) {
   return true;
 }
 
-template <int NT, GemmMode MODE>
+template <int NT, GemmMode MODE, bool SUB>
 cudaError_t launch_d(const GemmArgs& a, cudaStream_t stream) {
-  using C = CfgD<NT, MODE>;
+  using C = CfgD<NT, MODE, SUB>;
   CUtensorMap m_act, m_s0, m_z0, m_s1, m_z1;
   WordMapsD words;
   const int K = a.w0.k;
@@ -791,7 +873,7 @@ cudaError_t launch_d(const GemmArgs& a, cudaStream_t stream) {
   p.out_ld = a.out_ld;
   p.row_weight = reinterpret_cast<const __half*>(a.row_weight);
   p.perm_out_nbits = a.perm_out_nbits;
-  auto kern = k_moe_tcd<NT, MODE>;
+  auto kern = k_moe_tcd<NT, MODE, SUB>;
   // set once per instantiation and device (outside any graph capture)
   static std::atomic<size_t> smem_done[kMaxDevices];
   if (cudaError_t err = raise_smem_limit(kern, static_cast<size_t>(C::kSmemBytes), smem_done); err != cudaSuccess)
@@ -820,16 +902,21 @@ bool tcd_gemm_supported(const GemmArgs& a) {
   return (reinterpret_cast<uintptr_t>(a.act) & 15u) == 0;
 }
 
+template <int NT>
+cudaError_t launch_nt_d(const GemmArgs& a, bool sub, cudaStream_t stream) {
+  if (a.mode == GemmMode::kSwiGLU)
+    return sub ? launch_d<NT, GemmMode::kSwiGLU, true>(a, stream) : launch_d<NT, GemmMode::kSwiGLU, false>(a, stream);
+  return sub ? launch_d<NT, GemmMode::kRouteWeight, true>(a, stream)
+             : launch_d<NT, GemmMode::kRouteWeight, false>(a, stream);
+}
+
 cudaError_t launch_tcd_gemm(const GemmArgs& a, cudaStream_t stream) {
   if (!tcd_gemm_supported(a)) return cudaErrorNotSupported;
-  if (a.nt == kNtTiny)
-    return a.mode == GemmMode::kSwiGLU ? launch_d<kNtTiny, GemmMode::kSwiGLU>(a, stream)
-                                       : launch_d<kNtTiny, GemmMode::kRouteWeight>(a, stream);
-  if (a.nt == kNtMid)
-    return a.mode == GemmMode::kSwiGLU ? launch_d<kNtMid, GemmMode::kSwiGLU>(a, stream)
-                                       : launch_d<kNtMid, GemmMode::kRouteWeight>(a, stream);
-  return a.mode == GemmMode::kSwiGLU ? launch_d<kNtSmall, GemmMode::kSwiGLU>(a, stream)
-                                     : launch_d<kNtSmall, GemmMode::kRouteWeight>(a, stream);
+  // the subnormal dequant form when every scale of the projection(s) allows it
+  const bool sub = a.w0.sub_ok != 0 && (a.mode != GemmMode::kSwiGLU || a.w1.sub_ok != 0);
+  if (a.nt == kNtTiny) return launch_nt_d<kNtTiny>(a, sub, stream);
+  if (a.nt == kNtMid) return launch_nt_d<kNtMid>(a, sub, stream);
+  return launch_nt_d<kNtSmall>(a, sub, stream);
 }
 
 // Source column of destination column k of an activation row stored in the decode
