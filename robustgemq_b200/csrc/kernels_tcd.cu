@@ -481,7 +481,14 @@ __device__ __forceinline__ int perm_dst(int nb, int f) {
 }
 
 // ---------------------------------------------------------------- epilogue math
-__device__ __forceinline__ float silu_ref_d(float x) { return x / (1.f + expf(-x)); }
+// F.silu in fp32 from the hardware exponential and reciprocal: within a few fp32 ulps
+// of x / (1 + exp(-x)); the caller rounds it to fp16, as torch does, so the two differ
+// only where the exact value sits within those ulps of an fp16 rounding midpoint
+// (one fp16 ulp there; the exponential's error grows with |x|, to about 14 ulps at
+// |x| = 10). The exponent is clamped at 80 so the divisor stays below 2^126, where
+// the fast quotient is defined; silu(x) for x < -80 has magnitude below 2^-100 and
+// rounds to -0 in fp16 either way.
+__device__ __forceinline__ float silu_fast_d(float x) { return __fdividef(x, 1.f + __expf(fminf(-x, 80.f))); }
 
 // ---------------------------------------------------------------- the kernel
 template <int NT, GemmMode MODE, bool SUB>
@@ -704,57 +711,73 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       const uint32_t lane_base =
           tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * C::kAccCols);
       const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
+      // routing weights of the item's rows, before the wait: lane j holds rows 2j and
+      // 2j + 1 as an fp16 pair (loads issued together here, not one per row behind
+      // the output stores, which the compiler may not move them past)
+      uint32_t wpair = 0;
+      if constexpr (MODE == GemmMode::kRouteWeight) {
+        const int r = 2 * lane;
+        const __half wa = r < wk.rows ? p.row_weight[wk.out_row + r] : __ushort_as_half(0);
+        const __half wb = r + 1 < wk.rows ? p.row_weight[wk.out_row + r + 1] : __ushort_as_half(0);
+        wpair = h2_as_u32(__halves2half2(wa, wb));
+      }
       if (!warp_wait(&acc_full[buf], (it / C::kAccBufs) & 1, kDevTimeoutAccFull, kIdleSleepNs)) break;
       tc_fence_after();
       __half* out = static_cast<__half*>(p.out);
-      if constexpr (MODE == GemmMode::kSwiGLU) {
-        const int f = wk.n0 + 32 * q + lane;
-        const int col =
-            (p.perm_out_nbits != nullptr) ? perm_dst(min(max(__ldg(p.perm_out_nbits + wk.e), 1), 4), f) : f;
+      // 16 token columns at a time; the accumulator buffer goes back to the MMA issuer
+      // as soon as the item's last columns are in registers. Two tokens per step, as
+      // fp16 pairs: fp16(a) * fp16(b) rounded once to fp16 is the fp32 product
+      // rounded to fp16 (the product of two fp16 numbers is exact in fp32).
+      const int nck = (min(wk.rows, NT) + 15) >> 4;  // warp-uniform
+      if (nck == 0) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      }
+      const int f = (MODE == GemmMode::kSwiGLU ? wk.n0 : 2 * wk.n0) + 32 * q + lane;
+      int col = f;
+      if constexpr (MODE == GemmMode::kSwiGLU)
+        if (p.perm_out_nbits != nullptr) col = perm_dst(min(max(__ldg(p.perm_out_nbits + wk.e), 1), 4), f);
 #pragma unroll
-        for (int c0 = 0; c0 < NT; c0 += 16) {
-          if (c0 >= wk.rows) break;  // warp-uniform
-          uint32_t r0[16], r1[16];
-          tmem_ld16(lane_base + c0, r0);
-          tmem_ld16(lane_base + NT + c0, r1);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            if (c0 + i < wk.rows) {
-              // x1, x3 stored fp16; F.silu(x1) -> fp16; * x3 -> fp16 (moe_block.py:774-775)
-              const float x1 = __half2float(__float2half_rn(__uint_as_float(r0[i])));
-              const float x3 = __half2float(__float2half_rn(__uint_as_float(r1[i])));
-              const float sl = __half2float(__float2half_rn(silu_ref_d(x1)));
-              out[static_cast<int64_t>(wk.out_row + c0 + i) * p.out_ld + col] = __float2half_rn(sl * x3);
-            }
-          }
+      for (int ck = 0; ck < NT / 16; ++ck) {
+        if (ck >= nck) break;
+        const int c0 = 16 * ck;
+        uint32_t r0[16], r1[16];
+        tmem_ld16(lane_base + c0, r0);
+        tmem_ld16(lane_base + NT + c0, r1);
+        tmem_ld_wait();
+        if (ck == nck - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
-      } else {
-        // two feature tiles: y = fp16(acc), y * w -> fp16 (moe_block.py:778, 811)
-        const int f0 = 2 * wk.n0 + 32 * q + lane;
 #pragma unroll
-        for (int c0 = 0; c0 < NT; c0 += 16) {
-          if (c0 >= wk.rows) break;  // warp-uniform
-          uint32_t r0[16], r1[16];
-          tmem_ld16(lane_base + c0, r0);
-          tmem_ld16(lane_base + NT + c0, r1);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            if (c0 + i < wk.rows) {
-              const int64_t row = wk.out_row + c0 + i;
-              const float wt = __half2float(p.row_weight[row]);
-              const float y0 = __half2float(__float2half_rn(__uint_as_float(r0[i])));
-              const float y1 = __half2float(__float2half_rn(__uint_as_float(r1[i])));
-              out[row * p.out_ld + f0] = __float2half_rn(y0 * wt);
-              out[row * p.out_ld + f0 + 128] = __float2half_rn(y1 * wt);
+        for (int i = 0; i < 16; i += 2) {
+          const int64_t row = wk.out_row + c0 + i;
+          const bool v0 = c0 + i < wk.rows, v1 = c0 + i + 1 < wk.rows;
+          const __half2 a0 = __floats2half2_rn(__uint_as_float(r0[i]), __uint_as_float(r0[i + 1]));
+          const __half2 a1 = __floats2half2_rn(__uint_as_float(r1[i]), __uint_as_float(r1[i + 1]));
+          if constexpr (MODE == GemmMode::kSwiGLU) {
+            // x1, x3 stored fp16; F.silu(x1) -> fp16; * x3 -> fp16 (moe_block.py:774-775)
+            const float2 x1 = __half22float2(a0);
+            const __half2 h = __hmul2(__floats2half2_rn(silu_fast_d(x1.x), silu_fast_d(x1.y)), a1);
+            if (v0) out[row * p.out_ld + col] = __low2half(h);
+            if (v1) out[(row + 1) * p.out_ld + col] = __high2half(h);
+          } else {
+            // two feature tiles: y = fp16(acc), y * w -> fp16 (moe_block.py:778, 811)
+            const __half2 wv = u32_as_h2(__shfl_sync(0xffffffffu, wpair, (c0 + i) >> 1));
+            const __half2 y0 = __hmul2(a0, wv), y1 = __hmul2(a1, wv);
+            if (v0) {
+              out[row * p.out_ld + col] = __low2half(y0);
+              out[row * p.out_ld + col + 128] = __low2half(y1);
+            }
+            if (v1) {
+              out[(row + 1) * p.out_ld + col] = __high2half(y0);
+              out[(row + 1) * p.out_ld + col + 128] = __high2half(y1);
             }
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   } else {
     // ------------------------------------------------------------ dequant
