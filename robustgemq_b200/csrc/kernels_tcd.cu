@@ -26,9 +26,10 @@
 //   2      producer: activation sub-tile 1 (k0+64..k0+127) and words of matrix 1
 //   3      producer: scale / zero chunks
 //   4-7    epilogue: tcgen05.ld -> rounding -> global stores (lane quarter = warp % 4)
-//   8-23   dequant: two groups of 8 warps taking alternate stages (group (w-8)/8 the
-//          stages kt with kt % 2 == group); in a group, warp w owns features
-//          32*(w%4) .. +31 (its TMEM lane quarter) of matrix ((w-8)/4)%2, all 128 k
+//   8-23   dequant: two groups of 8 warps taking alternate stages of the CTA's whole
+//          stage sequence (group (w-8)/8 the even / odd ones); in a group, warp w
+//          owns features 32*(w%4) .. +31 (its TMEM lane quarter) of matrix
+//          ((w-8)/4)%2, all 128 k
 // Every wait is bounded (gemq_common.cuh); on expiry all roles drain and return.
 #include <cudaTypedefs.h>
 
@@ -381,31 +382,39 @@ __device__ __forceinline__ bool dq_fetch(int kt, DqStage& d, bool tok, int ch, c
 }
 
 // One work item of one dequant warp, specialised by bit-width, group layout and the
-// warp's columns [C0, C0 + NC) of its matrix. The warp takes the stages of its group
-// (kt = grp, grp + 2, ...): read the packed words and scale / zero of its feature
-// row, release the stage, dequantise into TMEM and hand the A stage to the MMA. The
-// first poll of its next stage's A slot is issued while the TMEM stores are in
-// flight. Ring positions, scale chunk and 3-bit phase advance on every stage.
+// warp's columns [C0, C0 + NC) of its matrix. The two groups take alternate stages
+// of the CTA's whole sequence of stages (all its items back to back), so this warp's
+// stages in the item are kt0, kt0 + 2, ... with kt0 = (grp + stages before the item)
+// % 2. For each: read the packed words and scale / zero of its feature row, release
+// the stage, dequantise into TMEM and hand the A stage to the MMA. The first poll of
+// its next stage's A slot is issued while the TMEM stores are in flight. Ring
+// positions (two per own stage) stay on this warp's next own stage across items.
+//
+// The A slot waits are parity tests, unambiguous only while the slot's reads lag the
+// position waited for by at most one round: the MMA must have read position
+// P - 2 * kAStages. It reads positions in order, and once this warp's wait for
+// position Q has passed it has read every position up to Q - kAStages. This warp
+// waits (and polls) positions two apart, in this item or the next, so kAStages >= 2
+// is enough. (Restarting each item at kt = grp would make group 1 jump three
+// positions after an item with an odd stage count.)
 // Returns false if a wait expired.
 template <class C, int NB, bool G2, int C0, int NC>
-__device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
+__device__ __forceinline__ bool dq_item(int kt0, DqRings& r, const DqEnv& e) {
   using Bar = BarsD<C>;
   int ch = -1;
-  // 3-bit phase index: P = (128 kt) % 10 = 0, 8, 6, 4, 2 -> index 0, 4, 3, 2, 1
-  int ph3 = (e.grp == 0) ? 0 : 4;
+  // 3-bit phase index of stage kt: P = (128 kt) % 10 = 0, 8, 6, 4, 2 -> P / 2
+  int ph3 = ((kSK * kt0) % 10) / 2;
   bool tok_a = false;
-  // this warp's ring positions start at its group's first stage
-  if (e.grp == 1) {
-    if (++r.s == C::kStages) { r.s = 0; r.ph ^= 1u; }
-    if (++r.as == C::kAStages) { r.as = 0; r.aph ^= 1u; }
-  }
-  // the group's stages only (each chunk of 16 scale groups spans at least two
-  // stages, so both groups visit, and release, every chunk)
-  for (int kt = e.grp; kt < e.KT; kt += 2) {
+  // the group's stages only (every chunk of 16 scale groups either holds stages of
+  // both groups or is passed over and released by dq_chunk_to)
+  for (int kt = kt0; kt < e.KT; kt += 2) {
     if (!dq_chunk_to<C>(chunk_of(kt, e.log2g), true, ch, r, e)) return false;
     {
       const bool tok_f = mbar_try_wait(Bar::full(e.bars, r.s), r.ph);
-      if (kt < 2) tok_a = mbar_try_wait(Bar::aempty(e.bars, r.as), r.aph ^ 1u);  // item's first own stage
+      // item's first own stage: poll its A slot before the fetch. With two slots that
+      // slot's last use is this warp's previous stage, still being read by the MMA, and
+      // the try_wait would hold the fetch back: the fetch goes first then.
+      if (C::kAStages > 2 && kt == kt0) tok_a = mbar_try_wait(Bar::aempty(e.bars, r.as), r.aph ^ 1u);
       DqStage cur;
       if (!dq_fetch<C, NB, G2>(kt, cur, tok_f, ch, r, e)) return false;
       if (!warp_wait_tok(Bar::aempty(e.bars, r.as), r.aph ^ 1u, tok_a, kDevTimeoutAEmpty, kBusySleepNs))
@@ -426,14 +435,16 @@ __device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
         dq_store<kSub, NB, 0, G2, C0, NC>(cur.w, sc, taddr);
       }
       // first poll of the A slot of this warp's next stage (two positions on), in
-      // flight with the stores. No false positive from an older phase: this warp's
-      // wait above saw the MMA finish position - 3, hence also the slot's use before
-      // last (position - 4).
-      {
+      // flight with the stores; unambiguous as the waits are (see dq_item). With two
+      // A slots that is the slot just written, which the MMA cannot release before
+      // this warp hands it over: no poll then (try_wait may block until a time limit).
+      if constexpr (C::kAStages > 2) {
         int as2 = r.as + 2;
         uint32_t aph2 = r.aph;
         if (as2 >= C::kAStages) { as2 -= C::kAStages; aph2 ^= 1u; }
         tok_a = mbar_try_wait(Bar::aempty(e.bars, as2), aph2 ^ 1u);
+      } else {
+        tok_a = false;
       }
       tmem_st_wait();
       tc_fence_before();
@@ -447,30 +458,24 @@ __device__ __forceinline__ bool dq_item(DqRings& r, const DqEnv& e) {
     if (r.as >= C::kAStages) { r.as -= C::kAStages; r.aph ^= 1u; }
     if constexpr (NB == 3) ph3 = (ph3 + 3) % 5;
   }
-  // ring positions end at the item's end: back off the overshoot past KT
-  const int over = (e.KT - e.grp + 1) / 2 * 2 + e.grp - e.KT;  // stages walked past KT (0 or 1)
-  if (over == 1) {
-    if (--r.s < 0) { r.s += C::kStages; r.ph ^= 1u; }
-    if (--r.as < 0) { r.as += C::kAStages; r.aph ^= 1u; }
-  }
   // release the item's remaining scale chunks, through its last
   dq_chunk_to<C>(chunk_of(e.KT - 1, e.log2g) + 1, false, ch, r, e);
   return true;
 }
 
 template <class C, bool G2, int C0, int NC>
-__device__ __forceinline__ bool dq_item_nb(int nb, DqRings& r, const DqEnv& e) {
+__device__ __forceinline__ bool dq_item_nb(int nb, int kt0, DqRings& r, const DqEnv& e) {
   switch (nb) {
-    case 1: return dq_item<C, 1, G2, C0, NC>(r, e);
-    case 2: return dq_item<C, 2, G2, C0, NC>(r, e);
-    case 3: return dq_item<C, 3, G2, C0, NC>(r, e);
-    default: return dq_item<C, 4, G2, C0, NC>(r, e);
+    case 1: return dq_item<C, 1, G2, C0, NC>(kt0, r, e);
+    case 2: return dq_item<C, 2, G2, C0, NC>(kt0, r, e);
+    case 3: return dq_item<C, 3, G2, C0, NC>(kt0, r, e);
+    default: return dq_item<C, 4, G2, C0, NC>(kt0, r, e);
   }
 }
 
 template <class C, int C0, int NC>
-__device__ __forceinline__ bool dq_item_any(bool g2, int nb, DqRings& r, const DqEnv& e) {
-  return g2 ? dq_item_nb<C, true, C0, NC>(nb, r, e) : dq_item_nb<C, false, C0, NC>(nb, r, e);
+__device__ __forceinline__ bool dq_item_any(bool g2, int nb, int kt0, DqRings& r, const DqEnv& e) {
+  return g2 ? dq_item_nb<C, true, C0, NC>(nb, kt0, r, e) : dq_item_nb<C, false, C0, NC>(nb, kt0, r, e);
 }
 
 // Destination column of source column f of the next projection's input.
@@ -795,16 +800,16 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     env.KT = KT;
     env.log2g = 31 - __clz(g);
     const bool g2 = (g == 64);
-    DqRings rings{0, 0, 0, 0u, 0u, 0u};
+    // group 1 starts at the CTA's second stage
+    DqRings rings{env.grp, env.grp, 0, 0u, 0u, 0u};
     ItemWalk items(total);
     int w;
-    while (items.next(w)) {
+    for (int it = 0; items.next(w); ++it) {
       const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
       if ((wk.nb < 1 || wk.nb > 4) && dw == 0 && lane == 0) set_device_error(kDevBadBits);
       const int nb = min(max(wk.nb, 1), 4);
-      bool ok;
-      ok = dq_item_any<C, 0, 64>(g2, nb, rings, env);
-      if (!ok) break;
+      const int kt0 = (env.grp + it * KT) & 1;  // first own stage of the item
+      if (!dq_item_any<C, 0, 64>(g2, nb, kt0, rings, env)) break;
     }
   }
 
