@@ -7,6 +7,7 @@
 //   combine    gemq/inference/moe_block.py:799-812 (fp16 index_add_ in ascending expert order)
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cfloat>
 
 #include "gemq_common.cuh"
@@ -24,54 +25,53 @@ namespace {
 constexpr int kMaxExperts = 256;
 
 // Top-k of one token's probabilities v (slot i of lane l = expert 32 i + l; NV slots
-// in use) by rank: a value's rank is the number of values ahead of it in the order
-// "larger probability first, lower expert id on ties" (NaN ahead of every number:
-// torch.topk's order), so the values of rank < k are the top k, in order. All
-// comparisons run at once instead of k rounds of an argmax. The selected weights
-// are summed in rank order (the order of the k-round selection), then lane r writes
-// the rank-r expert and its (renormalised) weight.
+// in use) in k rounds of a warp argmax, in the order "larger probability first,
+// lower expert id on ties", NaN ahead of every number (torch.topk's order). Each
+// value has an unsigned key that orders the same way: the probability's bits + 1
+// (non-negative floats order as their bits; a NaN counts as FLT_MAX, a zero of
+// either sign as +0), 0 for a slot out of range or already taken. A round takes the
+// warp maximum of the lanes' best keys, then the lowest expert id holding it (two
+// redux.sync). The selected weights are summed in selection order, then lane r
+// writes the rank-r expert and its (renormalised) weight.
 template <int NV>
 __device__ __forceinline__ void select_topk(const float (&v)[kMaxExperts / 32], int E, int k, int norm,
                                             int fp16_softmax, int32_t* __restrict__ idx_out,
                                             __half* __restrict__ w_out) {
   const int lane = threadIdx.x & 31;
-  auto key = [](float a) { return (a != a) ? FLT_MAX : a; };
-  float m[NV];
-  int rank[NV];
+  uint32_t key[NV];
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    m[i] = key(v[i]);
-    rank[i] = 0;
-  }
-#pragma unroll
-  for (int jo = 0; jo < NV; ++jo) {
-#pragma unroll 8
-    for (int src = 0; src < 32; ++src) {
-      const float o = __shfl_sync(0xffffffffu, m[jo], src);
-      const int oe = jo * 32 + src;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int e = i * 32 + lane;
-        rank[i] += (oe < E && (o > m[i] || (o == m[i] && oe < e))) ? 1 : 0;
-      }
-    }
+    const uint32_t bits = __float_as_uint(v[i] != v[i] ? FLT_MAX : v[i]);
+    key[i] = (i * 32 + lane >= E) ? 0u : (bits & 0x80000000u) ? 1u : bits + 1u;
   }
   float wsum = 0.f, myw = 0.f;
   int mye = 0;
   for (int r = 0; r < k; ++r) {
+    uint32_t best = 0u;
+    int bi = 0;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const unsigned b = __ballot_sync(0xffffffffu, i * 32 + lane < E && rank[i] == r);
-      if (b != 0u) {  // warp-uniform
-        const int src = __ffs(b) - 1;
-        const float val = __shfl_sync(0xffffffffu, v[i], src);
-        wsum += val;
-        if (lane == r) {
-          myw = val;
-          mye = i * 32 + src;
-        }
-        break;
+      if (key[i] > best) {  // strict: the lowest slot (expert id) of the lane on ties
+        best = key[i];
+        bi = i;
       }
+    }
+    const uint32_t wmax = __reduce_max_sync(0xffffffffu, best);
+    if (wmax == 0u) break;  // fewer valid experts than k (warp-uniform)
+    const uint32_t win = __reduce_min_sync(0xffffffffu, best == wmax ? static_cast<uint32_t>(bi * 32 + lane) : ~0u);
+    float mine = v[0];
+#pragma unroll
+    for (int i = 1; i < NV; ++i) mine = (bi == i) ? v[i] : mine;
+    const int src = static_cast<int>(win & 31u);
+    const float val = __shfl_sync(0xffffffffu, mine, src);
+    wsum += val;
+    if (lane == r) {
+      myw = val;
+      mye = static_cast<int>(win);
+    }
+    if (lane == src) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) key[i] = (i == bi) ? 0u : key[i];
     }
   }
   if (lane < k) {
@@ -212,15 +212,11 @@ __global__ void __launch_bounds__(256) k_gate_logits(const __half* __restrict__ 
   }
 }
 
-// Copies token row `src` to `dst` (D fp16, D % 8 == 0) by one warp: as is, or in
-// the decode GEMM's K slot order for bit-width nb (kperm.cuh; D % 128 == 0 then),
-// gathering through the warp's staging buffer `sbuf` (D halves of shared memory) and
-// the 3-bit slot table `fwd3` staged in shared memory (lanes index it divergently).
-__device__ __forceinline__ void copy_row(const __half* __restrict__ src, __half* __restrict__ dst, int D, int nb,
-                                         int lane, __half* sbuf, const uint8_t (*fwd3)[128]) {
+// Loads token row `src` (D fp16, D % 8 == 0) into the warp's staging buffer `sbuf`
+// (D halves of shared memory), each lane's 16-byte chunks of a batch of 8 in flight
+// together.
+__device__ __forceinline__ void stage_row(const __half* __restrict__ src, __half* sbuf, int D, int lane) {
   const uint4* s4 = reinterpret_cast<const uint4*>(src);
-  uint4* d4 = reinterpret_cast<uint4*>(dst);
-  // each lane's loads of a batch of 8 chunks go out before any store
   uint4* b4 = reinterpret_cast<uint4*>(sbuf);
   for (int base = lane; base < D / 8; base += 8 * 32) {
     uint4 t[8];
@@ -228,39 +224,85 @@ __device__ __forceinline__ void copy_row(const __half* __restrict__ src, __half*
     for (int j = 0; j < 8; ++j)
       if (base + 32 * j < D / 8) t[j] = s4[base + 32 * j];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (base + 32 * j < D / 8) {
-        if (nb == 0) d4[base + 32 * j] = t[j];
-        else b4[base + 32 * j] = t[j];
-      }
-    }
+    for (int j = 0; j < 8; ++j)
+      if (base + 32 * j < D / 8) b4[base + 32 * j] = t[j];
   }
-  if (nb == 0) return;
   __syncwarp();
+}
+
+// Writes the staged row to `dst` by one warp: as is (nb = 0), or in the decode
+// GEMM's K slot order for bit-width nb (kperm.cuh; D % 128 == 0 then), gathered
+// through the 3-bit slot table `fwd3` staged in shared memory (lanes index it
+// divergently).
+__device__ __forceinline__ void store_row(const __half* sbuf, __half* __restrict__ dst, int D, int nb, int lane,
+                                          const uint8_t (*fwd3)[128]) {
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+  if (nb == 0) {
+    const uint4* b4 = reinterpret_cast<const uint4*>(sbuf);
+    for (int i = lane; i < D / 8; i += 32) d4[i] = b4[i];
+    return;
+  }
   const unsigned short* b16 = reinterpret_cast<const unsigned short*>(sbuf);
   // b in {1, 2, 4}: eps = 32 / b codes per word, slot 2j + h of a word block <-> code
   // j + h * eps / 2 (kperm::perm_pow2), with shifts and masks instead of divisions
   const int lg_eps = 5 - (nb >> 1);  // nb = 1, 2, 4 -> 5, 4, 3
   const int eps_mask = (1 << lg_eps) - 1, half = 1 << (lg_eps - 1);
-  for (int i = lane; i < D / 8; i += 32) {
+  auto chunk = [&](int i) {
     const int k0 = 8 * i, st = k0 >> 7;
     const unsigned short* row = b16 + (st << 7);
-    uint32_t v[4];
     if (nb == 3) {
-      const uint8_t* f = fwd3[kperm::phase3(st)] + (k0 & 127);
-#pragma unroll
-      for (int m = 0; m < 4; ++m)
-        v[m] = static_cast<uint32_t>(row[f[2 * m]]) | (static_cast<uint32_t>(row[f[2 * m + 1]]) << 16);
-    } else {
+      const uint2 fw = *reinterpret_cast<const uint2*>(fwd3[kperm::phase3(st)] + (k0 & 127));
+      uint32_t v[4];
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        const int sa = (k0 + 2 * m) & 127;  // even slot: code j, odd slot sa + 1: code j + eps / 2
-        const int a = (sa & ~eps_mask) + ((sa & eps_mask) >> 1);
-        v[m] = static_cast<uint32_t>(row[a]) | (static_cast<uint32_t>(row[a + half]) << 16);
+        const uint32_t f = m < 2 ? fw.x : fw.y;
+        const int sh = 16 * (m & 1);
+        v[m] = static_cast<uint32_t>(row[(f >> sh) & 0xffu]) | (static_cast<uint32_t>(row[(f >> (sh + 8)) & 0xffu]) << 16);
       }
+      return make_uint4(v[0], v[1], v[2], v[3]);
     }
-    d4[i] = make_uint4(v[0], v[1], v[2], v[3]);
+    // slots 2m, 2m + 1 of the chunk hold codes j0 + m and j0 + m + eps / 2 of its word
+    // block: two runs of four consecutive halves (8-byte aligned), interleaved
+    const int sa = k0 & 127;
+    const int a = (sa & ~eps_mask) + ((sa & eps_mask) >> 1);
+    const uint2 lo = *reinterpret_cast<const uint2*>(row + a);
+    const uint2 hi = *reinterpret_cast<const uint2*>(row + a + half);
+    return make_uint4(__byte_perm(lo.x, hi.x, 0x5410), __byte_perm(lo.x, hi.x, 0x7632),
+                      __byte_perm(lo.y, hi.y, 0x5410), __byte_perm(lo.y, hi.y, 0x7632));
+  };
+  // four chunks gathered, then their four stores issued together
+  for (int base = lane; base < D / 8; base += 4 * 32) {
+    uint4 o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (base + 32 * u < D / 8) o[u] = chunk(base + 32 * u);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (base + 32 * u < D / 8) d4[base + 32 * u] = o[u];
   }
+}
+
+// Copies token row `src` to `dst` by one warp: as is (nb = 0: directly, `sbuf` unused
+// and may be empty) or in the K slot order of bit-width nb through the warp's staging
+// buffer (store_row).
+__device__ __forceinline__ void copy_row(const __half* __restrict__ src, __half* __restrict__ dst, int D, int nb,
+                                         int lane, __half* sbuf, const uint8_t (*fwd3)[128]) {
+  if (nb == 0) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    for (int base = lane; base < D / 8; base += 8 * 32) {
+      uint4 t[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (base + 32 * j < D / 8) t[j] = s4[base + 32 * j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (base + 32 * j < D / 8) d4[base + 32 * j] = t[j];
+    }
+    return;
+  }
+  stage_row(src, sbuf, D, lane);
+  store_row(sbuf, dst, D, nb, lane, fwd3);
   __syncwarp();
 }
 
@@ -269,16 +311,24 @@ __device__ __forceinline__ void stage_fwd3(uint8_t (*fwd3)[128]) {
 }
 
 // ------------------------------------------------------------------ dispatch (large batches)
+// Rows per expert: a shared-memory histogram per CTA over a stretch of slots, then
+// one global atomic per expert hit (E <= 1024).
+constexpr int kCountSlotsPerCta = 2048;
+
 __global__ void k_count(const int32_t* __restrict__ topk_idx, int64_t P, int E, int32_t* __restrict__ counts) {
   grid_dep_wait();
-  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (i >= P) return;
-  const int e = topk_idx[i];
-  if (e < 0 || e >= E) {
-    set_device_error(kDevBadExpert);
-    return;
+  __shared__ int s_cnt[1024];
+  for (int i = threadIdx.x; i < E; i += blockDim.x) s_cnt[i] = 0;
+  __syncthreads();
+  const int64_t i0 = static_cast<int64_t>(blockIdx.x) * kCountSlotsPerCta;
+  for (int64_t i = i0 + threadIdx.x; i < P && i < i0 + kCountSlotsPerCta; i += blockDim.x) {
+    const int e = topk_idx[i];
+    if (e >= 0 && e < E) atomicAdd(&s_cnt[e], 1);
+    else set_device_error(kDevBadExpert);
   }
-  atomicAdd(&counts[e], 1);
+  __syncthreads();
+  for (int i = threadIdx.x; i < E; i += blockDim.x)
+    if (s_cnt[i] != 0) atomicAdd(&counts[i], s_cnt[i]);
 }
 
 // Single block: exclusive scans over experts (E <= 1024).
@@ -309,41 +359,55 @@ __global__ void k_scan_segs(const int32_t* __restrict__ counts, int E, int nt, S
   }
 }
 
-// One warp per slot: claim a row, record it, copy the token's activation row. Rows
-// within a segment are in arrival order, which changes no result: each row is
-// computed alone and the combine visits a token's experts in ascending id. A slot
-// whose expert id is out of range (k_count recorded kDevBadExpert) gets no row and
-// slot_pos -1, which the combine skips.
-__global__ void k_scatter(const int32_t* __restrict__ topk_idx, const __half* __restrict__ topk_w,
-                          const __half* __restrict__ x, int64_t P, int k, int E, int D, int32_t* __restrict__ cursor,
-                          int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm, __half* __restrict__ x_perm,
-                          const int32_t* __restrict__ perm_nbits) {
+// One warp per token: lanes j < k claim the rows of the token's slots (one atomic
+// each, in parallel) and record them; the token's activation row is staged in the
+// warp's shared buffer once and written to each claimed row, as is or in the K slot
+// order of the expert's bit-width. Rows within a segment are in arrival order, which
+// changes no result: each row is computed alone and the combine visits a token's
+// experts in ascending id. A slot whose expert id is out of range (k_count recorded
+// kDevBadExpert) gets no row and slot_pos -1, which the combine skips.
+constexpr int kScatterWarps = 8;
+
+__global__ void __launch_bounds__(32 * kScatterWarps, 4)
+    k_scatter(const int32_t* __restrict__ topk_idx, const __half* __restrict__ topk_w, const __half* __restrict__ x,
+              int64_t T, int k, int E, int D, int32_t* __restrict__ cursor, int32_t* __restrict__ slot_pos,
+              __half* __restrict__ w_perm, __half* __restrict__ x_perm, const int32_t* __restrict__ perm_nbits) {
   grid_dep_wait();
-  __shared__ uint8_t s_fwd3[5][128];
+  __shared__ __align__(16) uint8_t s_fwd3[5][128];
   if (perm_nbits != nullptr) {
     stage_fwd3(s_fwd3);
     __syncthreads();
   }
-  const int64_t slot = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t t = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (slot >= P) return;
-  const int e = topk_idx[slot];
-  if (e < 0 || e >= E) {
-    if (lane == 0) slot_pos[slot] = -1;
-    return;
-  }
-  int pos = 0;
-  if (lane == 0) {
-    pos = atomicAdd(&cursor[e], 1);
+  if (t >= T) return;
+  int pos = -1, nb = 0;
+  if (lane < k) {
+    const int64_t slot = t * k + lane;
+    const int e = topk_idx[slot];
+    if (e >= 0 && e < E) {
+      pos = atomicAdd(&cursor[e], 1);
+      w_perm[pos] = topk_w[slot];
+      if (perm_nbits != nullptr) nb = min(max(__ldg(perm_nbits + e), 1), 4);
+    }
     slot_pos[slot] = pos;
-    w_perm[pos] = topk_w[slot];
   }
-  pos = __shfl_sync(0xffffffffu, pos, 0);
-  const int64_t t = slot / k;
-  const int nb = perm_nbits != nullptr ? min(max(__ldg(perm_nbits + e), 1), 4) : 0;
   extern __shared__ __align__(16) __half s_stage_rows[];
-  copy_row(x + t * D, x_perm + static_cast<int64_t>(pos) * D, D, nb, lane,
-           s_stage_rows + static_cast<size_t>(threadIdx.x >> 5) * D, s_fwd3);
+  __half* sbuf = s_stage_rows + static_cast<size_t>(threadIdx.x >> 5) * D;
+  const __half* src = x + t * D;
+  if (perm_nbits != nullptr) stage_row(src, sbuf, D, lane);
+  for (int j = 0; j < k; ++j) {
+    const int pj = __shfl_sync(0xffffffffu, pos, j), nj = __shfl_sync(0xffffffffu, nb, j);
+    if (pj < 0) continue;  // warp-uniform
+    __half* dst = x_perm + static_cast<int64_t>(pj) * D;
+    if (perm_nbits != nullptr) {
+      store_row(sbuf, dst, D, nj, lane, s_fwd3);
+    } else {
+      const uint4* s4 = reinterpret_cast<const uint4*>(src);
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+      for (int i = lane; i < D / 8; i += 32) d4[i] = s4[i];
+    }
+  }
 }
 
 // ------------------------------------------------------------------ dispatch (small batches)
@@ -392,7 +456,7 @@ __global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restric
   __shared__ int s_tiles[kMaxExperts];
   __shared__ int s_start[kMaxExperts + 1];
   __shared__ int s_tstart[kMaxExperts + 1];
-  __shared__ uint8_t s_fwd3[5][128];
+  __shared__ __align__(16) uint8_t s_fwd3[5][128];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
   if (perm_nbits != nullptr) stage_fwd3(s_fwd3);
@@ -478,64 +542,91 @@ __global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restric
 // every partial sum rounded to fp16: the fp16 index_add_ of forward_n_tokens
 // (moe_block.py:799-812). fp32_sum: one fp32 sum, one rounding. `add` (DeepSeek
 // shared experts) is added in fp16 afterwards (moe_block.py:575), then `residual`.
-__global__ void k_combine(const __half* __restrict__ y_perm, const int32_t* __restrict__ slot_pos,
-                          const int32_t* __restrict__ topk_idx, int64_t T, int k, int D, int fp32_sum,
-                          const __half* __restrict__ add, const __half* __restrict__ residual,
-                          __half* __restrict__ out) {
+//
+// One warp per (token, column part): 8 warps per CTA over tokens, blockIdx.y the
+// part of the row (parts > 1 for small batches, so that enough warps share the
+// loads). Lane j < k holds slot j; its rank in the order (expert id, then slot index)
+// is counted with shuffles, and lane r ends up with the row of the rank-r slot. Each
+// lane then sums 16-byte chunks of the rows in rank order, the loads of two chunks
+// of every row in flight together.
+constexpr int kCombineWarps = 8;
+constexpr int kCombineSms = 148;  // sizing of the column split only
+
+template <int KMAX>  // bound on k: 8 or 16 (registers for the rows in flight)
+__global__ void __launch_bounds__(32 * kCombineWarps, KMAX == 8 ? 2 : 1)
+    k_combine(const __half* __restrict__ y_perm, const int32_t* __restrict__ slot_pos,
+              const int32_t* __restrict__ topk_idx, int64_t T, int k, int D, int fp32_sum,
+              const __half* __restrict__ add, const __half* __restrict__ residual, __half* __restrict__ out) {
   grid_dep_wait();
-  const int64_t t = blockIdx.x;
-  int order[16];
-  int eid[16];
+  const int64_t t = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int e = lane < k ? topk_idx[t * k + lane] : 0x7fffffff;
+  const int pos = lane < k ? slot_pos[t * k + lane] : -1;
+  int rank = 0;
   for (int j = 0; j < k; ++j) {
-    order[j] = slot_pos[t * k + j];
-    eid[j] = topk_idx[t * k + j];
+    const int ej = __shfl_sync(0xffffffffu, e, j);
+    rank += (ej < e || (ej == e && j < lane)) ? 1 : 0;
   }
-  for (int a = 1; a < k; ++a) {  // insertion sort by expert id
-    int e = eid[a], o = order[a], b = a - 1;
-    while (b >= 0 && eid[b] > e) {
-      eid[b + 1] = eid[b];
-      order[b + 1] = order[b];
-      --b;
+  int row_r = -1;  // row of the rank-`lane` slot
+  for (int j = 0; j < k; ++j) {
+    const int rj = __shfl_sync(0xffffffffu, rank, j), pj = __shfl_sync(0xffffffffu, pos, j);
+    if (lane == rj) row_r = pj;
+  }
+  int rows[KMAX];
+#pragma unroll
+  for (int r = 0; r < KMAX; ++r) {
+    const int p = __shfl_sync(0xffffffffu, row_r, r);
+    rows[r] = (r < k) ? p : -1;  // -1: a slot with an invalid expert id
+  }
+  const int d8 = D / 8;
+  const int per = (d8 + gridDim.y - 1) / gridDim.y;  // chunks of this part
+  const int cbeg = blockIdx.y * per, cend = min(d8, cbeg + per);
+  for (int c0 = cbeg + lane; c0 < cend; c0 += 64) {
+    uint4 yv[2][KMAX];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = c0 + 32 * h;
+#pragma unroll
+      for (int r = 0; r < KMAX; ++r)
+        if (rows[r] >= 0 && c < cend)
+          yv[h][r] = reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(rows[r]) * D)[c];
     }
-    eid[b + 1] = e;
-    order[b + 1] = o;
-  }
-  for (int d = threadIdx.x * 8; d < D; d += blockDim.x * 8) {
-    float acc[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    // the token's rows are loaded together (one round trip), then summed in order
-    uint4 yv[16];
+    for (int h = 0; h < 2; ++h) {
+      const int c = c0 + 32 * h;
+      if (c >= cend) break;
+      float acc[8];
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < k && order[j] >= 0) yv[j] = *reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(order[j]) * D + d);
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (j >= k) break;
-      if (order[j] < 0) continue;  // slot with an invalid expert id
-      const __half* yh = reinterpret_cast<const __half*>(&yv[j]);
+      for (int r = 0; r < KMAX; ++r) {
+        if (rows[r] < 0) continue;
+        const __half* yh = reinterpret_cast<const __half*>(&yv[h][r]);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float y = __half2float(yh[i]);
-        acc[i] = fp32_sum ? acc[i] + y : __half2float(__float2half_rn(acc[i] + y));
+        for (int i = 0; i < 8; ++i) {
+          const float y = __half2float(yh[i]);
+          acc[i] = fp32_sum ? acc[i] + y : __half2float(__float2half_rn(acc[i] + y));
+        }
       }
-    }
-    __half r[8];
+      __half res[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) r[i] = __float2half_rn(acc[i]);
-    if (add != nullptr) {
-      const uint4 av = *reinterpret_cast<const uint4*>(add + t * D + d);
-      const __half* ah = reinterpret_cast<const __half*>(&av);
+      for (int i = 0; i < 8; ++i) res[i] = __float2half_rn(acc[i]);
+      const int64_t o = t * D + 8 * static_cast<int64_t>(c);
+      if (add != nullptr) {
+        const uint4 av = *reinterpret_cast<const uint4*>(add + o);
+        const __half* ah = reinterpret_cast<const __half*>(&av);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) r[i] = __float2half_rn(__half2float(r[i]) + __half2float(ah[i]));
-    }
-    if (residual != nullptr) {
-      const uint4 rv = *reinterpret_cast<const uint4*>(residual + t * D + d);
-      const __half* rh = reinterpret_cast<const __half*>(&rv);
+        for (int i = 0; i < 8; ++i) res[i] = __float2half_rn(__half2float(res[i]) + __half2float(ah[i]));
+      }
+      if (residual != nullptr) {
+        const uint4 rv = *reinterpret_cast<const uint4*>(residual + o);
+        const __half* rh = reinterpret_cast<const __half*>(&rv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) r[i] = __float2half_rn(__half2float(r[i]) + __half2float(rh[i]));
+        for (int i = 0; i < 8; ++i) res[i] = __float2half_rn(__half2float(res[i]) + __half2float(rh[i]));
+      }
+      *reinterpret_cast<uint4*>(out + o) = *reinterpret_cast<const uint4*>(res);
     }
-    *reinterpret_cast<uint4*>(out + t * D + d) = *reinterpret_cast<const uint4*>(r);
   }
 }
 
@@ -632,21 +723,26 @@ cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, con
   }
   err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, stream);
   if (err != cudaSuccess) return err;
-  err = launch_dep(k_count, dim3(static_cast<unsigned>((P + 255) / 256)), dim3(256), 0, stream, topk_idx, P, E, counts);
+  err = launch_dep(k_count, dim3(static_cast<unsigned>((P + kCountSlotsPerCta - 1) / kCountSlotsPerCta)), dim3(256), 0,
+                   stream, topk_idx, P, E, counts);
   if (err != cudaSuccess) return err;
   err = launch_dep(k_scan_segs, dim3(1), dim3(1024), 0, stream, counts, E, nt, segs, tile_prefix, cursor);
   if (err != cudaSuccess) return err;
-  return launch_dep(k_scatter, dim3(static_cast<unsigned>((P * 32 + 255) / 256)), dim3(256), row_smem, stream,
-                    topk_idx, reinterpret_cast<const __half*>(topk_w), reinterpret_cast<const __half*>(x), P, k, E, D,
-                    cursor, slot_pos, reinterpret_cast<__half*>(w_perm), reinterpret_cast<__half*>(x_perm),
-                    perm_nbits);
+  return launch_dep(k_scatter, dim3(static_cast<unsigned>((T + kScatterWarps - 1) / kScatterWarps)),
+                    dim3(32 * kScatterWarps), row_smem, stream, topk_idx, reinterpret_cast<const __half*>(topk_w),
+                    reinterpret_cast<const __half*>(x), T, k, E, D, cursor, slot_pos,
+                    reinterpret_cast<__half*>(w_perm), reinterpret_cast<__half*>(x_perm), perm_nbits);
 }
 
 cudaError_t launch_combine(const uint16_t* y_perm, const int32_t* slot_pos, const int32_t* topk_idx, int64_t T, int k,
                            int D, bool fp32_sum, const uint16_t* add, const uint16_t* residual, uint16_t* out,
                            cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  return launch_dep(k_combine, dim3(static_cast<unsigned>(T)), dim3(256), 0, stream,
+  const unsigned grid = static_cast<unsigned>((T + kCombineWarps - 1) / kCombineWarps);
+  // column parts of 32 chunks (256 halves) or more, until about 16 warps per SM
+  const int64_t want = (static_cast<int64_t>(kCombineSms) * 16 + T - 1) / T;
+  const unsigned parts = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, D / 256)));
+  return launch_dep(k <= 8 ? k_combine<8> : k_combine<16>, dim3(grid, parts), dim3(32 * kCombineWarps), 0, stream,
                     reinterpret_cast<const __half*>(y_perm), slot_pos, topk_idx, T, k, D, fp32_sum ? 1 : 0,
                     reinterpret_cast<const __half*>(add), reinterpret_cast<const __half*>(residual),
                     reinterpret_cast<__half*>(out));
