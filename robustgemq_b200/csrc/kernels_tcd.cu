@@ -62,6 +62,8 @@ constexpr uint32_t kIdleSleepNs = 256;  // pause between polls of waiters off th
 // Pause between polls of the dequant warps and the MMA issuer: a spinning warp takes
 // issue slots and integer-pipe cycles from the dequant warps of its sub-partition.
 constexpr uint32_t kBusySleepNs = 64;
+// Items per CTA whose segment is looked up once at kernel start (later ones search).
+constexpr int kMaxCtaItems = 256;
 
 __constant__ kperm::Perm3 c_perm3 = kperm::make_perm3();
 
@@ -81,10 +83,16 @@ struct CfgD {
   static constexpr int kStageBytes = round_up_d(kActBytes + kMats * kWordBytes, 1024);
   static constexpr int kScBytes = kScRows * 128 * 2;
   static constexpr int kChunkBytes = kMats * 2 * kScBytes;
-  static constexpr int kBudget = 225 * 1024 - tcw::kMetaBytes - 2 * kChunkBytes - 2048;
+  // route-weight epilogue: each of the 4 epilogue warps stages 16 rows of its 64
+  // output columns (32 per feature tile) before writing them as 16-byte pieces
+  static constexpr int kOutBytes = (MODE == GemmMode::kRouteWeight) ? 4 * 16 * 64 * 2 : 0;
+  static constexpr int kItemBytes = kMaxCtaItems * 4;  // segment of each of the CTA's items
+  static constexpr int kBudget = 225 * 1024 - tcw::kMetaBytes - 2 * kChunkBytes - 2048 - kOutBytes - kItemBytes;
   static constexpr int kStages = cmin_d(8, kBudget / kStageBytes);
   static constexpr int kChunkOff = kStages * kStageBytes;
-  static constexpr int kBarOff = kChunkOff + 2 * kChunkBytes;
+  static constexpr int kOutOff = kChunkOff + 2 * kChunkBytes;
+  static constexpr int kItemOff = kOutOff + kOutBytes;
+  static constexpr int kBarOff = kItemOff + kItemBytes;
   // TMEM: accumulator buffers (two when they fit beside the A ring, so one item's
   // epilogue overlaps the next item's MMAs), then the A ring.
   static constexpr int kAccCols = kMats * NT;  // one accumulator buffer
@@ -140,10 +148,14 @@ struct ItemWalk {
     full = total / G * G;
     n = total / G + ((G - 1 - c) < total - full ? 1 : 0);
   }
+  // the CTA's item number i
+  __device__ __forceinline__ int w_of(int i) const {
+    const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+    return (i * G < full) ? i * G + c : full + (G - 1 - c);
+  }
   __device__ __forceinline__ bool next(int& w) {
     if (j >= n) return false;
-    const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
-    w = (j * G < full) ? j * G + c : full + (G - 1 - c);
+    w = w_of(j);
     ++j;
     return true;
   }
@@ -554,9 +566,22 @@ __global__ void __launch_bounds__(kThreadsD, 1)
   Meta& meta = *reinterpret_cast<Meta*>(smem + C::kMetaOff);
   tcw::stage_meta(meta, p, false);
   __syncthreads();
+  const int total = meta.tp[p.num_segs] * p.n_tiles;
+  // segment of each of the CTA's first kMaxCtaItems items, searched once here instead
+  // of by every role at every item
+  int* item_seg = reinterpret_cast<int*>(smem + C::kItemOff);
+  {
+    const ItemWalk iw(total);
+    for (int i = threadIdx.x; i < iw.n && i < kMaxCtaItems; i += blockDim.x)
+      item_seg[i] = tcw::seg_of_tile(meta, p.num_segs, iw.w_of(i) / p.n_tiles);
+  }
+  __syncthreads();
+  auto work_of = [&](int i, int w) {
+    return i < kMaxCtaItems ? tcw::work_in_seg<NT>(meta, item_seg[i], p.n_tiles, w)
+                            : tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
+  };
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int total = meta.tp[p.num_segs] * p.n_tiles;
   const int KT = p.K / kSK;
   const int g = p.group_size;
   const int groups = p.K / g;
@@ -584,7 +609,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       ItemWalk items(total);
       int w;
       while (ok && items.next(w)) {
-        const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
+        const Work wk = work_of(items.j - 1, w);
         const int nb = min(max(wk.nb, 1), 4);
         const int rows = kperm::stage_word_rows(nb);
         const bool words = first || kMats == 2;
@@ -632,7 +657,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       ItemWalk items(total);
       int w;
       while (ok && items.next(w)) {
-        const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
+        const Work wk = work_of(items.j - 1, w);
         for (int ch = 0; ch < nchunks; ++ch) {
           if (!warp_wait(&sempty[c], cph ^ 1u, kDevTimeoutTmaEmpty, kIdleSleepNs)) { ok = false; break; }
           uint8_t* cb = smem + C::kChunkOff + c * C::kChunkBytes;
@@ -715,7 +740,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       const int buf = it % C::kAccBufs;
       const uint32_t lane_base =
           tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * C::kAccCols);
-      const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
+      const Work wk = work_of(items.j - 1, w);
       // routing weights of the item's rows, before the wait: lane j holds rows 2j and
       // 2j + 1 as an fp16 pair (loads issued together here, not one per row behind
       // the output stores, which the compiler may not move them past)
@@ -741,6 +766,8 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       }
       const int f = (MODE == GemmMode::kSwiGLU ? wk.n0 : 2 * wk.n0) + 32 * q + lane;
       int col = f;
+      // this warp's staging rows (route-weight mode): [16][64] fp16
+      __half* stg = reinterpret_cast<__half*>(smem + C::kOutOff) + q * (16 * 64);
       if constexpr (MODE == GemmMode::kSwiGLU)
         if (p.perm_out_nbits != nullptr) col = perm_dst(min(max(__ldg(p.perm_out_nbits + wk.e), 1), 4), f);
 #pragma unroll
@@ -769,18 +796,29 @@ __global__ void __launch_bounds__(kThreadsD, 1)
             if (v0) out[row * p.out_ld + col] = __low2half(h);
             if (v1) out[(row + 1) * p.out_ld + col] = __high2half(h);
           } else {
-            // two feature tiles: y = fp16(acc), y * w -> fp16 (moe_block.py:778, 811)
+            // two feature tiles: y = fp16(acc), y * w -> fp16 (moe_block.py:778, 811),
+            // staged as row i: [tile 0: 32 features | tile 1: 32 features]
             const __half2 wv = u32_as_h2(__shfl_sync(0xffffffffu, wpair, (c0 + i) >> 1));
             const __half2 y0 = __hmul2(a0, wv), y1 = __hmul2(a1, wv);
-            if (v0) {
-              out[row * p.out_ld + col] = __low2half(y0);
-              out[row * p.out_ld + col + 128] = __low2half(y1);
-            }
-            if (v1) {
-              out[(row + 1) * p.out_ld + col] = __high2half(y0);
-              out[(row + 1) * p.out_ld + col + 128] = __high2half(y1);
-            }
+            stg[i * 64 + lane] = __low2half(y0);
+            stg[i * 64 + 32 + lane] = __low2half(y1);
+            stg[(i + 1) * 64 + lane] = __high2half(y0);
+            stg[(i + 1) * 64 + 32 + lane] = __high2half(y1);
           }
+        }
+        if constexpr (MODE == GemmMode::kRouteWeight) {
+          // the chunk's rows: 2 x 64-byte pieces each (one per feature tile), written
+          // as 16-byte stores, 8 rows per warp instruction
+          __syncwarp();
+          const uint4* s4 = reinterpret_cast<const uint4*>(stg);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int idx = lane + 32 * u, r = idx >> 3, pc = idx & 7;
+            if (c0 + r < wk.rows)
+              *reinterpret_cast<uint4*>(out + (wk.out_row + c0 + r) * p.out_ld + col - lane + (pc >> 2) * 128 +
+                                        (pc & 3) * 8) = s4[idx];
+          }
+          __syncwarp();
         }
       }
     }
@@ -805,7 +843,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     ItemWalk items(total);
     int w;
     for (int it = 0; items.next(w); ++it) {
-      const Work wk = tcw::decode_work<NT>(meta, p.num_segs, p.n_tiles, w);
+      const Work wk = work_of(items.j - 1, w);
       if ((wk.nb < 1 || wk.nb > 4) && dw == 0 && lane == 0) set_device_error(kDevBadBits);
       const int nb = min(max(wk.nb, 1), 4);
       const int kt0 = (env.grp + it * KT) & 1;  // first own stage of the item
@@ -926,7 +964,11 @@ bool tcd_gemm_supported(const GemmArgs& a) {
   if (a.num_segs <= 0 || a.num_segs > tcw::kMaxSegs) return false;
   if (a.mode == GemmMode::kSwiGLU && (a.w1.n != a.w0.n || a.w1.k != a.w0.k || a.w1.group_size != a.w0.group_size))
     return false;
-  if (a.mode == GemmMode::kRouteWeight && a.w0.n % 256 != 0) return false;  // tiles pair up
+  if (a.mode == GemmMode::kRouteWeight) {
+    if (a.w0.n % 256 != 0) return false;  // tiles pair up
+    // the epilogue writes 16-byte pieces of its output rows
+    if ((reinterpret_cast<uintptr_t>(a.out) & 15u) != 0 || a.out_ld % 8 != 0) return false;
+  }
   return (reinterpret_cast<uintptr_t>(a.act) & 15u) == 0;
 }
 

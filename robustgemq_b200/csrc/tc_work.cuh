@@ -45,16 +45,22 @@ __device__ __forceinline__ void stage_meta(Meta& m, const Args& p, bool dense) {
   }
 }
 
-template <int NT>
-__device__ __forceinline__ Work decode_work(const Meta& m, int num_segs, int n_tiles, int w) {
-  Work wk;
-  const int t = w / n_tiles;
-  const int i = w - t * n_tiles;
+// Segment of tile t: the last segment whose tile prefix is <= t (binary search).
+__device__ __forceinline__ int seg_of_tile(const Meta& m, int num_segs, int t) {
   int lo = 0, hi = num_segs;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (m.tp[mid] <= t) lo = mid; else hi = mid;
   }
+  return lo;
+}
+
+// Work item w of segment lo (the segment of its token tile).
+template <int NT>
+__device__ __forceinline__ Work work_in_seg(const Meta& m, int lo, int n_tiles, int w) {
+  Work wk;
+  const int t = w / n_tiles;
+  const int i = w - t * n_tiles;
   const Seg sg = m.seg[lo];
   const int j = t - m.tp[lo];
   wk.e = sg.x;
@@ -68,6 +74,11 @@ __device__ __forceinline__ Work decode_work(const Meta& m, int num_segs, int n_t
   wk.wrow1 = m.wrow1[lo];
   wk.srow1 = m.srow1[lo];
   return wk;
+}
+
+template <int NT>
+__device__ __forceinline__ Work decode_work(const Meta& m, int num_segs, int n_tiles, int w) {
+  return work_in_seg<NT>(m, seg_of_tile(m, num_segs, w / n_tiles), n_tiles, w);
 }
 
 }  // namespace tcw
