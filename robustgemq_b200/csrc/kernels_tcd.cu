@@ -688,7 +688,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     // converged warp) issues every MMA and commit, so each commit tracks them all.
     {
       int s = 0, as = 0;
-      uint32_t ph = 0, aph = 0;
+      uint32_t aph = 0;
       int it = 0;
       bool ok = true;
       ItemWalk items(total);
@@ -699,11 +699,11 @@ __global__ void __launch_bounds__(kThreadsD, 1)
         if (!warp_wait(&acc_empty[buf], ((it / C::kAccBufs) & 1) ^ 1u, kDevTimeoutAccEmpty, kBusySleepNs)) break;
         tc_fence_after();
         for (int kt = 0; kt < KT; ++kt) {
-          // both first polls in flight together
-          const bool tf = mbar_try_wait(smem_u32(&full[s]), ph);
-          const bool ta = mbar_try_wait(smem_u32(&afull[as]), aph);
-          if (!warp_wait_tok(smem_u32(&full[s]), ph, tf, kDevTimeoutTmaFull, kBusySleepNs)) { ok = false; break; }
-          if (!warp_wait_tok(smem_u32(&afull[as]), aph, ta, kDevTimeoutAFull, kBusySleepNs)) { ok = false; break; }
+          // The stage's A slot only: each dequant warp of the group waited for the
+          // stage's full barrier (activations and words landed) before it arrived on
+          // afull, so afull completing orders the stage's copies before these MMAs
+          // (release / acquire through the two barriers).
+          if (!warp_wait(smem_u32(&afull[as]), aph, kDevTimeoutAFull, kBusySleepNs)) { ok = false; break; }
           tc_fence_after();
           const uint32_t act = smem_u32(smem + s * C::kStageBytes);
           const uint64_t b0 = sdesc_sw128(act);
@@ -719,7 +719,7 @@ __global__ void __launch_bounds__(kThreadsD, 1)
             umma_commit(&aempty[as]);
           }
           __syncwarp();
-          if (++s == kStages) { s = 0; ph ^= 1u; }
+          if (++s == kStages) s = 0;
           if (++as == kAStages) { as = 0; aph ^= 1u; }
         }
         if (!ok) break;
