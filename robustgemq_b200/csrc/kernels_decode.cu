@@ -165,17 +165,20 @@ __device__ __forceinline__ void row_pow2(const uint4& wv, const void* xr, const 
   for (int c = 0; c < 4; ++c) word_pow2<NB, XF16>(words[c], s_c[c], z_c[c], x, acc[c][0], acc[c][1]);
 }
 
-// Accumulates word rows [wr0, wr1) of a warp; `wv` holds the first batch, loaded by
-// the caller before it staged x and the scales. The next batch's loads are issued
-// before the current one is used.
+// Accumulates word rows of a warp, one row (its 16-byte word piece of the four
+// feature columns) at a time, keeping the current group's scale and zero.
 template <bool XF16>
-__device__ __forceinline__ void gemv_rows(const int32_t* wbase, int K, int N, int g, int nb, int lane, int n, int wr0,
-                                          int wr1, int k0, const void* s_x, const GroupStage& gs, uint4 (&wv)[kBatch],
-                                          float (&acc)[4][2]) {
-  const int eps = 32 / nb;
-  int cur_g = -1;
+struct RowAcc {
+  int K, g, nb, lane, k0, eps, cur_g;
+  const char* xbase;
+  GroupStage gs;
   __half2 s_c[4], z_c[4];  // scale / zero of the current group, per column
-  auto load_group = [&](int gi, __half2 (&sd)[4], __half2 (&zd)[4]) {
+
+  __device__ __forceinline__ RowAcc(int K_, int g_, int nb_, int lane_, int k0_, const void* s_x, const GroupStage& gs_)
+      : K(K_), g(g_), nb(nb_), lane(lane_), k0(k0_), eps(32 / nb_), cur_g(-1),
+        xbase(static_cast<const char*>(s_x)), gs(gs_) {}
+
+  __device__ __forceinline__ void load_group(int gi, __half2 (&sd)[4], __half2 (&zd)[4]) const {
     const int off = (gi - gs.g0) * 128 + lane * 4;
     const uint2 sv = *reinterpret_cast<const uint2*>(gs.s + off);
     const uint2 zv = *reinterpret_cast<const uint2*>(gs.z + off);
@@ -186,58 +189,68 @@ __device__ __forceinline__ void gemv_rows(const int32_t* wbase, int K, int N, in
       sd[c] = __halves2half2(sp[c], sp[c]);
       zd[c] = __halves2half2(zp[c], zp[c]);
     }
-  };
-  constexpr int kXBytes = XF16 ? 2 : 4;
-  const char* xbase = static_cast<const char*>(s_x);
+  }
+
+  __device__ __forceinline__ void row(int r, const uint4& w, float (&acc)[4][2]) {
+    constexpr int kXBytes = XF16 ? 2 : 4;
+    const int kr = r * eps;
+    const int ga = kr / g;
+    if (ga != cur_g) {
+      cur_g = ga;
+      load_group(ga, s_c, z_c);
+    }
+    const void* xr = xbase + static_cast<size_t>(kr - k0) * kXBytes;
+    if (nb == 3) {
+      XRow<3, XF16> x;
+      x.load(xr);
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+      const int gb = min(kr + 9, K - 1) / g;
+      if (gb == ga) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_c[c]), __low2half(z_c[c]), 10,
+                          x, acc[c][0], acc[c][1]);
+      } else {
+        // codes at k >= gb * g use the next group's scale and zero
+        __half2 s_n[4], z_n[4];
+        load_group(gb, s_n, z_n);
+        const int b = gb * g - kr;  // first code index in the next group (1..9)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_n[c]), __low2half(z_n[c]), b,
+                          x, acc[c][0], acc[c][1]);
+        cur_g = gb;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          s_c[c] = s_n[c];
+          z_c[c] = z_n[c];
+        }
+      }
+      // codes past K in a ragged last word are zero-padded and their x staged as 0
+    } else if (nb == 2) {
+      row_pow2<2, XF16>(w, xr, s_c, z_c, acc);
+    } else if (nb == 4) {
+      row_pow2<4, XF16>(w, xr, s_c, z_c, acc);
+    } else {
+      row_pow2<1, XF16>(w, xr, s_c, z_c, acc);
+    }
+  }
+};
+
+// Accumulates word rows [wr0, wr1) of a warp from global memory; `wv` holds the
+// first batch, loaded by the caller before it staged x and the scales. The next
+// batch's loads are issued before the current one is used.
+template <bool XF16>
+__device__ __forceinline__ void gemv_rows(const int32_t* wbase, int N, int n, int wr0, int wr1, RowAcc<XF16>& ra,
+                                          uint4 (&wv)[kBatch], float (&acc)[4][2]) {
   for (int rb = wr0; rb < wr1; rb += kBatch) {
     uint4 nx[kBatch];
     const bool more = rb + kBatch < wr1;
     if (more) load_words(wbase, N, n, rb + kBatch, wr1, nx);
 #pragma unroll
     for (int i = 0; i < kBatch; ++i) {
-      const int r = rb + i;
-      if (r >= wr1) break;
-      const int kr = r * eps;
-      const int ga = kr / g;
-      if (ga != cur_g) {
-        cur_g = ga;
-        load_group(ga, s_c, z_c);
-      }
-      const void* xr = xbase + static_cast<size_t>(kr - k0) * kXBytes;
-      if (nb == 3) {
-        XRow<3, XF16> x;
-        x.load(xr);
-        const uint32_t words[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
-        const int gb = min(kr + 9, K - 1) / g;
-        if (gb == ga) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_c[c]), __low2half(z_c[c]),
-                            10, x, acc[c][0], acc[c][1]);
-        } else {
-          // codes at k >= gb * g use the next group's scale and zero
-          __half2 s_n[4], z_n[4];
-          load_group(gb, s_n, z_n);
-          const int b = gb * g - kr;  // first code index in the next group (1..9)
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_n[c]), __low2half(z_n[c]),
-                            b, x, acc[c][0], acc[c][1]);
-          cur_g = gb;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            s_c[c] = s_n[c];
-            z_c[c] = z_n[c];
-          }
-        }
-        // codes past K in a ragged last word are zero-padded and their x staged as 0
-      } else if (nb == 2) {
-        row_pow2<2, XF16>(wv[i], xr, s_c, z_c, acc);
-      } else if (nb == 4) {
-        row_pow2<4, XF16>(wv[i], xr, s_c, z_c, acc);
-      } else {
-        row_pow2<1, XF16>(wv[i], xr, s_c, z_c, acc);
-      }
+      if (rb + i >= wr1) break;
+      ra.row(rb + i, wv[i], acc);
     }
     if (more) {
 #pragma unroll
@@ -250,14 +263,24 @@ __device__ __forceinline__ void gemv_rows(const int32_t* wbase, int K, int N, in
 // staged scale and zero rows.
 __host__ __device__ inline int gemv_x_elems(int k, int splits) { return (k + splits - 1) / splits + 128; }
 __host__ __device__ inline int gemv_groups(int k, int splits, int g) { return gemv_x_elems(k, splits) / g + 2; }
+// word rows of a split, bounded over bit-widths (4-bit has the most: k / 8)
+__host__ __device__ inline int gemv_word_rows(int k, int splits) { return (k / 8 + 1 + splits - 1) / splits + 1; }
+__host__ __device__ inline int gemv_words_off(int k, int splits, int g, bool xf16) {
+  const int xbytes = ((xf16 ? 2 : 4) * gemv_x_elems(k, splits) + 15) & ~15;
+  return xbytes + 2 * 2 * 128 * gemv_groups(k, splits, g);
+}
+// Words of a split staged whole in shared memory by bulk copies (one per 512-byte row
+// piece of the block's 128 features), when they fit this budget.
+constexpr int kGemvWordBudget = 96 * 1024;
 
 template <bool XF16>
 __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1, const int32_t* __restrict__ idx,
                                                           int rows_a, GemvSrc src, float* __restrict__ part,
-                                                          int splits) {
+                                                          int splits, int bulk_words) {
   grid_dep_wait();
   extern __shared__ __align__(16) unsigned char s_raw[];
   __shared__ float s_red[8][kGemvCols];
+  __shared__ uint64_t s_wbar;
   const int slab = blockIdx.x, s = blockIdx.y;
   const int mat = blockIdx.z / rows_a, a = blockIdx.z - mat * rows_a;
   const ProjDev& w = (mat == 0) ? w0 : w1;
@@ -286,7 +309,25 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
   const int wr0 = r0 + warp * per, wr1 = min(r1, wr0 + per);
   const int32_t* wbase = w.wq + static_cast<int64_t>(w.wq_strides[e]);
   uint4 wv[kBatch];
-  if (n < N) load_words(wbase, N, n, wr0, wr1, wv);
+  // whole-split staging: every row piece of the block in flight at once (one HBM
+  // round trip for all its words), else each warp's rows in batches of kBatch
+  const bool bulk = bulk_words != 0 && (N % kGemvCols) == 0 && (reinterpret_cast<uintptr_t>(wbase) & 15u) == 0;
+  int32_t* s_words = reinterpret_cast<int32_t*>(s_raw + gemv_words_off(K, splits, g, XF16));
+  if (bulk) {
+    if (threadIdx.x == 0) {
+      mbar_init(&s_wbar, 1);
+      fence_barrier_init();
+    }
+    __syncthreads();
+    const int nr = r1 - r0;
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(&s_wbar, static_cast<uint32_t>(nr) * kGemvCols * 4u);
+    const uint64_t policy = l2_evict_first_policy();  // read once: streamed
+    for (int r = threadIdx.x; r < nr; r += blockDim.x)
+      bulk_load_hint(s_words + r * kGemvCols, wbase + static_cast<int64_t>(r0 + r) * N + slab * kGemvCols,
+                     kGemvCols * 4u, &s_wbar, policy);
+  } else if (n < N) {
+    load_words(wbase, N, n, wr0, wr1, wv);
+  }
   // Stage x and the scale / zero rows. Every thread first issues all of its loads
   // for a batch of elements into registers and only then stores them, so a batch
   // costs one memory round trip instead of one per element.
@@ -391,7 +432,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
   __syncthreads();
   float acc[4][2] = {};
   const GroupStage gs{s_s, s_z, g0};
-  if (n < N) gemv_rows<XF16>(wbase, K, N, g, nb, lane, n, wr0, wr1, k0, s_raw, gs, wv, acc);
+  RowAcc<XF16> ra(K, g, nb, lane, k0, s_raw, gs);
+  if (bulk) {
+    if (warp_wait(&s_wbar, 0u, kDevTimeoutTmaFull)) {
+      for (int r = wr0; r < wr1; ++r)
+        ra.row(r, *reinterpret_cast<const uint4*>(s_words + (r - r0) * kGemvCols + lane * 4), acc);
+    }
+  } else if (n < N) {
+    gemv_rows<XF16>(wbase, N, n, wr0, wr1, ra, wv, acc);
+  }
 #pragma unroll
   for (int c = 0; c < 4; ++c) s_red[warp][lane * 4 + c] = acc[c][0] + acc[c][1];
   __syncthreads();
@@ -455,8 +504,9 @@ cudaError_t launch_gemv_t(const ProjDev& w0, const ProjDev* w1, const int32_t* i
   const int nmat = (w1 != nullptr) ? 2 : 1;
   // x of a split (at most cdiv(rows, splits) word rows of <= 32 codes: < k/splits + 64)
   // plus the scale and zero rows of the groups it touches
-  const int xbytes = (XF16 ? 2 : 4) * gemv_x_elems(w0.k, splits);
-  const size_t smem = ((xbytes + 15) & ~15) + 2 * 2 * 128 * static_cast<size_t>(gemv_groups(w0.k, splits, w0.group_size));
+  const int word_bytes = gemv_word_rows(w0.k, splits) * kGemvCols * 4;
+  const int bulk = (w0.n % kGemvCols == 0 && word_bytes <= kGemvWordBudget) ? 1 : 0;
+  const size_t smem = static_cast<size_t>(gemv_words_off(w0.k, splits, w0.group_size, XF16)) + (bulk ? word_bytes : 0);
   static std::atomic<size_t> smem_done[kMaxDevices];  // per device: the attribute is per device
   if (smem > 48 * 1024) {
     cudaError_t e = raise_smem_limit(k_gemv<XF16>, smem, smem_done);
@@ -464,7 +514,7 @@ cudaError_t launch_gemv_t(const ProjDev& w0, const ProjDev* w1, const int32_t* i
   }
   dim3 grid((w0.n + kGemvCols - 1) / kGemvCols, splits, nmat * rows_a);
   return launch_dep(k_gemv<XF16>, grid, dim3(kGemvThreads), smem, s, w0, w1 != nullptr ? *w1 : w0, idx, rows_a, src,
-                    part, splits);
+                    part, splits, bulk);
 }
 
 }  // namespace
