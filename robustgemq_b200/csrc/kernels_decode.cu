@@ -9,10 +9,11 @@
 // order, so every result is bit-reproducible (the reference's fp16 atomics are not,
 // dequant_gemv.py:115).
 //
-// Inner loop: two codes per magic-number pair, dequantised with one fma.rn.f16x2
-// (bit-exact with utils.py:206-210); fp16 inputs accumulate with the mixed-precision
-// fma.rn.f32.f16 (exact product, one rounding: identical to converting and using an
-// fp32 fma), fp32 inputs (the one-token path's fp32 SiLU*mul) with fma.rn.f32x2.
+// Inner loop: two codes per pair dequantised with one fma.rn.f16x2 (bit-exact with
+// utils.py:206-210), in the single-instruction subnormal-operand form when the
+// layer's scale check allows it, else the magic-number form; the inputs are staged
+// in shared memory as fp32 (fp16 inputs convert exactly; the one-token path's SiLU*mul
+// is fp32) and accumulate with fma.rn.f32x2 (exact products, one rounding each).
 //
 // Input modes (xin):
 //   kGemvX        fp16 rows x[a * x_stride + k]
@@ -32,15 +33,9 @@ namespace {
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvCols = 128;
+constexpr int kGemvCtasPerSm = 2;  // 128 registers per thread (fewer spill)
 
 __device__ __forceinline__ float silu_f32(float x) { return x / (1.f + expf(-x)); }
-
-// acc + a * b with a, b fp16 and one rounding to fp32
-__device__ __forceinline__ float fma_f32_f16(__half a, __half b, float c) {
-  float d;
-  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(__half_as_ushort(a)), "h"(__half_as_ushort(b)), "f"(c));
-  return d;
-}
 
 // (d0, d1) += (a0, a1) * (b0, b1), each lane one rounding
 __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
@@ -92,47 +87,72 @@ struct XRow {
   __device__ __forceinline__ float f(int j) const { return __uint_as_float(v[j]); }
 };
 
+// Adds k_lo / k_hi to the exponent fields of the two halves of a pair (the scale
+// times 2^k, exact for the normal scales the subnormal form is used with).
+__device__ __forceinline__ __half2 exp_add2(__half2 v, int k_lo, int k_hi) {
+  return u32_as_h2(h2_as_u32(v) + ((static_cast<uint32_t>(k_lo) << 10) | (static_cast<uint32_t>(k_hi) << 26)));
+}
+
 // Accumulates one word of one feature column. Pair p holds codes (p, p + eps/2):
-// 16 bits apart, so one shift + mask per pair.
-template <int NB, bool XF16>
+// 16 bits apart, so one shift + mask per pair. SUB: the subnormal-operand form of
+// the tensor-memory GEMM (kernels_tcd.cu, dq_col_sub): the pair moved to mantissa
+// offset o (b = 4: 6; b = 2: 6 / 8 for even / odd p; b = 1: 8 / 9) reads as
+// q * 2^(o - 24), the scale carries 2^(24 - o), one fma.rn.f16x2 gives the same
+// single rounding of q * s + z'. Otherwise the magic-number form. Products with the
+// fp32 inputs are exact, each sum rounded once (fma.rn.f32x2).
+template <int NB, bool XF16, bool SUB>
 __device__ __forceinline__ void word_pow2(uint32_t w, __half2 s2, __half2 z2, const XRow<NB, XF16>& x, float& acc0,
                                           float& acc1) {
+  static_assert(!XF16, "inputs are staged as fp32");
   constexpr int kEps = 32 / NB, kHalf = kEps / 2;
   constexpr uint32_t kMask = ((1u << NB) - 1u) * 0x00010001u;
+  __half2 sa2 = s2, sb2 = s2;
+  if constexpr (SUB) {
+    sa2 = exp_add2(s2, NB == 1 ? 16 : 18, NB == 1 ? 16 : 18);
+    sb2 = exp_add2(s2, NB == 1 ? 15 : (NB == 2 ? 16 : 18), NB == 1 ? 15 : (NB == 2 ? 16 : 18));
+  }
 #pragma unroll
   for (int j = 0; j < kHalf; ++j) {
-    const __half2 wq = u32_as_h2(dq_pair(((w >> (NB * j)) & kMask) | 0x64006400u, s2, z2));
-    if constexpr (XF16) {
-      acc0 = fma_f32_f16(__low2half(wq), x.h(j), acc0);
-      acc1 = fma_f32_f16(__high2half(wq), x.h(j + kHalf), acc1);
+    __half2 wq;
+    if constexpr (SUB) {
+      const bool alt = (NB != 4) && (j & 1);
+      const int o = (NB == 4 ? 6 : (NB == 2 ? 6 : 8)) + (alt ? (NB == 2 ? 2 : 1) : 0);
+      const int sh = o - NB * j;
+      const uint32_t v = sh >= 0 ? (w << sh) : (w >> (-sh));
+      wq = __hfma2(u32_as_h2(v & (kMask << o)), alt ? sb2 : sa2, z2);
     } else {
-      const float2 wf = __half22float2(wq);
-      ffma2(acc0, acc1, x.f(j), x.f(j + kHalf), wf.x, wf.y);
+      wq = u32_as_h2(dq_pair(((w >> (NB * j)) & kMask) | 0x64006400u, s2, z2));
     }
+    const float2 wf = __half22float2(wq);
+    ffma2(acc0, acc1, x.f(j), x.f(j + kHalf), wf.x, wf.y);
   }
 }
 
 // 3-bit: ten codes per word (bits 30-31 unused); pair p holds codes (p, p + 5).
 // A word may straddle a scale-group boundary: codes j < b use (sa, za), codes
-// j >= b the next group's (sb, zb) (b = 10 when the word lies in one group).
-template <bool XF16>
+// j >= b the next group's (sb, zb) (b = 10 when the word lies in one group). SUB:
+// code p moved to bit 6 (o = 6), code p + 5 to bit 21 (o = 5 of the high half).
+template <bool XF16, bool SUB>
 __device__ __forceinline__ void word_3bit(uint32_t w, __half sa, __half za, __half sb, __half zb, int b,
                                           const XRow<3, XF16>& x, float& acc0, float& acc1) {
+  static_assert(!XF16, "inputs are staged as fp32");
 #pragma unroll
   for (int j = 0; j < 5; ++j) {
-    const uint32_t t = w >> (3 * j);        // code j at bits 0..2
-    const uint32_t u = w >> (3 * j + 15);   // code j + 5 at bits 0..2
-    const uint32_t m = (t & 7u) | ((u & 7u) << 16) | 0x64006400u;
     const __half2 s2 = __halves2half2(j >= b ? sb : sa, j + 5 >= b ? sb : sa);
     const __half2 z2 = __halves2half2(j >= b ? zb : za, j + 5 >= b ? zb : za);
-    const __half2 wq = u32_as_h2(dq_pair(m, s2, z2));
-    if constexpr (XF16) {
-      acc0 = fma_f32_f16(__low2half(wq), x.h(j), acc0);
-      acc1 = fma_f32_f16(__high2half(wq), x.h(j + 5), acc1);
+    __half2 wq;
+    if constexpr (SUB) {
+      const int sh = 6 - 3 * j;  // code j: bit 3j -> 6; code j + 5: bit 3j + 15 -> 21
+      const uint32_t v = sh >= 0 ? (w << sh) : (w >> (-sh));
+      wq = __hfma2(u32_as_h2(v & ((7u << 6) | (7u << 21))), exp_add2(s2, 18, 19), z2);
     } else {
-      const float2 wf = __half22float2(wq);
-      ffma2(acc0, acc1, x.f(j), x.f(j + 5), wf.x, wf.y);
+      const uint32_t t = w >> (3 * j);       // code j at bits 0..2
+      const uint32_t u = w >> (3 * j + 15);  // code j + 5 at bits 0..2
+      const uint32_t m = (t & 7u) | ((u & 7u) << 16) | 0x64006400u;
+      wq = u32_as_h2(dq_pair(m, s2, z2));
     }
+    const float2 wf = __half22float2(wq);
+    ffma2(acc0, acc1, x.f(j), x.f(j + 5), wf.x, wf.y);
   }
 }
 
@@ -155,19 +175,19 @@ __device__ __forceinline__ void load_words(const int32_t* wbase, int N, int n, i
 }
 
 // One word row of the four feature columns of a lane.
-template <int NB, bool XF16>
+template <int NB, bool SUB>
 __device__ __forceinline__ void row_pow2(const uint4& wv, const void* xr, const __half2 (&s_c)[4],
                                          const __half2 (&z_c)[4], float (&acc)[4][2]) {
-  XRow<NB, XF16> x;
+  XRow<NB, false> x;
   x.load(xr);
   const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-  for (int c = 0; c < 4; ++c) word_pow2<NB, XF16>(words[c], s_c[c], z_c[c], x, acc[c][0], acc[c][1]);
+  for (int c = 0; c < 4; ++c) word_pow2<NB, false, SUB>(words[c], s_c[c], z_c[c], x, acc[c][0], acc[c][1]);
 }
 
 // Accumulates word rows of a warp, one row (its 16-byte word piece of the four
 // feature columns) at a time, keeping the current group's scale and zero.
-template <bool XF16>
+template <bool SUB>
 struct RowAcc {
   int K, g, nb, lane, k0, eps, cur_g;
   const char* xbase;
@@ -192,7 +212,7 @@ struct RowAcc {
   }
 
   __device__ __forceinline__ void row(int r, const uint4& w, float (&acc)[4][2]) {
-    constexpr int kXBytes = XF16 ? 2 : 4;
+    constexpr int kXBytes = 4;  // fp32 inputs
     const int kr = r * eps;
     const int ga = kr / g;
     if (ga != cur_g) {
@@ -201,14 +221,14 @@ struct RowAcc {
     }
     const void* xr = xbase + static_cast<size_t>(kr - k0) * kXBytes;
     if (nb == 3) {
-      XRow<3, XF16> x;
+      XRow<3, false> x;
       x.load(xr);
       const uint32_t words[4] = {w.x, w.y, w.z, w.w};
       const int gb = min(kr + 9, K - 1) / g;
       if (gb == ga) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-          word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_c[c]), __low2half(z_c[c]), 10,
+          word_3bit<false, SUB>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_c[c]), __low2half(z_c[c]), 10,
                           x, acc[c][0], acc[c][1]);
       } else {
         // codes at k >= gb * g use the next group's scale and zero
@@ -217,7 +237,7 @@ struct RowAcc {
         const int b = gb * g - kr;  // first code index in the next group (1..9)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-          word_3bit<XF16>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_n[c]), __low2half(z_n[c]), b,
+          word_3bit<false, SUB>(words[c], __low2half(s_c[c]), __low2half(z_c[c]), __low2half(s_n[c]), __low2half(z_n[c]), b,
                           x, acc[c][0], acc[c][1]);
         cur_g = gb;
 #pragma unroll
@@ -228,11 +248,11 @@ struct RowAcc {
       }
       // codes past K in a ragged last word are zero-padded and their x staged as 0
     } else if (nb == 2) {
-      row_pow2<2, XF16>(w, xr, s_c, z_c, acc);
+      row_pow2<2, SUB>(w, xr, s_c, z_c, acc);
     } else if (nb == 4) {
-      row_pow2<4, XF16>(w, xr, s_c, z_c, acc);
+      row_pow2<4, SUB>(w, xr, s_c, z_c, acc);
     } else {
-      row_pow2<1, XF16>(w, xr, s_c, z_c, acc);
+      row_pow2<1, SUB>(w, xr, s_c, z_c, acc);
     }
   }
 };
@@ -240,8 +260,8 @@ struct RowAcc {
 // Accumulates word rows [wr0, wr1) of a warp from global memory; `wv` holds the
 // first batch, loaded by the caller before it staged x and the scales. The next
 // batch's loads are issued before the current one is used.
-template <bool XF16>
-__device__ __forceinline__ void gemv_rows(const int32_t* wbase, int N, int n, int wr0, int wr1, RowAcc<XF16>& ra,
+template <bool SUB>
+__device__ __forceinline__ void gemv_rows(const int32_t* wbase, int N, int n, int wr0, int wr1, RowAcc<SUB>& ra,
                                           uint4 (&wv)[kBatch], float (&acc)[4][2]) {
   for (int rb = wr0; rb < wr1; rb += kBatch) {
     uint4 nx[kBatch];
@@ -273,8 +293,8 @@ __host__ __device__ inline int gemv_words_off(int k, int splits, int g, bool xf1
 // piece of the block's 128 features), when they fit this budget.
 constexpr int kGemvWordBudget = 96 * 1024;
 
-template <bool XF16>
-__global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1, const int32_t* __restrict__ idx,
+template <bool SUB>
+__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) k_gemv(ProjDev w0, ProjDev w1, const int32_t* __restrict__ idx,
                                                           int rows_a, GemvSrc src, float* __restrict__ part,
                                                           int splits, int bulk_words) {
   grid_dep_wait();
@@ -312,7 +332,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
   // whole-split staging: every row piece of the block in flight at once (one HBM
   // round trip for all its words), else each warp's rows in batches of kBatch
   const bool bulk = bulk_words != 0 && (N % kGemvCols) == 0 && (reinterpret_cast<uintptr_t>(wbase) & 15u) == 0;
-  int32_t* s_words = reinterpret_cast<int32_t*>(s_raw + gemv_words_off(K, splits, g, XF16));
+  int32_t* s_words = reinterpret_cast<int32_t*>(s_raw + gemv_words_off(K, splits, g, false));
   if (bulk) {
     if (threadIdx.x == 0) {
       mbar_init(&s_wbar, 1);
@@ -376,15 +396,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
     for (int j = 0; j < kXB; ++j) {
       const int i = base + j * kGemvThreads + threadIdx.x;
       if (i < kspan) {
-        if constexpr (XF16)
-          reinterpret_cast<__half*>(s_raw)[i] = __float2half_rn(v[j]);  // exact: kGemvX inputs are fp16
-        else
-          reinterpret_cast<float*>(s_raw)[i] = v[j];
+        reinterpret_cast<float*>(s_raw)[i] = v[j];  // fp32 (fp16 inputs convert exactly)
       }
     }
   }
   // the scale / zero rows of the groups [g0, g1] this block's K range touches
-  const int xbytes = (XF16 ? 2 : 4) * gemv_x_elems(K, splits);
+  const int xbytes = 4 * gemv_x_elems(K, splits);
   __half* s_s = reinterpret_cast<__half*>(s_raw + ((xbytes + 15) & ~15));
   const int ng_max = gemv_groups(K, splits, g);
   __half* s_z = s_s + ng_max * 128;
@@ -432,14 +449,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(ProjDev w0, ProjDev w1
   __syncthreads();
   float acc[4][2] = {};
   const GroupStage gs{s_s, s_z, g0};
-  RowAcc<XF16> ra(K, g, nb, lane, k0, s_raw, gs);
+  RowAcc<SUB> ra(K, g, nb, lane, k0, s_raw, gs);
   if (bulk) {
     if (warp_wait(&s_wbar, 0u, kDevTimeoutTmaFull)) {
       for (int r = wr0; r < wr1; ++r)
         ra.row(r, *reinterpret_cast<const uint4*>(s_words + (r - r0) * kGemvCols + lane * 4), acc);
     }
   } else if (n < N) {
-    gemv_rows<XF16>(wbase, N, n, wr0, wr1, ra, wv, acc);
+    gemv_rows<SUB>(wbase, N, n, wr0, wr1, ra, wv, acc);
   }
 #pragma unroll
   for (int c = 0; c < 4; ++c) s_red[warp][lane * 4 + c] = acc[c][0] + acc[c][1];
@@ -498,7 +515,7 @@ __global__ void k_decode_combine(const float* __restrict__ part, int splits, int
   out[i] = r;
 }
 
-template <bool XF16>
+template <bool SUB>
 cudaError_t launch_gemv_t(const ProjDev& w0, const ProjDev* w1, const int32_t* idx, int rows_a, const GemvSrc& src,
                           float* part, int splits, cudaStream_t s) {
   const int nmat = (w1 != nullptr) ? 2 : 1;
@@ -506,26 +523,26 @@ cudaError_t launch_gemv_t(const ProjDev& w0, const ProjDev* w1, const int32_t* i
   // plus the scale and zero rows of the groups it touches
   const int word_bytes = gemv_word_rows(w0.k, splits) * kGemvCols * 4;
   const int bulk = (w0.n % kGemvCols == 0 && word_bytes <= kGemvWordBudget) ? 1 : 0;
-  const size_t smem = static_cast<size_t>(gemv_words_off(w0.k, splits, w0.group_size, XF16)) + (bulk ? word_bytes : 0);
+  const size_t smem = static_cast<size_t>(gemv_words_off(w0.k, splits, w0.group_size, false)) + (bulk ? word_bytes : 0);
   static std::atomic<size_t> smem_done[kMaxDevices];  // per device: the attribute is per device
   if (smem > 48 * 1024) {
-    cudaError_t e = raise_smem_limit(k_gemv<XF16>, smem, smem_done);
+    cudaError_t e = raise_smem_limit(k_gemv<SUB>, smem, smem_done);
     if (e != cudaSuccess) return e;
   }
   dim3 grid((w0.n + kGemvCols - 1) / kGemvCols, splits, nmat * rows_a);
-  return launch_dep(k_gemv<XF16>, grid, dim3(kGemvThreads), smem, s, w0, w1 != nullptr ? *w1 : w0, idx, rows_a, src,
+  return launch_dep(k_gemv<SUB>, grid, dim3(kGemvThreads), smem, s, w0, w1 != nullptr ? *w1 : w0, idx, rows_a, src,
                     part, splits, bulk);
 }
 
 }  // namespace
 
 int gemv_default_splits(int k, int n, int rows_a, int num_sms, int nmat) {
-  // the largest power-of-two split that keeps the grid within one wave of two CTAs
-  // per SM (each CTA issues all its word loads early; a second wave would pay the
-  // HBM latency again), with at least 256 k per split
+  // the largest power-of-two split that keeps the grid within one wave of
+  // kGemvCtasPerSm CTAs per SM (each CTA issues all its word loads early; a second
+  // wave would pay the HBM latency again), with at least 256 k per split
   const int ctas = ((n + kGemvCols - 1) / kGemvCols) * rows_a * nmat;
   int s = 1;
-  while (ctas * s * 2 <= 2 * num_sms && s < 16 && (k / (s * 2)) >= 256) s *= 2;
+  while (ctas * s * 2 <= kGemvCtasPerSm * num_sms && s < 16 && (k / (s * 2)) >= 256) s *= 2;
   return s;
 }
 
@@ -534,8 +551,10 @@ cudaError_t launch_gemv(const ProjDev& w0, const ProjDev* w1, const int32_t* idx
   if (rows_a == 0) return cudaSuccess;
   // the fast inner loop needs whole words inside one scale group for b in {1, 2, 4}
   if (w0.group_size % 32 != 0 || (w1 != nullptr && w1->group_size % 32 != 0)) return cudaErrorNotSupported;
-  return src.mode == kGemvX ? launch_gemv_t<true>(w0, w1, idx, rows_a, src, part, splits, s)
-                            : launch_gemv_t<false>(w0, w1, idx, rows_a, src, part, splits, s);
+  // the single-instruction dequant when every scale of the projection(s) allows it
+  const bool sub = w0.sub_ok != 0 && (w1 == nullptr || w1->sub_ok != 0);
+  return sub ? launch_gemv_t<true>(w0, w1, idx, rows_a, src, part, splits, s)
+             : launch_gemv_t<false>(w0, w1, idx, rows_a, src, part, splits, s);
 }
 
 cudaError_t launch_gemv_reduce(const float* part, int splits, int rows_a, int n, uint16_t* out, cudaStream_t s) {

@@ -6,7 +6,8 @@ compute fp16(q * s + z) with one rounding (gemq/triton_kernels/utils.py:206-210)
 the GEMM's summation order does not depend on the form, so a block whose only change
 is one scale of an expert no token is routed to must give the same bits. Every
 bit-width (1-4) meets both forms, at decode (token tiles 16 / 32) and prefill (64)
-sizes; the outputs are also checked against the oracle's dequantised weights.
+sizes and in the one-token GEMV path; the outputs are also checked against the
+oracle's dequantised weights.
 """
 
 from __future__ import annotations
@@ -70,7 +71,10 @@ def test_dequant_forms_bit_identical(proj):
         idx, w = _routing(T, seed)
         cases.append((x, idx, w))
     _lib.device_error()
+    one_x = torch.randn((1, HIDDEN), generator=torch.Generator(device="cuda").manual_seed(9), device="cuda").half()
+    one_idx, one_w = _routing(1, 9)
     y_sub = [blk.forward_routed(x, idx, w) for x, idx, w in cases]
+    y_sub.append(blk.forward_routed(one_x, one_idx, one_w, one_token=True))  # the one-token GEMV path
     # one scale of the unrouted expert out of the single-instruction range (exponent 15)
     scales = getattr(blk, f"{proj}_scales")
     z0 = int(getattr(blk, f"{proj}_zs_strides")[E - 1].item())
@@ -79,6 +83,7 @@ def test_dequant_forms_bit_identical(proj):
     forms = _forms(blk)
     assert forms == [int(p != proj) for p in ("w1", "w3", "w2")]
     y_gen = [blk.forward_routed(x, idx, w) for x, idx, w in cases]
+    y_gen.append(blk.forward_routed(one_x, one_idx, one_w, one_token=True))
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
     for a, b in zip(y_sub, y_gen):
