@@ -264,6 +264,15 @@ int gemq_layer_stage_times(gemq_layer_t* layer, float* ms_out /* host */);
  * counterpart (a diagnostic). */
 int gemq_layer_dequant_forms(const gemq_layer_t* layer, int32_t* forms_out /* host */);
 
+/* RMSNorm of the decoder layers around the MoE blocks (transformers' OlmoeRMSNorm):
+ * out = fp16(weight * fp16(x * rsqrt(mean(x^2) + eps))) per row, x in fp32, in one
+ * launch. x, out fp16 [rows, n], weight fp16 [n]; n % 8 == 0; pointers 16-byte
+ * aligned. Not part of the reference's MoE path: the whole-model decode harness
+ * (robustgemq_b200/inference/generate.py) uses it in place of the eager module's six
+ * kernels per norm. */
+int gemq_rms_norm(const uint16_t* x, const uint16_t* weight, int64_t rows, int32_t n, float eps, uint16_t* out,
+                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

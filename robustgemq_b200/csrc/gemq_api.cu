@@ -1035,6 +1035,19 @@ int gemq_layer_dequant_forms(const gemq_layer_t* layer, int32_t* forms_out) {
   return GEMQ_OK;
 }
 
+int gemq_rms_norm(const uint16_t* x, const uint16_t* weight, int64_t rows, int32_t n, float eps, uint16_t* out,
+                  void* stream) {
+  TraceRange trace("gemq_rms_norm");
+  if (rows < 0 || rows > INT32_MAX || n <= 0 || n % 8 != 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad rows or n");
+  if (rows == 0) return GEMQ_OK;
+  if (x == nullptr || weight == nullptr || out == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(out)) &
+       15u) != 0)
+    return fail(GEMQ_ERR_UNSUPPORTED, "x, weight and out must start on a 16-byte boundary");
+  GEMQ_CUDA(launch_rms_norm(x, weight, rows, n, eps, out, static_cast<cudaStream_t>(stream)), "rms norm");
+  return GEMQ_OK;
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------------ allocation-free group GEMM

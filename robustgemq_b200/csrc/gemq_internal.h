@@ -157,6 +157,8 @@ cudaError_t launch_unpack(const int32_t* packed, int64_t rows, int64_t pcols, in
                           cudaStream_t s);
 cudaError_t launch_dequant_expert(const ProjDev& p, int expert, uint16_t* out, cudaStream_t s);
 cudaError_t launch_swiglu_f16(const uint16_t* a, const uint16_t* b, int64_t n, uint16_t* h, cudaStream_t s);
+cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, int n, float eps, uint16_t* y,
+                            cudaStream_t s);
 
 // Decode GEMV family (CUDA cores, deterministic split-K); see kernels_decode.cu.
 enum GemvMode : int { kGemvX = 0, kGemvSwiGLU = 1, kGemvPartF32 = 2, kGemvPartF16 = 3 };

@@ -181,4 +181,62 @@ cudaError_t launch_swiglu_f16(const uint16_t* a, const uint16_t* b, int64_t n, u
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ RMSNorm (model harness)
+// y = fp16(w * fp16(x * rsqrt(mean(x^2) + eps))), x in fp32: the RMSNorm of the
+// decoder layers around the MoE blocks (transformers' OlmoeRMSNorm, T5-style), one
+// launch instead of the six element-wise and reduction kernels of the eager module.
+// One CTA per row, 8 fp16 per thread and chunk (n % 8 == 0); the sum of squares is
+// reduced in fp32 (warp shuffles, then the warps' sums in order).
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) k_rms_norm(const __half* __restrict__ x, const __half* __restrict__ w,
+                                                          int n, float eps, __half* __restrict__ y) {
+  const int64_t row = blockIdx.x;
+  const uint4* x4 = reinterpret_cast<const uint4*>(x + row * n);
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  uint4* y4 = reinterpret_cast<uint4*>(y + row * n);
+  const int n8 = n / 8;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n8; i += kNormThreads) {
+    const uint4 v = x4[i];
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+  __shared__ float s_part[kNormThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += s_part[i];
+  const float inv = rsqrtf(tot / static_cast<float>(n) + eps);
+  for (int i = threadIdx.x; i < n8; i += kNormThreads) {
+    const uint4 v = x4[i], wv = w4[i];
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+    const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+    uint4 o;
+    __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      oh[j] = __hmul2(wh[j], __floats2half2_rn(f.x * inv, f.y * inv));
+    }
+    y4[i] = o;
+  }
+}
+
+cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, int n, float eps, uint16_t* y,
+                            cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  k_rms_norm<<<static_cast<unsigned>(rows), kNormThreads, 0, s>>>(
+      reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(w), n, eps, reinterpret_cast<__half*>(y));
+  return cudaGetLastError();
+}
+
 }  // namespace gemq

@@ -8,7 +8,8 @@ which replays CUDA graphs the same way).
 own modelling code) with seeded random weights. No checkpoint is available here. Its MoE
 blocks are ``QuantFusedOlmoeMoEBlock`` with packed experts (the config's bit mix),
 and its attention projections are 4-bit ``QuantLinear`` layers (the reference's
-GemLite 4-bit attention). Embeddings, norms and the LM head stay fp16.
+GemLite 4-bit attention). Embeddings and the LM head stay fp16; the RMSNorms run in
+one launch each (``RMSNormF16``, this library's ``gemq_rms_norm``).
 ``StaticDecoder`` prefills a prompt eagerly and then decodes greedily, one CUDA graph
 replay per token.
 """
@@ -21,7 +22,7 @@ from typing import Optional
 import torch
 from torch import Tensor, nn
 
-from .. import synth
+from .. import _lib, synth
 from ..quant import rtn_quantize
 from .linear import QuantLinear
 from .moe_block import QuantFusedOlmoeMoEBlock
@@ -41,6 +42,33 @@ class MoEAdapter(nn.Module):
         return out[0] if isinstance(out, tuple) else out
 
 
+class RMSNormF16(nn.Module):
+    """transformers' OlmoeRMSNorm on fp16 rows in one launch (``gemq_rms_norm``):
+    ``weight * fp16(x * rsqrt(mean(x^2) + eps))`` with x in fp32, where the eager module
+    runs six element-wise and reduction kernels. The sum of squares is reduced in
+    another order than torch's, so a result can differ from the eager module's by one
+    fp16 ulp."""
+
+    def __init__(self, weight: Tensor, eps: float):
+        super().__init__()
+        self.weight = nn.Parameter(weight.detach().to(torch.float16).contiguous(), requires_grad=False)
+        self.variance_epsilon = float(eps)
+
+    def forward(self, hidden_states: Tensor) -> Tensor:
+        n = hidden_states.shape[-1]
+        x = hidden_states.reshape(-1, n).contiguous()
+        if x.dtype != torch.float16 or not x.is_cuda:
+            raise ValueError("RMSNormF16 takes fp16 CUDA tensors")
+        out = torch.empty_like(x)
+        _lib.check(_lib.load().gemq_rms_norm(_lib.ptr(x), _lib.ptr(self.weight), x.shape[0], n, self.variance_epsilon,
+                                             _lib.ptr(out), _lib.stream_ptr(x.device)))
+        return out.reshape(hidden_states.shape)
+
+
+def _fused_norm(norm: nn.Module) -> RMSNormF16:
+    return RMSNormF16(norm.weight, norm.variance_epsilon)
+
+
 def _quant_linear(out_f: int, in_f: int, nbits: int, group_size: int, gen: torch.Generator, device) -> QuantLinear:
     W = (torch.randn((out_f, in_f), generator=gen, device=device) * 0.02).half()
     Q, s, z = rtn_quantize(W, nbits, group_size)
@@ -48,11 +76,13 @@ def _quant_linear(out_f: int, in_f: int, nbits: int, group_size: int, gen: torch
 
 
 def synthetic_olmoe(num_layers: int = 16, device="cuda", seed: int = 0, attn_bits: int = 4,
-                    attn_group: int = 64, max_position_embeddings: int = 4096, blocks=None):
+                    attn_group: int = 64, max_position_embeddings: int = 4096, blocks=None,
+                    fused_norms: bool = True):
     """OLMoE-1B-7B-shaped causal LM (hidden 2048, 16 heads, 64 experts top-8,
     intermediate 1024, vocab 50304) with seeded random weights, MoE blocks of this
     library (``blocks``: already built ``QuantFusedOlmoeMoEBlock`` layers to use, one
-    per decoder layer) and ``attn_bits``-bit attention projections."""
+    per decoder layer), ``attn_bits``-bit attention projections, and (``fused_norms``)
+    the RMSNorms in one launch each (``RMSNormF16``)."""
     from transformers import OlmoeConfig, OlmoeForCausalLM
     from transformers.models.olmoe.modeling_olmoe import OlmoeRotaryEmbedding
 
@@ -87,6 +117,13 @@ def synthetic_olmoe(num_layers: int = 16, device="cuda", seed: int = 0, attn_bit
         att = layer.self_attn
         for pname in ("q_proj", "k_proj", "v_proj", "o_proj"):
             setattr(att, pname, _quant_linear(D, D, attn_bits, attn_group, gen, device))
+        if fused_norms:
+            layer.input_layernorm = _fused_norm(layer.input_layernorm)
+            layer.post_attention_layernorm = _fused_norm(layer.post_attention_layernorm)
+            att.q_norm = _fused_norm(att.q_norm)
+            att.k_norm = _fused_norm(att.k_norm)
+    if fused_norms:
+        model.model.norm = _fused_norm(model.model.norm)
     model.eval()
     return model
 

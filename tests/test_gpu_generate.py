@@ -36,3 +36,29 @@ def test_graph_decode_matches_eager_decode(cuda_device):
     seq2, _ = dec.generate(prompt, new)
     assert torch.equal(seq2, seq)
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("rows", [1, 9, 64])
+def test_fused_rms_norm_matches_transformers(cuda_device, rows):
+    """``RMSNormF16`` (one launch) against transformers' OlmoeRMSNorm on the same
+    fp16 rows and random weights. The sums of squares are reduced in different
+    orders, so the normalised value fp16(x * rsqrt(.)) may differ by one fp16 ulp;
+    after the multiply by the weight and its rounding that is at most |w| times that
+    ulp plus one ulp of the output, about two output ulps."""
+    from transformers.models.olmoe.modeling_olmoe import OlmoeRMSNorm
+
+    from robustgemq_b200.inference.generate import RMSNormF16
+
+    g = torch.Generator(device="cuda").manual_seed(rows)
+    x = (torch.randn((rows, 2048), generator=g, device="cuda") * 3).half()
+    ref = OlmoeRMSNorm(2048, eps=1e-5).cuda().half()
+    with torch.no_grad():
+        ref.weight.copy_(torch.rand((2048,), generator=g, device="cuda") * 2 - 0.5)
+        y_ref = ref(x)
+    y = RMSNormF16(ref.weight, ref.variance_epsilon)(x)
+    torch.cuda.synchronize()
+    assert y.shape == y_ref.shape and y.dtype == torch.float16
+    ulp = torch.finfo(torch.float16).eps * y_ref.float().abs().clamp_min(2.0 ** -14)
+    assert ((y.float() - y_ref.float()).abs() <= 2 * ulp).all()
+    mismatched = (y != y_ref).float().mean().item()
+    assert mismatched < 0.01
