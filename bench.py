@@ -668,9 +668,9 @@ def run_generate(blocks, device):
         layer.mlp = None
     del dec, model
     torch.cuda.empty_cache()
-    return {"workload": "olmoe-1b-7b-shaped model, 16 MoE layers of this library, 4-bit attention, fused fp16 "
-                        "RMSNorms, fp16 embeddings / LM head; 9-token prompt, 64 new tokens, greedy; median of 3 "
-                        "rounds",
+    return {"workload": "olmoe-1b-7b-shaped model, 16 MoE layers of this library, 4-bit attention (one q|k|v "
+                        "projection, q/k norm + rotary in one launch), fused fp16 RMSNorms, fp16 embeddings / LM "
+                        "head; 9-token prompt, 64 new tokens, greedy; median of 3 rounds",
             "decode_tokens_per_s": round(dec_tps, 1), "prefill_tokens_per_s": round(pre_tps, 1),
             "decode_path": "static KV cache, decode step replayed as one CUDA graph"}
 

@@ -273,6 +273,18 @@ int gemq_layer_dequant_forms(const gemq_layer_t* layer, int32_t* forms_out /* ho
 int gemq_rms_norm(const uint16_t* x, const uint16_t* weight, int64_t rows, int32_t n, float eps, uint16_t* out,
                   void* stream);
 
+/* The attention prologue of transformers' OlmoeAttention after a fused q|k|v
+ * projection, in one launch: per row of qkv (fp16 [rows, >= 2n], row stride ld),
+ * q and k (the first two blocks of n values) each through RMSNorm with its own weight
+ * (as gemq_rms_norm), then the rotary embedding of apply_rotary_pos_emb on fp16
+ * tensors per head of head_dim values: out = fp16(fp16(x * cos) +
+ * fp16(rotate_half(x) * sin)), cos / sin fp16 [rows, head_dim]. q_out, k_out fp16
+ * [rows, n]. n % 8 == 0, ld % 8 == 0, qkv and the weights 16-byte aligned. Not part of
+ * the reference's MoE path: used by the whole-model decode harness. */
+int gemq_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, int32_t n, int32_t head_dim,
+                      const uint16_t* q_norm_weight, const uint16_t* k_norm_weight, float eps, const uint16_t* cos,
+                      const uint16_t* sin, uint16_t* q_out, uint16_t* k_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

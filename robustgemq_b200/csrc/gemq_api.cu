@@ -1048,6 +1048,26 @@ int gemq_rms_norm(const uint16_t* x, const uint16_t* weight, int64_t rows, int32
   return GEMQ_OK;
 }
 
+int gemq_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, int32_t n, int32_t head_dim,
+                      const uint16_t* q_norm_weight, const uint16_t* k_norm_weight, float eps, const uint16_t* cos,
+                      const uint16_t* sin, uint16_t* q_out, uint16_t* k_out, void* stream) {
+  TraceRange trace("gemq_qk_norm_rope");
+  if (rows < 0 || rows > INT32_MAX || n <= 0 || n % 8 != 0 || head_dim <= 0 || head_dim % 2 != 0 ||
+      n % head_dim != 0 || ld < 2 * static_cast<int64_t>(n) || ld % 8 != 0)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad rows, n, head_dim or ld");
+  if (rows == 0) return GEMQ_OK;
+  if (qkv == nullptr || q_norm_weight == nullptr || k_norm_weight == nullptr || cos == nullptr || sin == nullptr ||
+      q_out == nullptr || k_out == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(q_norm_weight) |
+        reinterpret_cast<uintptr_t>(k_norm_weight)) & 15u) != 0)
+    return fail(GEMQ_ERR_UNSUPPORTED, "qkv and the norm weights must start on a 16-byte boundary");
+  GEMQ_CUDA(launch_qk_norm_rope(qkv, ld, rows, n, head_dim, q_norm_weight, k_norm_weight, eps, cos, sin, q_out, k_out,
+                                static_cast<cudaStream_t>(stream)),
+            "q/k norm + rotary");
+  return GEMQ_OK;
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------------ allocation-free group GEMM

@@ -159,6 +159,9 @@ cudaError_t launch_dequant_expert(const ProjDev& p, int expert, uint16_t* out, c
 cudaError_t launch_swiglu_f16(const uint16_t* a, const uint16_t* b, int64_t n, uint16_t* h, cudaStream_t s);
 cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, int n, float eps, uint16_t* y,
                             cudaStream_t s);
+cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, int n, int hd, const uint16_t* wq,
+                                const uint16_t* wk, float eps, const uint16_t* cos_t, const uint16_t* sin_t,
+                                uint16_t* q_out, uint16_t* k_out, cudaStream_t s);
 
 // Decode GEMV family (CUDA cores, deterministic split-K); see kernels_decode.cu.
 enum GemvMode : int { kGemvX = 0, kGemvSwiGLU = 1, kGemvPartF32 = 2, kGemvPartF16 = 3 };

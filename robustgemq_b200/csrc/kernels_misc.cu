@@ -239,4 +239,100 @@ cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, 
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ Q/K norm + rotary (model harness)
+// For one token row of a fused q|k|v projection (row stride ld): qn = RMSNorm(q) and
+// kn = RMSNorm(k) with their own weights (as k_rms_norm), then the rotary embedding
+// of transformers' apply_rotary_pos_emb on fp16 tensors: out = fp16(fp16(x * cos) +
+// fp16(rotate_half(x) * sin)), rotate_half(x)[j] = -x[j + hd/2] for j < hd/2, else
+// x[j - hd/2], per head of hd values; cos / sin fp16 [rows, hd]. The normalised rows
+// are staged in shared memory (the rotation pairs values of different threads).
+__global__ void __launch_bounds__(kNormThreads) k_qk_norm_rope(const __half* __restrict__ qkv, int64_t ld, int n, int hd,
+                                                              const __half* __restrict__ wq, const __half* __restrict__ wk,
+                                                              float eps, const __half* __restrict__ cos_t,
+                                                              const __half* __restrict__ sin_t, __half* __restrict__ q_out,
+                                                              __half* __restrict__ k_out) {
+  extern __shared__ __align__(16) __half s_qk[];  // [2][n]
+  const int64_t row = blockIdx.x;
+  const __half* src[2] = {qkv + row * ld, qkv + row * ld + n};
+  const __half* wts[2] = {wq, wk};
+  const int n8 = n / 8;
+  float ss[2] = {0.f, 0.f};
+  for (int m = 0; m < 2; ++m) {
+    const uint4* x4 = reinterpret_cast<const uint4*>(src[m]);
+    for (int i = threadIdx.x; i < n8; i += kNormThreads) {
+      const uint4 v = x4[i];
+      const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        ss[m] = fmaf(f.x, f.x, ss[m]);
+        ss[m] = fmaf(f.y, f.y, ss[m]);
+      }
+    }
+  }
+  __shared__ float s_part[2][kNormThreads / 32];
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], o);
+    if ((threadIdx.x & 31) == 0) s_part[m][threadIdx.x >> 5] = ss[m];
+  }
+  __syncthreads();
+  for (int m = 0; m < 2; ++m) {
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNormThreads / 32; ++i) tot += s_part[m][i];
+    const float inv = rsqrtf(tot / static_cast<float>(n) + eps);
+    const uint4* x4 = reinterpret_cast<const uint4*>(src[m]);
+    const uint4* w4 = reinterpret_cast<const uint4*>(wts[m]);
+    uint4* d4 = reinterpret_cast<uint4*>(s_qk + m * n);
+    for (int i = threadIdx.x; i < n8; i += kNormThreads) {
+      const uint4 v = x4[i], wv = w4[i];
+      const __half2* h = reinterpret_cast<const __half2*>(&v);
+      const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+      uint4 o;
+      __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        oh[j] = __hmul2(wh[j], __floats2half2_rn(f.x * inv, f.y * inv));
+      }
+      d4[i] = o;
+    }
+  }
+  __syncthreads();
+  const int half = hd / 2;
+  const __half* c = cos_t + row * hd;
+  const __half* sn = sin_t + row * hd;
+  for (int m = 0; m < 2; ++m) {
+    const __half* xs = s_qk + m * n;
+    __half* out = (m == 0 ? q_out : k_out) + row * n;
+    for (int i = threadIdx.x; i < n; i += kNormThreads) {
+      const int j = i % hd;
+      const __half x = xs[i];
+      const __half rot = j < half ? __hneg(xs[i + half]) : xs[i - half];
+      // the _rn forms keep each product and the sum rounded on its own, as the
+      // three fp16 tensor ops are (no contraction into an fp16 fma)
+      out[i] = __hadd_rn(__hmul_rn(x, c[j]), __hmul_rn(rot, sn[j]));
+    }
+  }
+}
+
+cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, int n, int hd, const uint16_t* wq,
+                                const uint16_t* wk, float eps, const uint16_t* cos_t, const uint16_t* sin_t,
+                                uint16_t* q_out, uint16_t* k_out, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const size_t smem = 2 * static_cast<size_t>(n) * sizeof(__half);
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(k_qk_norm_rope, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  k_qk_norm_rope<<<static_cast<unsigned>(rows), kNormThreads, smem, s>>>(
+      reinterpret_cast<const __half*>(qkv), ld, n, hd, reinterpret_cast<const __half*>(wq),
+      reinterpret_cast<const __half*>(wk), eps, reinterpret_cast<const __half*>(cos_t),
+      reinterpret_cast<const __half*>(sin_t), reinterpret_cast<__half*>(q_out), reinterpret_cast<__half*>(k_out));
+  return cudaGetLastError();
+}
+
 }  // namespace gemq

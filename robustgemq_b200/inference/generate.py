@@ -69,20 +69,85 @@ def _fused_norm(norm: nn.Module) -> RMSNormF16:
     return RMSNormF16(norm.weight, norm.variance_epsilon)
 
 
-def _quant_linear(out_f: int, in_f: int, nbits: int, group_size: int, gen: torch.Generator, device) -> QuantLinear:
-    W = (torch.randn((out_f, in_f), generator=gen, device=device) * 0.02).half()
+def _rand_w(out_f: int, in_f: int, gen: torch.Generator, device) -> Tensor:
+    return (torch.randn((out_f, in_f), generator=gen, device=device) * 0.02).half()
+
+
+def _quant_from_w(W: Tensor, nbits: int, group_size: int) -> QuantLinear:
+    # RTN groups run along the input dim of each output row, so quantising stacked
+    # weights row-wise equals quantising each part alone
     Q, s, z = rtn_quantize(W, nbits, group_size)
-    return QuantLinear(nbits, group_size, in_f, out_f).pack(Q, s, z)
+    return QuantLinear(nbits, group_size, W.shape[1], W.shape[0]).pack(Q, s, z)
+
+
+class FusedOlmoeAttention(nn.Module):
+    """transformers' OlmoeAttention (``modeling_olmoe.OlmoeAttention.forward``) with
+    q, k and v from one 4-bit projection (one GEMV) and its prologue, q_norm / k_norm
+    and the rotary embedding, in one launch (``gemq_qk_norm_rope``); the cache update,
+    the attention kernel (the model's ``_attn_implementation``) and o_proj are the
+    module's own. ``attn`` is the replaced module, kept for its configuration."""
+
+    def __init__(self, attn: nn.Module, qkv_proj: QuantLinear):
+        super().__init__()
+        if getattr(attn.config, "clip_qkv", None) is not None:
+            raise ValueError("clip_qkv is not supported by the fused attention prologue")
+        self.config = attn.config
+        self.layer_idx = attn.layer_idx
+        self.head_dim = attn.head_dim
+        self.scaling = attn.scaling
+        self.is_causal = True
+        self.num_key_value_groups = attn.num_key_value_groups
+        self.attention_dropout = attn.attention_dropout
+        self.qkv_proj = qkv_proj
+        self.o_proj = attn.o_proj
+        self.q_norm_weight = nn.Parameter(attn.q_norm.weight.detach().half().contiguous(), requires_grad=False)
+        self.k_norm_weight = nn.Parameter(attn.k_norm.weight.detach().half().contiguous(), requires_grad=False)
+        self.eps = float(attn.q_norm.variance_epsilon)
+        if float(attn.k_norm.variance_epsilon) != self.eps:
+            raise ValueError("q_norm and k_norm must share eps")
+
+    def forward(self, hidden_states: Tensor, position_embeddings, attention_mask, past_key_values=None, **kwargs):
+        from transformers.models.olmoe.modeling_olmoe import ALL_ATTENTION_FUNCTIONS, eager_attention_forward
+
+        input_shape = hidden_states.shape[:-1]
+        hidden_shape = (*input_shape, -1, self.head_dim)
+        qkv = self.qkv_proj(hidden_states)  # [..., 3 D]
+        n = qkv.shape[-1] // 3
+        rows = qkv.numel() // qkv.shape[-1]
+        cos, sin = position_embeddings
+        cos = cos.to(torch.float16).contiguous()
+        sin = sin.to(torch.float16).contiguous()
+        if cos.numel() != rows * self.head_dim:
+            raise ValueError("rotary tables must have one row per token")
+        q = torch.empty((*input_shape, n), dtype=torch.float16, device=qkv.device)
+        k = torch.empty_like(q)
+        _lib.check(_lib.load().gemq_qk_norm_rope(
+            _lib.ptr(qkv), qkv.stride(-2) if qkv.dim() > 1 else 3 * n, rows, n, self.head_dim,
+            _lib.ptr(self.q_norm_weight), _lib.ptr(self.k_norm_weight), self.eps, _lib.ptr(cos), _lib.ptr(sin),
+            _lib.ptr(q), _lib.ptr(k), _lib.stream_ptr(qkv.device)))
+        query_states = q.view(hidden_shape).transpose(1, 2)
+        key_states = k.view(hidden_shape).transpose(1, 2)
+        value_states = qkv[..., 2 * n:].view(hidden_shape).transpose(1, 2)
+        if past_key_values is not None:
+            key_states, value_states = past_key_values.update(key_states, value_states, self.layer_idx)
+        attention_interface = ALL_ATTENTION_FUNCTIONS.get_interface(self.config._attn_implementation,
+                                                                    eager_attention_forward)
+        attn_output, attn_weights = attention_interface(
+            self, query_states, key_states, value_states, attention_mask, dropout=0.0, scaling=self.scaling,
+            sliding_window=getattr(self.config, "sliding_window", None), **kwargs)
+        attn_output = attn_output.reshape(*input_shape, -1).contiguous()
+        return self.o_proj(attn_output), attn_weights
 
 
 def synthetic_olmoe(num_layers: int = 16, device="cuda", seed: int = 0, attn_bits: int = 4,
                     attn_group: int = 64, max_position_embeddings: int = 4096, blocks=None,
-                    fused_norms: bool = True):
+                    fused_norms: bool = True, fused_attention: bool = True):
     """OLMoE-1B-7B-shaped causal LM (hidden 2048, 16 heads, 64 experts top-8,
     intermediate 1024, vocab 50304) with seeded random weights, MoE blocks of this
     library (``blocks``: already built ``QuantFusedOlmoeMoEBlock`` layers to use, one
-    per decoder layer), ``attn_bits``-bit attention projections, and (``fused_norms``)
-    the RMSNorms in one launch each (``RMSNormF16``)."""
+    per decoder layer), ``attn_bits``-bit attention projections, (``fused_norms``) the
+    RMSNorms in one launch each (``RMSNormF16``) and (``fused_attention``) the attention
+    as ``FusedOlmoeAttention``. The random weights do not depend on the two flags."""
     from transformers import OlmoeConfig, OlmoeForCausalLM
     from transformers.models.olmoe.modeling_olmoe import OlmoeRotaryEmbedding
 
@@ -115,13 +180,20 @@ def synthetic_olmoe(num_layers: int = 16, device="cuda", seed: int = 0, attn_bit
                                      shp["num_experts"], shp["mean_bits"], shp["group_size"], seed * 1000 + l, device)
         layer.mlp = MoEAdapter(blk)
         att = layer.self_attn
-        for pname in ("q_proj", "k_proj", "v_proj", "o_proj"):
-            setattr(att, pname, _quant_linear(D, D, attn_bits, attn_group, gen, device))
+        wq, wk, wv, wo = (_rand_w(D, D, gen, device) for _ in range(4))
+        att.o_proj = _quant_from_w(wo, attn_bits, attn_group)
+        if fused_attention:
+            layer.self_attn = FusedOlmoeAttention(att, _quant_from_w(torch.cat([wq, wk, wv]), attn_bits, attn_group))
+        else:
+            att.q_proj = _quant_from_w(wq, attn_bits, attn_group)
+            att.k_proj = _quant_from_w(wk, attn_bits, attn_group)
+            att.v_proj = _quant_from_w(wv, attn_bits, attn_group)
         if fused_norms:
             layer.input_layernorm = _fused_norm(layer.input_layernorm)
             layer.post_attention_layernorm = _fused_norm(layer.post_attention_layernorm)
-            att.q_norm = _fused_norm(att.q_norm)
-            att.k_norm = _fused_norm(att.k_norm)
+            if not fused_attention:
+                att.q_norm = _fused_norm(att.q_norm)
+                att.k_norm = _fused_norm(att.k_norm)
     if fused_norms:
         model.model.norm = _fused_norm(model.model.norm)
     model.eval()

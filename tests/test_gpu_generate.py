@@ -62,3 +62,65 @@ def test_fused_rms_norm_matches_transformers(cuda_device, rows):
     assert ((y.float() - y_ref.float()).abs() <= 2 * ulp).all()
     mismatched = (y != y_ref).float().mean().item()
     assert mismatched < 0.01
+
+
+@pytest.mark.parametrize("rows", [1, 9])
+def test_fused_qk_norm_rope_matches_transformers(cuda_device, rows):
+    """``gemq_qk_norm_rope`` against transformers' q_norm / k_norm (OlmoeRMSNorm) and
+    apply_rotary_pos_emb on the same fp16 rows, random norm weights and the model's
+    own rotary tables. The norm may differ by about two fp16 ulps (see above); the
+    rotation adds and rounds two such values, which may nearly cancel, so the bound is
+    four ulps of the result plus a small absolute term (a quarter ulp of the largest
+    value)."""
+    from transformers import OlmoeConfig
+    from transformers.models.olmoe.modeling_olmoe import OlmoeRMSNorm, OlmoeRotaryEmbedding, apply_rotary_pos_emb
+
+    from robustgemq_b200 import _lib
+
+    D, H, hd = 2048, 16, 128
+    g = torch.Generator(device="cuda").manual_seed(10 + rows)
+    qkv = (torch.randn((1, rows, 3 * D), generator=g, device="cuda") * 2).half()
+    qn, kn = OlmoeRMSNorm(D).cuda().half(), OlmoeRMSNorm(D).cuda().half()
+    with torch.no_grad():
+        qn.weight.copy_(torch.rand((D,), generator=g, device="cuda") + 0.5)
+        kn.weight.copy_(torch.rand((D,), generator=g, device="cuda") + 0.5)
+        cfg = OlmoeConfig(hidden_size=D, num_attention_heads=H, num_key_value_heads=H, max_position_embeddings=64)
+        rope = OlmoeRotaryEmbedding(config=cfg, device="cuda")
+        pos = torch.arange(5, 5 + rows, device="cuda").view(1, -1)
+        cos, sin = rope(qkv, pos)
+        q_ref = qn(qkv[..., :D]).view(1, rows, H, hd).transpose(1, 2)
+        k_ref = kn(qkv[..., D:2 * D]).view(1, rows, H, hd).transpose(1, 2)
+        q_ref, k_ref = apply_rotary_pos_emb(q_ref, k_ref, cos, sin)
+    q = torch.empty((rows, D), dtype=torch.float16, device="cuda")
+    k = torch.empty_like(q)
+    cos16, sin16 = cos.half().contiguous(), sin.half().contiguous()
+    _lib.check(_lib.load().gemq_qk_norm_rope(_lib.ptr(qkv), 3 * D, rows, D, hd, _lib.ptr(qn.weight.data),
+                                             _lib.ptr(kn.weight.data), qn.variance_epsilon, _lib.ptr(cos16),
+                                             _lib.ptr(sin16), _lib.ptr(q), _lib.ptr(k), _lib.stream_ptr(q.device)))
+    torch.cuda.synchronize()
+    for got, ref in ((q, q_ref), (k, k_ref)):
+        ref = ref.transpose(1, 2).reshape(rows, D).float()
+        ulp = torch.finfo(torch.float16).eps * ref.abs().clamp_min(2.0 ** -14)
+        err = (got.float() - ref).abs()
+        assert (err <= 4 * ulp + 4 * torch.finfo(torch.float16).eps * ref.abs().max() * 2.0 ** -4).all()
+        assert (got != ref.half()).float().mean().item() < 0.02
+
+
+def test_fused_attention_model_matches_unfused(cuda_device):
+    """The same synthetic weights with transformers' attention (separate 4-bit q / k /
+    v projections, norms and rotary) and with ``FusedOlmoeAttention``: the last-token
+    logits of a prompt agree to rounding (the projections' split-K sums and the norms'
+    reductions run in another order)."""
+    from conftest import rel_l2
+
+    from robustgemq_b200.inference.generate import synthetic_olmoe
+
+    prompt = torch.randint(0, 50304, (1, 9), generator=torch.Generator().manual_seed(1)).cuda()
+    outs = []
+    for fused in (False, True):
+        model = synthetic_olmoe(num_layers=2, seed=5, max_position_embeddings=64, fused_norms=fused,
+                                fused_attention=fused)
+        with torch.no_grad():
+            outs.append(model(input_ids=prompt).logits[0, -1].float().cpu().numpy())
+        del model
+    assert rel_l2(outs[1], outs[0]) <= 5e-3
