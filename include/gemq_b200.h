@@ -279,11 +279,18 @@ int gemq_rms_norm(const uint16_t* x, const uint16_t* weight, int64_t rows, int32
  * (as gemq_rms_norm), then the rotary embedding of apply_rotary_pos_emb on fp16
  * tensors per head of head_dim values: out = fp16(fp16(x * cos) +
  * fp16(rotate_half(x) * sin)), cos / sin fp16 [rows, head_dim]. q_out, k_out fp16
- * [rows, n]. n % 8 == 0, ld % 8 == 0, qkv and the weights 16-byte aligned. Not part of
- * the reference's MoE path: used by the whole-model decode harness. */
+ * [rows, n]. n % 8 == 0, ld % 8 == 0, qkv and the weights 16-byte aligned.
+ * KV-cache write (k_cache != NULL; one row only): k after the rotation and v (the
+ * third block of qkv) also go to position *cache_len (device int64) of k_cache /
+ * v_cache (fp16 [n / head_dim heads][max_len][head_dim], batch 1), and *cache_len
+ * advances by one: the update of a static KV cache (transformers' StaticLayer) in the
+ * same launch. k_out may then be NULL. A position outside [0, max_len) writes nothing
+ * and records a device error. Not part of the reference's MoE path: used by the
+ * whole-model decode harness. */
 int gemq_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, int32_t n, int32_t head_dim,
                       const uint16_t* q_norm_weight, const uint16_t* k_norm_weight, float eps, const uint16_t* cos,
-                      const uint16_t* sin, uint16_t* q_out, uint16_t* k_out, void* stream);
+                      const uint16_t* sin, uint16_t* q_out, uint16_t* k_out, uint16_t* k_cache, uint16_t* v_cache,
+                      int32_t max_len, int64_t* cache_len, void* stream);
 
 #ifdef __cplusplus
 }

@@ -117,7 +117,8 @@ def _declare(lib: ctypes.CDLL) -> None:
         "gemq_layer_stage_times": (ctypes.c_int, [vp, P(ctypes.c_float)]),
         "gemq_layer_dequant_forms": (ctypes.c_int, [vp, P(ctypes.c_int32)]),
         "gemq_rms_norm": (ctypes.c_int, [vp, vp, i64, i32, ctypes.c_float, vp, vp]),
-        "gemq_qk_norm_rope": (ctypes.c_int, [vp, i64, i64, i32, i32, vp, vp, ctypes.c_float, vp, vp, vp, vp, vp]),
+        "gemq_qk_norm_rope": (ctypes.c_int, [vp, i64, i64, i32, i32, vp, vp, ctypes.c_float, vp, vp, vp, vp,
+                                             vp, vp, i32, vp, vp]),
         "gemq_route": (ctypes.c_int, [vp, i64, i32, vp, i32, i32, i32, i32, u32, vp, vp, vp, vp, sz, vp]),
         "gemq_moe_combine": (ctypes.c_int, [vp, vp, vp, i64, i32, i32, u32, vp, vp, vp]),
         "gemq_dispatch_workspace_size": (sz, [i64, i32, i32]),

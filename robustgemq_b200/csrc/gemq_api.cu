@@ -1050,20 +1050,23 @@ int gemq_rms_norm(const uint16_t* x, const uint16_t* weight, int64_t rows, int32
 
 int gemq_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, int32_t n, int32_t head_dim,
                       const uint16_t* q_norm_weight, const uint16_t* k_norm_weight, float eps, const uint16_t* cos,
-                      const uint16_t* sin, uint16_t* q_out, uint16_t* k_out, void* stream) {
+                      const uint16_t* sin, uint16_t* q_out, uint16_t* k_out, uint16_t* k_cache, uint16_t* v_cache,
+                      int32_t max_len, int64_t* cache_len, void* stream) {
   TraceRange trace("gemq_qk_norm_rope");
   if (rows < 0 || rows > INT32_MAX || n <= 0 || n % 8 != 0 || head_dim <= 0 || head_dim % 2 != 0 ||
       n % head_dim != 0 || ld < 2 * static_cast<int64_t>(n) || ld % 8 != 0)
     return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad rows, n, head_dim or ld");
   if (rows == 0) return GEMQ_OK;
   if (qkv == nullptr || q_norm_weight == nullptr || k_norm_weight == nullptr || cos == nullptr || sin == nullptr ||
-      q_out == nullptr || k_out == nullptr)
+      q_out == nullptr || (k_out == nullptr && k_cache == nullptr))
     return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
+  if (k_cache != nullptr && (v_cache == nullptr || cache_len == nullptr || max_len <= 0 || rows != 1))
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "a cache write takes one row, both caches, max_len and the length");
   if (((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(q_norm_weight) |
         reinterpret_cast<uintptr_t>(k_norm_weight)) & 15u) != 0)
     return fail(GEMQ_ERR_UNSUPPORTED, "qkv and the norm weights must start on a 16-byte boundary");
   GEMQ_CUDA(launch_qk_norm_rope(qkv, ld, rows, n, head_dim, q_norm_weight, k_norm_weight, eps, cos, sin, q_out, k_out,
-                                static_cast<cudaStream_t>(stream)),
+                                k_cache, v_cache, max_len, cache_len, static_cast<cudaStream_t>(stream)),
             "q/k norm + rotary");
   return GEMQ_OK;
 }

@@ -33,6 +33,7 @@ enum DeviceError : uint32_t {
   kDevTimeoutDrain = 7,
   kDevBadExpert = 8,
   kDevBadBits = 9,
+  kDevBadCachePos = 10,  // a KV-cache write past the cache's length (model harness)
 };
 
 // g_device_error: first error recorded (any kind), reported by gemq_get_device_error.

@@ -161,7 +161,8 @@ cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, 
                             cudaStream_t s);
 cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, int n, int hd, const uint16_t* wq,
                                 const uint16_t* wk, float eps, const uint16_t* cos_t, const uint16_t* sin_t,
-                                uint16_t* q_out, uint16_t* k_out, cudaStream_t s);
+                                uint16_t* q_out, uint16_t* k_out, uint16_t* k_cache, uint16_t* v_cache, int max_len,
+                                int64_t* cache_len, cudaStream_t s);
 
 // Decode GEMV family (CUDA cores, deterministic split-K); see kernels_decode.cu.
 enum GemvMode : int { kGemvX = 0, kGemvSwiGLU = 1, kGemvPartF32 = 2, kGemvPartF16 = 3 };

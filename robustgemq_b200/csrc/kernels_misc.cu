@@ -246,11 +246,17 @@ cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, 
 // fp16(rotate_half(x) * sin)), rotate_half(x)[j] = -x[j + hd/2] for j < hd/2, else
 // x[j - hd/2], per head of hd values; cos / sin fp16 [rows, hd]. The normalised rows
 // are staged in shared memory (the rotation pairs values of different threads).
+// With k_cache (one row only): k and v (the third block of qkv) also go to row
+// *cache_len of the caches ([n / hd heads][max_len][hd] fp16), and *cache_len
+// advances by one, as a static cache's update does; a position past max_len writes
+// nothing and records kDevBadCachePos.
 __global__ void __launch_bounds__(kNormThreads) k_qk_norm_rope(const __half* __restrict__ qkv, int64_t ld, int n, int hd,
                                                               const __half* __restrict__ wq, const __half* __restrict__ wk,
                                                               float eps, const __half* __restrict__ cos_t,
                                                               const __half* __restrict__ sin_t, __half* __restrict__ q_out,
-                                                              __half* __restrict__ k_out) {
+                                                              __half* __restrict__ k_out, __half* __restrict__ k_cache,
+                                                              __half* __restrict__ v_cache, int max_len,
+                                                              int64_t* __restrict__ cache_len) {
   extern __shared__ __align__(16) __half s_qk[];  // [2][n]
   const int64_t row = blockIdx.x;
   const __half* src[2] = {qkv + row * ld, qkv + row * ld + n};
@@ -300,27 +306,44 @@ __global__ void __launch_bounds__(kNormThreads) k_qk_norm_rope(const __half* __r
       d4[i] = o;
     }
   }
-  __syncthreads();
+  int64_t pos = -1;
+  if (k_cache != nullptr) {
+    pos = *cache_len;
+    if (pos < 0 || pos >= max_len) {
+      if (threadIdx.x == 0) set_device_error(kDevBadCachePos);
+      pos = -1;
+    }
+  }
+  __syncthreads();  // every thread has read the cache length before it advances
+  if (k_cache != nullptr && threadIdx.x == 0) *cache_len += 1;
   const int half = hd / 2;
   const __half* c = cos_t + row * hd;
   const __half* sn = sin_t + row * hd;
   for (int m = 0; m < 2; ++m) {
     const __half* xs = s_qk + m * n;
-    __half* out = (m == 0 ? q_out : k_out) + row * n;
+    __half* out = (m == 0 ? q_out : k_out);
     for (int i = threadIdx.x; i < n; i += kNormThreads) {
       const int j = i % hd;
       const __half x = xs[i];
       const __half rot = j < half ? __hneg(xs[i + half]) : xs[i - half];
       // the _rn forms keep each product and the sum rounded on its own, as the
       // three fp16 tensor ops are (no contraction into an fp16 fma)
-      out[i] = __hadd_rn(__hmul_rn(x, c[j]), __hmul_rn(rot, sn[j]));
+      const __half r = __hadd_rn(__hmul_rn(x, c[j]), __hmul_rn(rot, sn[j]));
+      if (out != nullptr) out[row * n + i] = r;
+      if (m == 1 && pos >= 0) k_cache[(static_cast<int64_t>(i / hd) * max_len + pos) * hd + j] = r;
     }
+  }
+  if (pos >= 0) {
+    const __half* v = qkv + row * ld + 2 * n;
+    for (int i = threadIdx.x; i < n; i += kNormThreads)
+      v_cache[(static_cast<int64_t>(i / hd) * max_len + pos) * hd + i % hd] = v[i];
   }
 }
 
 cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, int n, int hd, const uint16_t* wq,
                                 const uint16_t* wk, float eps, const uint16_t* cos_t, const uint16_t* sin_t,
-                                uint16_t* q_out, uint16_t* k_out, cudaStream_t s) {
+                                uint16_t* q_out, uint16_t* k_out, uint16_t* k_cache, uint16_t* v_cache, int max_len,
+                                int64_t* cache_len, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
   const size_t smem = 2 * static_cast<size_t>(n) * sizeof(__half);
   if (smem > 48 * 1024) {
@@ -331,7 +354,8 @@ cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, i
   k_qk_norm_rope<<<static_cast<unsigned>(rows), kNormThreads, smem, s>>>(
       reinterpret_cast<const __half*>(qkv), ld, n, hd, reinterpret_cast<const __half*>(wq),
       reinterpret_cast<const __half*>(wk), eps, reinterpret_cast<const __half*>(cos_t),
-      reinterpret_cast<const __half*>(sin_t), reinterpret_cast<__half*>(q_out), reinterpret_cast<__half*>(k_out));
+      reinterpret_cast<const __half*>(sin_t), reinterpret_cast<__half*>(q_out), reinterpret_cast<__half*>(k_out),
+      reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), max_len, cache_len);
   return cudaGetLastError();
 }
 

@@ -83,8 +83,9 @@ def _quant_from_w(W: Tensor, nbits: int, group_size: int) -> QuantLinear:
 class FusedOlmoeAttention(nn.Module):
     """transformers' OlmoeAttention (``modeling_olmoe.OlmoeAttention.forward``) with
     q, k and v from one 4-bit projection (one GEMV) and its prologue, q_norm / k_norm
-    and the rotary embedding, in one launch (``gemq_qk_norm_rope``); the cache update,
-    the attention kernel (the model's ``_attn_implementation``) and o_proj are the
+    and the rotary embedding, in one launch (``gemq_qk_norm_rope``), which for one token
+    also writes k and v into a transformers static cache and advances its length; the
+    attention kernel (the model's ``_attn_implementation``) and o_proj are the
     module's own. ``attn`` is the replaced module, kept for its configuration."""
 
     def __init__(self, attn: nn.Module, qkv_proj: QuantLinear):
@@ -106,6 +107,25 @@ class FusedOlmoeAttention(nn.Module):
         if float(attn.k_norm.variance_epsilon) != self.eps:
             raise ValueError("q_norm and k_norm must share eps")
 
+    def _static_layer(self, cache, rows: int, qkv: Tensor):
+        """The cache layer to write directly: one token, batch 1, an initialised
+        transformers ``StaticLayer`` with contiguous fp16 keys / values and an int64
+        device length; else None (the cache's own update runs)."""
+        if cache is None or rows != 1 or qkv.shape[0] != 1:
+            return None
+        layers = getattr(cache, "layers", None)
+        if layers is None or self.layer_idx >= len(layers):
+            return None
+        layer = layers[self.layer_idx]
+        if type(layer).__name__ != "StaticLayer" or not getattr(layer, "is_initialized", False):
+            return None
+        keys, values, length = layer.keys, layer.values, getattr(layer, "cumulative_length", None)
+        if not (isinstance(length, Tensor) and length.dtype == torch.int64 and length.is_cuda and length.numel() == 1):
+            return None
+        ok = all(t.dtype == torch.float16 and t.is_contiguous() and t.dim() == 4 and t.shape[0] == 1 and
+                 t.shape[-1] == self.head_dim for t in (keys, values))
+        return layer if ok else None
+
     def forward(self, hidden_states: Tensor, position_embeddings, attention_mask, past_key_values=None, **kwargs):
         from transformers.models.olmoe.modeling_olmoe import ALL_ATTENTION_FUNCTIONS, eager_attention_forward
 
@@ -120,16 +140,28 @@ class FusedOlmoeAttention(nn.Module):
         if cos.numel() != rows * self.head_dim:
             raise ValueError("rotary tables must have one row per token")
         q = torch.empty((*input_shape, n), dtype=torch.float16, device=qkv.device)
-        k = torch.empty_like(q)
-        _lib.check(_lib.load().gemq_qk_norm_rope(
-            _lib.ptr(qkv), qkv.stride(-2) if qkv.dim() > 1 else 3 * n, rows, n, self.head_dim,
-            _lib.ptr(self.q_norm_weight), _lib.ptr(self.k_norm_weight), self.eps, _lib.ptr(cos), _lib.ptr(sin),
-            _lib.ptr(q), _lib.ptr(k), _lib.stream_ptr(qkv.device)))
+        ld = qkv.stride(-2) if qkv.dim() > 1 else 3 * n
+        layer = self._static_layer(past_key_values, rows, qkv)
+        if layer is not None:
+            # one token: k and v straight into the static cache at its device-side
+            # length, which the kernel advances (the cache's own update, in this launch)
+            _lib.check(_lib.load().gemq_qk_norm_rope(
+                _lib.ptr(qkv), ld, rows, n, self.head_dim, _lib.ptr(self.q_norm_weight), _lib.ptr(self.k_norm_weight),
+                self.eps, _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(q), None, _lib.ptr(layer.keys),
+                _lib.ptr(layer.values), layer.keys.shape[2], _lib.ptr(layer.cumulative_length),
+                _lib.stream_ptr(qkv.device)))
+            key_states, value_states = layer.keys, layer.values
+        else:
+            k = torch.empty_like(q)
+            _lib.check(_lib.load().gemq_qk_norm_rope(
+                _lib.ptr(qkv), ld, rows, n, self.head_dim, _lib.ptr(self.q_norm_weight), _lib.ptr(self.k_norm_weight),
+                self.eps, _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(q), _lib.ptr(k), None, None, 0, None,
+                _lib.stream_ptr(qkv.device)))
+            key_states = k.view(hidden_shape).transpose(1, 2)
+            value_states = qkv[..., 2 * n:].view(hidden_shape).transpose(1, 2)
+            if past_key_values is not None:
+                key_states, value_states = past_key_values.update(key_states, value_states, self.layer_idx)
         query_states = q.view(hidden_shape).transpose(1, 2)
-        key_states = k.view(hidden_shape).transpose(1, 2)
-        value_states = qkv[..., 2 * n:].view(hidden_shape).transpose(1, 2)
-        if past_key_values is not None:
-            key_states, value_states = past_key_values.update(key_states, value_states, self.layer_idx)
         attention_interface = ALL_ATTENTION_FUNCTIONS.get_interface(self.config._attn_implementation,
                                                                     eager_attention_forward)
         attn_output, attn_weights = attention_interface(

@@ -96,7 +96,8 @@ def test_fused_qk_norm_rope_matches_transformers(cuda_device, rows):
     cos16, sin16 = cos.half().contiguous(), sin.half().contiguous()
     _lib.check(_lib.load().gemq_qk_norm_rope(_lib.ptr(qkv), 3 * D, rows, D, hd, _lib.ptr(qn.weight.data),
                                              _lib.ptr(kn.weight.data), qn.variance_epsilon, _lib.ptr(cos16),
-                                             _lib.ptr(sin16), _lib.ptr(q), _lib.ptr(k), _lib.stream_ptr(q.device)))
+                                             _lib.ptr(sin16), _lib.ptr(q), _lib.ptr(k), None, None, 0, None,
+                                             _lib.stream_ptr(q.device)))
     torch.cuda.synchronize()
     for got, ref in ((q, q_ref), (k, k_ref)):
         ref = ref.transpose(1, 2).reshape(rows, D).float()
@@ -108,19 +109,33 @@ def test_fused_qk_norm_rope_matches_transformers(cuda_device, rows):
 
 def test_fused_attention_model_matches_unfused(cuda_device):
     """The same synthetic weights with transformers' attention (separate 4-bit q / k /
-    v projections, norms and rotary) and with ``FusedOlmoeAttention``: the last-token
-    logits of a prompt agree to rounding (the projections' split-K sums and the norms'
-    reductions run in another order)."""
+    v projections, norms, rotary and static-cache update) and with
+    ``FusedOlmoeAttention``: the last-token logits of a prompt, and of one decode step
+    after it (the fused kernel writing the cache), agree to rounding (the projections'
+    split-K sums and the norms' reductions run in another order)."""
     from conftest import rel_l2
 
     from robustgemq_b200.inference.generate import synthetic_olmoe
 
+    from transformers import StaticCache
+
     prompt = torch.randint(0, 50304, (1, 9), generator=torch.Generator().manual_seed(1)).cuda()
-    outs = []
+    nxt = torch.tensor([[123]], device="cuda")
+    outs, steps = [], []
     for fused in (False, True):
         model = synthetic_olmoe(num_layers=2, seed=5, max_position_embeddings=64, fused_norms=fused,
                                 fused_attention=fused)
         with torch.no_grad():
             outs.append(model(input_ids=prompt).logits[0, -1].float().cpu().numpy())
-        del model
+            # prefill into a static cache (its own update), then one token, whose k / v
+            # the fused kernel writes into the cache itself
+            cache = StaticCache(config=model.config, max_cache_len=32)
+            model(input_ids=prompt, past_key_values=cache, cache_position=torch.arange(9, device="cuda"),
+                  use_cache=True)
+            step = model(input_ids=nxt, past_key_values=cache, cache_position=torch.tensor([9], device="cuda"),
+                         use_cache=True)
+            steps.append(step.logits[0, -1].float().cpu().numpy())
+            assert int(cache.layers[0].cumulative_length.item()) == 10
+        del model, cache
     assert rel_l2(outs[1], outs[0]) <= 5e-3
+    assert rel_l2(steps[1], steps[0]) <= 5e-3
