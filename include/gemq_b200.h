@@ -292,6 +292,17 @@ int gemq_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, int32_t n, 
                       const uint16_t* sin, uint16_t* q_out, uint16_t* k_out, uint16_t* k_cache, uint16_t* v_cache,
                       int32_t max_len, int64_t* cache_len, void* stream);
 
+/* Attention of one query token of one sequence over a static KV cache:
+ * out[h] = softmax(scale * q[h] K[h][0:L]^T) V[h][0:L] with L = *cache_len (device
+ * int64, clamped to [0, max_len]), i.e. the causal mask of a one-token decode step,
+ * which hides exactly the cache positions not yet written. q, out fp16 [heads,
+ * head_dim]; k_cache, v_cache fp16 [heads][max_len][head_dim], 16-byte aligned;
+ * head_dim % 8 == 0, at most 256; fp32 scores, softmax and sums, one rounding to fp16. Not part of the reference's MoE path: used by the
+ * whole-model decode harness in place of the attention library call. */
+int gemq_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int32_t heads,
+                          int32_t max_len, int32_t head_dim, const int64_t* cache_len, float scale, uint16_t* out,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

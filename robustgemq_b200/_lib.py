@@ -50,7 +50,7 @@ EXPORTED = [
     "gemq_moe_forward", "gemq_layer_stage_times", "gemq_route", "gemq_moe_combine",
     "gemq_dispatch_workspace_size", "gemq_moe_dispatch", "gemq_moe_experts_workspace_size", "gemq_moe_experts",
     "gemq_moe_experts_row_order", "gemq_layer_dequant_forms", "gemq_rms_norm",
-    "gemq_qk_norm_rope",
+    "gemq_qk_norm_rope", "gemq_decode_attention",
 ]
 
 
@@ -119,6 +119,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         "gemq_rms_norm": (ctypes.c_int, [vp, vp, i64, i32, ctypes.c_float, vp, vp]),
         "gemq_qk_norm_rope": (ctypes.c_int, [vp, i64, i64, i32, i32, vp, vp, ctypes.c_float, vp, vp, vp, vp,
                                              vp, vp, i32, vp, vp]),
+        "gemq_decode_attention": (ctypes.c_int, [vp, vp, vp, i32, i32, i32, vp, ctypes.c_float, vp, vp]),
         "gemq_route": (ctypes.c_int, [vp, i64, i32, vp, i32, i32, i32, i32, u32, vp, vp, vp, vp, sz, vp]),
         "gemq_moe_combine": (ctypes.c_int, [vp, vp, vp, i64, i32, i32, u32, vp, vp, vp]),
         "gemq_dispatch_workspace_size": (sz, [i64, i32, i32]),

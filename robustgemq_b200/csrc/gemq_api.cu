@@ -1071,6 +1071,22 @@ int gemq_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, int32_t n, 
   return GEMQ_OK;
 }
 
+int gemq_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int32_t heads,
+                          int32_t max_len, int32_t head_dim, const int64_t* cache_len, float scale, uint16_t* out,
+                          void* stream) {
+  TraceRange trace("gemq_decode_attention");
+  if (heads <= 0 || max_len <= 0 || head_dim <= 0 || head_dim > 256 || head_dim % 8 != 0 || max_len > 1 << 16)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "bad heads, max_len or head_dim (head_dim % 8 == 0, <= 256)");
+  if (((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u) != 0)
+    return fail(GEMQ_ERR_UNSUPPORTED, "k_cache and v_cache must start on a 16-byte boundary");
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || cache_len == nullptr || out == nullptr)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "null pointer");
+  GEMQ_CUDA(launch_decode_attention(q, k_cache, v_cache, heads, max_len, head_dim, cache_len, scale, out,
+                                    static_cast<cudaStream_t>(stream)),
+            "decode attention");
+  return GEMQ_OK;
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------------ allocation-free group GEMM

@@ -163,6 +163,9 @@ cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, i
                                 const uint16_t* wk, float eps, const uint16_t* cos_t, const uint16_t* sin_t,
                                 uint16_t* q_out, uint16_t* k_out, uint16_t* k_cache, uint16_t* v_cache, int max_len,
                                 int64_t* cache_len, cudaStream_t s);
+cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int heads,
+                                    int max_len, int hd, const int64_t* cache_len, float scale, uint16_t* out,
+                                    cudaStream_t s);
 
 // Decode GEMV family (CUDA cores, deterministic split-K); see kernels_decode.cu.
 enum GemvMode : int { kGemvX = 0, kGemvSwiGLU = 1, kGemvPartF32 = 2, kGemvPartF16 = 3 };

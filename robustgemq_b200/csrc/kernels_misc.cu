@@ -5,6 +5,7 @@
 //   dequant       gemq/triton_kernels/utils.py:192-212
 #include <cuda_fp16.h>
 
+#include <cmath>
 #include <mutex>
 
 #include "gemq_common.cuh"
@@ -356,6 +357,109 @@ cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t ld, int64_t rows, i
       reinterpret_cast<const __half*>(wk), eps, reinterpret_cast<const __half*>(cos_t),
       reinterpret_cast<const __half*>(sin_t), reinterpret_cast<__half*>(q_out), reinterpret_cast<__half*>(k_out),
       reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), max_len, cache_len);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ one-token attention (model harness)
+// softmax(scale * q K^T) V for one query token of one sequence against the first L =
+// *cache_len positions of a static KV cache ([heads][max_len][hd] fp16): the causal
+// mask of a one-token decode step, which hides exactly the positions not yet written.
+// One CTA per head: each thread takes whole keys (its dot product from 16-byte loads
+// of the key, q staged in shared memory as fp32), the scores stay in shared memory,
+// the block reduces their maximum and the sum of exp(score - max), and thread d sums
+// p_j * v_j[d] in fp32 (loads of eight positions in flight) before one rounding to
+// fp16. head_dim % 8 == 0, at most kAttnMaxHd.
+constexpr int kAttnThreads = 128;
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* s_red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, w) : v + w;
+  }
+  const int warp = threadIdx.x >> 5;
+  __syncthreads();  // s_red may still be read by the previous reduction
+  if ((threadIdx.x & 31) == 0) s_red[warp] = v;
+  __syncthreads();
+  float r = s_red[0];
+  for (int i = 1; i < kAttnThreads / 32; ++i) r = is_max ? fmaxf(r, s_red[i]) : r + s_red[i];
+  return r;
+}
+
+constexpr int kAttnMaxHd = 256;
+
+__global__ void __launch_bounds__(kAttnThreads) k_decode_attention(const __half* __restrict__ q,
+                                                                  const __half* __restrict__ kc,
+                                                                  const __half* __restrict__ vc, int max_len, int hd,
+                                                                  const int64_t* __restrict__ cache_len, float scale,
+                                                                  __half* __restrict__ out) {
+  extern __shared__ float s_sc[];  // [max_len]
+  __shared__ float s_red[kAttnThreads / 32];
+  __shared__ float s_q[kAttnMaxHd];
+  const int h = blockIdx.x;
+  const int64_t len = *cache_len;
+  const int L = static_cast<int>(len < 0 ? 0 : (len > max_len ? max_len : len));
+  const __half* qh = q + static_cast<int64_t>(h) * hd;
+  const __half* kh = kc + static_cast<int64_t>(h) * max_len * hd;
+  const __half* vh = vc + static_cast<int64_t>(h) * max_len * hd;
+  for (int c = threadIdx.x; c < hd; c += kAttnThreads) s_q[c] = __half2float(qh[c]);
+  __syncthreads();
+  const int hd8 = hd / 8;
+  for (int j = threadIdx.x; j < L; j += kAttnThreads) {
+    const uint4* k4 = reinterpret_cast<const uint4*>(kh + static_cast<int64_t>(j) * hd);
+    float d = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < hd8; ++c) {
+      const uint4 kv = k4[c];
+      const __half2* k2 = reinterpret_cast<const __half2*>(&kv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(k2[e]);
+        d = fmaf(s_q[8 * c + 2 * e], f.x, d);
+        d = fmaf(s_q[8 * c + 2 * e + 1], f.y, d);
+      }
+    }
+    s_sc[j] = d * scale;
+  }
+  __syncthreads();
+  float m = -INFINITY;
+  for (int j = threadIdx.x; j < L; j += kAttnThreads) m = fmaxf(m, s_sc[j]);
+  m = block_reduce(m, true, s_red);
+  float sum = 0.f;
+  for (int j = threadIdx.x; j < L; j += kAttnThreads) {
+    const float p = expf(s_sc[j] - m);
+    s_sc[j] = p;
+    sum += p;
+  }
+  sum = block_reduce(sum, false, s_red);  // its barriers also publish the p_j
+  const float inv = sum > 0.f ? 1.f / sum : 0.f;
+  for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
+    float acc = 0.f;
+    int j = 0;
+    for (; j + 8 <= L; j += 8) {
+      __half v8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v8[u] = vh[static_cast<int64_t>(j + u) * hd + d];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = fmaf(s_sc[j + u], __half2float(v8[u]), acc);
+    }
+    for (; j < L; ++j) acc = fmaf(s_sc[j], __half2float(vh[static_cast<int64_t>(j) * hd + d]), acc);
+    out[static_cast<int64_t>(h) * hd + d] = __float2half_rn(acc * inv);
+  }
+}
+
+cudaError_t launch_decode_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int heads,
+                                    int max_len, int hd, const int64_t* cache_len, float scale, uint16_t* out,
+                                    cudaStream_t s) {
+  const size_t smem = static_cast<size_t>(max_len) * sizeof(float);
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(k_decode_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  k_decode_attention<<<static_cast<unsigned>(heads), kAttnThreads, smem, s>>>(
+      reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k_cache),
+      reinterpret_cast<const __half*>(v_cache), max_len, hd, cache_len, scale, reinterpret_cast<__half*>(out));
   return cudaGetLastError();
 }
 

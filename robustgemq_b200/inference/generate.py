@@ -83,10 +83,12 @@ def _quant_from_w(W: Tensor, nbits: int, group_size: int) -> QuantLinear:
 class FusedOlmoeAttention(nn.Module):
     """transformers' OlmoeAttention (``modeling_olmoe.OlmoeAttention.forward``) with
     q, k and v from one 4-bit projection (one GEMV) and its prologue, q_norm / k_norm
-    and the rotary embedding, in one launch (``gemq_qk_norm_rope``), which for one token
-    also writes k and v into a transformers static cache and advances its length; the
-    attention kernel (the model's ``_attn_implementation``) and o_proj are the
-    module's own. ``attn`` is the replaced module, kept for its configuration."""
+    and the rotary embedding, in one launch (``gemq_qk_norm_rope``). For one token of
+    one sequence it also writes k and v into a transformers static cache, advancing
+    its length, and the attention over the cache's written positions runs in one more
+    launch (``gemq_decode_attention``; the causal mask of such a step hides exactly the
+    unwritten positions, so no padding mask is taken). Otherwise the cache's update and
+    the model's ``_attn_implementation`` run. o_proj is the module's own. ``attn`` is the replaced module, kept for its configuration."""
 
     def __init__(self, attn: nn.Module, qkv_proj: QuantLinear):
         super().__init__()
@@ -150,6 +152,15 @@ class FusedOlmoeAttention(nn.Module):
                 self.eps, _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(q), None, _lib.ptr(layer.keys),
                 _lib.ptr(layer.values), layer.keys.shape[2], _lib.ptr(layer.cumulative_length),
                 _lib.stream_ptr(qkv.device)))
+            if self.num_key_value_groups == 1:
+                # one query token over the cache's written positions (the causal mask
+                # of a one-token step of one sequence), in one launch
+                attn = torch.empty_like(q)
+                _lib.check(_lib.load().gemq_decode_attention(
+                    _lib.ptr(q), _lib.ptr(layer.keys), _lib.ptr(layer.values), n // self.head_dim,
+                    layer.keys.shape[2], self.head_dim, _lib.ptr(layer.cumulative_length), float(self.scaling),
+                    _lib.ptr(attn), _lib.stream_ptr(qkv.device)))
+                return self.o_proj(attn), None
             key_states, value_states = layer.keys, layer.values
         else:
             k = torch.empty_like(q)

@@ -139,3 +139,32 @@ def test_fused_attention_model_matches_unfused(cuda_device):
         del model, cache
     assert rel_l2(outs[1], outs[0]) <= 5e-3
     assert rel_l2(steps[1], steps[0]) <= 5e-3
+
+
+@pytest.mark.parametrize("length", [1, 9, 73])
+def test_decode_attention_matches_fp32_reference(cuda_device, length):
+    """``gemq_decode_attention`` against softmax(scale q K^T) V in fp32 over the first
+    ``length`` cache positions; the positions after them hold garbage that must not be
+    read. One fp16 rounding of an fp32 result: within 2e-3 relative."""
+    from conftest import rel_l2
+
+    from robustgemq_b200 import _lib
+
+    H, hd, max_len = 16, 128, 73
+    g = torch.Generator(device="cuda").manual_seed(length)
+    q = torch.randn((H, hd), generator=g, device="cuda").half()
+    kc = torch.randn((H, max_len, hd), generator=g, device="cuda").half()
+    vc = torch.randn((H, max_len, hd), generator=g, device="cuda").half()
+    kc[:, length:] = 1e4  # unwritten positions
+    vc[:, length:] = float("nan")
+    cache_len = torch.tensor([length], dtype=torch.int64, device="cuda")
+    out = torch.empty_like(q)
+    scale = hd ** -0.5
+    _lib.check(_lib.load().gemq_decode_attention(_lib.ptr(q), _lib.ptr(kc), _lib.ptr(vc), H, max_len, hd,
+                                                 _lib.ptr(cache_len), scale, _lib.ptr(out), _lib.stream_ptr(q.device)))
+    k, v = kc[:, :length].float(), vc[:, :length].float()
+    p = torch.softmax(torch.einsum("hd,hjd->hj", q.float(), k) * scale, dim=-1)
+    ref = torch.einsum("hj,hjd->hd", p, v)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    assert rel_l2(out.float().cpu().numpy(), ref.cpu().numpy()) <= 2e-3
