@@ -182,6 +182,29 @@ int gemq_layer_destroy(gemq_layer_t* layer);
 
 size_t gemq_moe_workspace_size(const gemq_layer_t* layer, int64_t num_tokens, uint32_t flags);
 
+/* Routing options beyond the block constructor's: DeepSeek-V2's group-limited greedy
+ * selection and routed_scaling_factor, which the reference's fused block rejects
+ * (gemq/inference/moe_block.py:18-66, check_deepseek_routing_supported and
+ * check_deepseek_gate_matches). Selection as transformers'
+ * DeepseekV2Moe.route_tokens_to_experts computes it: softmax in fp32; with
+ * n_group > 1 the experts form n_group equal groups of consecutive ids, each scored
+ * by its largest probability, the topk_group best groups are kept (lower group id on
+ * ties) and every other expert's probability reads 0.0; then the top-k. Weights:
+ * w / sum(w) when norm_topk_prob, else w * scale, rounded to fp16.
+ * Limits: 1 <= n_group <= 32, num_experts % n_group == 0, 1 <= topk_group <= n_group,
+ * topk_group * (num_experts / n_group) >= top_k, scale finite. */
+typedef struct gemq_routing {
+  int32_t norm_topk_prob;
+  int32_t n_group;     /* 1 = plain greedy */
+  int32_t topk_group;
+  float scale;         /* routed_scaling_factor (1.0 = none) */
+} gemq_routing_t;
+
+/* Replaces the layer's routing options (default: the descriptor's norm_topk_prob,
+ * n_group = topk_group = 1, scale = 1.0). Not to be called while a forward of the
+ * layer is being enqueued on another thread. */
+int gemq_layer_set_routing(gemq_layer_t* layer, const gemq_routing_t* routing /* host */);
+
 /* Router of forward_n_tokens / forward_one_token (moe_block.py:790-797, 828-833,
  * 549-556, 280-283): logits (fp16, or fp32 for GEMQ_ROUTER_FP32) [T, E],
  * topk_idx int32 [T, k], topk_w fp16 [T, k]. Ties go to the lower expert id. */
@@ -197,6 +220,12 @@ int gemq_route(const uint16_t* x, int64_t num_tokens, int32_t hidden, const uint
                int32_t num_experts, int32_t top_k, int32_t router, int32_t norm_topk_prob, uint32_t flags,
                void* logits, int32_t* topk_idx, uint16_t* topk_w, void* workspace, size_t workspace_bytes,
                void* stream);
+/* gemq_route with the routing options of gemq_routing_t (NULL = plain greedy without
+ * renormalisation). */
+int gemq_route_ex(const uint16_t* x, int64_t num_tokens, int32_t hidden, const uint16_t* gate_weight,
+                  int32_t num_experts, int32_t top_k, int32_t router, const gemq_routing_t* routing /* host */,
+                  uint32_t flags, void* logits, int32_t* topk_idx, uint16_t* topk_w, void* workspace,
+                  size_t workspace_bytes, void* stream);
 
 /* Combine of forward_n_tokens (moe_block.py:799-812) on already computed expert
  * outputs: out[t] = sum over the token's k slots of y[slot_row[t*k + j]], in

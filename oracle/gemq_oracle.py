@@ -255,9 +255,24 @@ class Routing:
     topk_w: np.ndarray      # [T, k] fp16
 
 
+def group_limit(p: np.ndarray, n_group: int, topk_group: int) -> np.ndarray:
+    """DeepSeek-V2's group-limited greedy mask (transformers
+    ``DeepseekV2Moe.route_tokens_to_experts``, ``topk_method == "group_limited_greedy"``):
+    each of the ``n_group`` groups of consecutive experts is scored by its largest
+    probability, the ``topk_group`` best groups are kept (lower group id first on
+    ties), and every other expert's probability is replaced by 0.0 (``masked_fill``)."""
+    T, E = p.shape
+    gs = p.reshape(T, n_group, E // n_group).max(axis=-1)
+    _, keep = topk_desc(gs, topk_group)
+    mask = np.zeros((T, n_group), dtype=bool)
+    np.put_along_axis(mask, keep, True, axis=-1)
+    return np.where(np.repeat(mask, E // n_group, axis=-1), p, np.zeros_like(p))
+
+
 def route(x: np.ndarray, gate_w: Optional[np.ndarray], top_k: int, norm_topk_prob: bool,
           router_fp32: bool = False, logits: Optional[np.ndarray] = None,
-          softmax_fp16: bool = False) -> Routing:
+          softmax_fp16: bool = False, n_group: int = 1, topk_group: int = 1,
+          scale: float = 1.0) -> Routing:
     """Router of forward_n_tokens / forward_one_token.
 
     fp16 logits ``x @ Wg^T`` (moe_block.py:790,828); DeepSeek forms them in fp32
@@ -266,6 +281,11 @@ def route(x: np.ndarray, gate_w: Optional[np.ndarray], top_k: int, norm_topk_pro
     ``softmax_fp16`` restates Mixtral's one-token router, whose softmax, top-k and
     renormalisation run on fp16 tensors (moe_block.py:280-283).
     ``logits`` may be given directly (the skewed-load benchmark configs).
+    Beyond the reference's fused block, which rejects them (moe_block.py:18-66):
+    ``n_group > 1`` restricts the top-k to the best groups (``group_limit``), and
+    without renormalisation the weights are multiplied by ``scale`` in fp32
+    (``routed_scaling_factor``, as the HF and official DeepSeek gates do) before the
+    fp16 cast.
     """
     if logits is None:
         if router_fp32:
@@ -280,9 +300,13 @@ def route(x: np.ndarray, gate_w: Optional[np.ndarray], top_k: int, norm_topk_pro
             w = (w.astype(F64) / ssum.astype(F64)).astype(F16)
         return Routing(logits, idx.astype(np.int64), w.astype(F16))
     p = softmax_f32(logits.astype(F32))
+    if n_group > 1:
+        p = group_limit(p, n_group, topk_group)
     w, idx = topk_desc(p, top_k)
     if norm_topk_prob:
         w = (w.astype(F64) / w.astype(F64).sum(axis=-1, keepdims=True)).astype(F32)
+    elif scale != 1.0:
+        w = (w.astype(F32) * F32(scale)).astype(F32)
     return Routing(logits, idx.astype(np.int64), w.astype(F16))
 
 
@@ -301,6 +325,9 @@ class BlockWeights:
     shared_w1: Optional[PackedProj] = None   # DeepSeek shared experts (moe_block.py:477-489)
     shared_w3: Optional[PackedProj] = None
     shared_w2: Optional[PackedProj] = None
+    n_group: int = 1              # DeepSeek-V2 group-limited greedy (1 = greedy)
+    topk_group: int = 1
+    route_scale: float = 1.0      # routed_scaling_factor when not renormalising
     dequant_cache: dict = field(default_factory=dict)
 
     def deq(self, name: str, e: int, fma: str = "single") -> np.ndarray:
@@ -341,7 +368,8 @@ def moe_forward_n_tokens(blk: BlockWeights, x: np.ndarray, routing: Optional[Rou
     x = np.asarray(x, dtype=F16)
     T, D = x.shape
     if routing is None:
-        routing = route(x, blk.gate_w, blk.top_k, blk.norm_topk_prob, blk.router_fp32)
+        routing = route(x, blk.gate_w, blk.top_k, blk.norm_topk_prob, blk.router_fp32, n_group=blk.n_group,
+                        topk_group=blk.topk_group, scale=blk.route_scale)
     out = np.zeros((T, D), dtype=F16)
     idx = routing.topk_idx
     for e in np.unique(idx):
@@ -366,7 +394,8 @@ def moe_forward_one_token(blk: BlockWeights, x: np.ndarray, routing: Optional[Ro
     x = np.asarray(x, dtype=F16).reshape(1, -1)
     if routing is None:
         routing = route(x, blk.gate_w, blk.top_k, blk.norm_topk_prob or mixtral, blk.router_fp32,
-                        softmax_fp16=mixtral)
+                        softmax_fp16=mixtral, n_group=blk.n_group, topk_group=blk.topk_group,
+                        scale=blk.route_scale)
     idx = [int(e) for e in routing.topk_idx[0]]
     x1, x3 = fused_up_proj(x, idx, blk.w1, blk.w3, fma)
     x2 = fused_down_proj(x1, x3, idx, blk.w2, fma).reshape(len(idx), -1)

@@ -50,7 +50,7 @@ EXPORTED = [
     "gemq_moe_forward", "gemq_layer_stage_times", "gemq_route", "gemq_moe_combine",
     "gemq_dispatch_workspace_size", "gemq_moe_dispatch", "gemq_moe_experts_workspace_size", "gemq_moe_experts",
     "gemq_moe_experts_row_order", "gemq_layer_dequant_forms", "gemq_rms_norm",
-    "gemq_qk_norm_rope", "gemq_decode_attention",
+    "gemq_qk_norm_rope", "gemq_decode_attention", "gemq_layer_set_routing", "gemq_route_ex",
 ]
 
 
@@ -84,6 +84,15 @@ class LayerDescT(ctypes.Structure):
         ("w1", ProjT), ("w3", ProjT), ("w2", ProjT),
         ("has_shared", ctypes.c_int32),
         ("shared_w1", ProjT), ("shared_w3", ProjT), ("shared_w2", ProjT),
+    ]
+
+
+class RoutingT(ctypes.Structure):
+    """gemq_routing_t: renormalisation, group-limited greedy and the routing scale."""
+
+    _fields_ = [
+        ("norm_topk_prob", ctypes.c_int32), ("n_group", ctypes.c_int32), ("topk_group", ctypes.c_int32),
+        ("scale", ctypes.c_float),
     ]
 
 
@@ -121,6 +130,9 @@ def _declare(lib: ctypes.CDLL) -> None:
                                              vp, vp, i32, vp, vp]),
         "gemq_decode_attention": (ctypes.c_int, [vp, vp, vp, i32, i32, i32, vp, ctypes.c_float, vp, vp]),
         "gemq_route": (ctypes.c_int, [vp, i64, i32, vp, i32, i32, i32, i32, u32, vp, vp, vp, vp, sz, vp]),
+        "gemq_route_ex": (ctypes.c_int, [vp, i64, i32, vp, i32, i32, i32, P(RoutingT), u32, vp, vp, vp, vp, sz,
+                                         vp]),
+        "gemq_layer_set_routing": (ctypes.c_int, [vp, P(RoutingT)]),
         "gemq_moe_combine": (ctypes.c_int, [vp, vp, vp, i64, i32, i32, u32, vp, vp, vp]),
         "gemq_dispatch_workspace_size": (sz, [i64, i32, i32]),
         "gemq_moe_dispatch": (ctypes.c_int, [vp, vp, vp, i64, i32, i32, i32, vp, vp, vp, vp, vp, vp, sz, vp]),

@@ -3,6 +3,7 @@
 #include <cuda_fp16.h>
 
 #include <cstdio>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -160,6 +161,7 @@ using namespace gemq;
 
 struct gemq_layer {
   gemq_layer_desc_t d;
+  gemq_routing_t ro;  // norm_topk_prob (from d unless replaced), group-limited greedy, scale
   ProjDev w1, w3, w2, sw1, sw3, sw2;
   ProjDev w3_as_w1;  // w3 read with w1's nbits/strides (one-token path, fused_dequant_bmm.py:98)
   int num_sms;
@@ -447,6 +449,7 @@ int gemq_layer_create(const gemq_layer_desc_t* desc, gemq_layer_t** out) {
   }
   gemq_layer_t* L = new gemq_layer();
   L->d = d;
+  L->ro = gemq_routing_t{d.norm_topk_prob, 1, 1, 1.0f};
   L->w1 = to_dev(d.w1);
   L->w3 = to_dev(d.w3);
   L->w2 = to_dev(d.w2);
@@ -546,12 +549,24 @@ FwdBufs carve(const gemq_layer_t* L, int64_t T, uint32_t flags, void* base, cons
 }
 
 // logits -> top-k (or nothing when routing is given)
-int run_router(const gemq_layer_desc_t& d, int num_sms, const uint16_t* x, int64_t T, void* logits_out,
-               bool logits_given, int32_t* idx, uint16_t* w, uint32_t flags, Seg* one_seg, int32_t* one_tp,
-               cudaStream_t s, StageTimer* tm = nullptr) {
+// Checks routing options against the layer shape (limits of gemq_routing_t).
+int check_routing(const gemq_routing_t& r, int E, int k) {
+  if (r.n_group < 1 || r.n_group > 32 || E % r.n_group != 0)
+    return fail(GEMQ_ERR_UNSUPPORTED, "n_group must be in [1, 32] and divide num_experts");
+  if (r.topk_group < 1 || r.topk_group > r.n_group)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "topk_group must be in [1, n_group]");
+  if (static_cast<int64_t>(r.topk_group) * (E / r.n_group) < k)
+    return fail(GEMQ_ERR_INVALID_ARGUMENT, "the kept groups hold fewer than top_k experts");
+  if (!std::isfinite(r.scale)) return fail(GEMQ_ERR_INVALID_ARGUMENT, "routing scale must be finite");
+  return GEMQ_OK;
+}
+
+int run_router(const gemq_layer_desc_t& d, const gemq_routing_t& ro, int num_sms, const uint16_t* x, int64_t T,
+               void* logits_out, bool logits_given, int32_t* idx, uint16_t* w, uint32_t flags, Seg* one_seg,
+               int32_t* one_tp, cudaStream_t s, StageTimer* tm = nullptr) {
   if (tm) tm->begin(GEMQ_STAGE_ROUTE);
   const bool fp32_logits = logits_given || d.router == GEMQ_ROUTER_FP32;
-  const bool norm = d.norm_topk_prob != 0;
+  const bool norm = ro.norm_topk_prob != 0;
   const bool fp16_softmax = (flags & GEMQ_FWD_FP16_SOFTMAX) != 0;
   if (!logits_given && T <= kSmallRouteTokens) {
     // small batches: gate dot products spread over (expert group x token group) CTAs
@@ -587,7 +602,9 @@ int run_router(const gemq_layer_desc_t& d, int num_sms, const uint16_t* x, int64
       GEMQ_CUDA(launch_simt_gemm(a, s), "router gemm");
     }
   }
-  GEMQ_CUDA(launch_topk(logits_out, fp32_logits, T, d.num_experts, d.top_k, norm, fp16_softmax, idx, w, s), "topk");
+  GEMQ_CUDA(launch_topk(logits_out, fp32_logits, T, d.num_experts, d.top_k, norm, fp16_softmax, ro.n_group,
+                        ro.topk_group, ro.scale, idx, w, s),
+            "topk");
   if (tm) tm->end(GEMQ_STAGE_ROUTE);
   return GEMQ_OK;
 }
@@ -758,9 +775,9 @@ int gemq_moe_route(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, v
   Seg* seg = c.take<Seg>(1);
   int32_t* tp = c.take<int32_t>(2);
   if (workspace == nullptr || workspace_bytes < c.off + 256) return fail(GEMQ_ERR_WORKSPACE, "workspace too small");
-  return run_router(layer->d, layer->num_sms, x, num_tokens, logits, (flags & GEMQ_FWD_GIVEN_LOGITS) != 0, topk_idx,
-                    topk_w, flags, seg,
-                    tp, static_cast<cudaStream_t>(stream));
+  return run_router(layer->d, layer->ro, layer->num_sms, x, num_tokens, logits,
+                    (flags & GEMQ_FWD_GIVEN_LOGITS) != 0, topk_idx, topk_w, flags, seg, tp,
+                    static_cast<cudaStream_t>(stream));
 }
 
 int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens, uint16_t* out, void* router_logits,
@@ -792,9 +809,8 @@ int gemq_moe_forward(gemq_layer_t* layer, const uint16_t* x, int64_t num_tokens,
   const uint16_t* w = topk_w;
   if (!given_routing) {
     void* logits = (router_logits != nullptr) ? router_logits : b.logits;
-    if (int rc = run_router(layer->d, layer->num_sms, x, num_tokens, logits, given_logits, b.topk_idx, b.topk_w,
-                            flags, b.one_seg,
-                            b.one_tp, s, &tm))
+    if (int rc = run_router(layer->d, layer->ro, layer->num_sms, x, num_tokens, logits, given_logits, b.topk_idx,
+                            b.topk_w, flags, b.one_seg, b.one_tp, s, &tm))
       return rc;
     idx = b.topk_idx;
     w = b.topk_w;
@@ -807,6 +823,15 @@ int gemq_route(const uint16_t* x, int64_t num_tokens, int32_t hidden, const uint
                int32_t num_experts, int32_t top_k, int32_t router, int32_t norm_topk_prob, uint32_t flags,
                void* logits, int32_t* topk_idx, uint16_t* topk_w, void* workspace, size_t workspace_bytes,
                void* stream) {
+  const gemq_routing_t r{norm_topk_prob, 1, 1, 1.0f};
+  return gemq_route_ex(x, num_tokens, hidden, gate_weight, num_experts, top_k, router, &r, flags, logits, topk_idx,
+                       topk_w, workspace, workspace_bytes, stream);
+}
+
+int gemq_route_ex(const uint16_t* x, int64_t num_tokens, int32_t hidden, const uint16_t* gate_weight,
+                  int32_t num_experts, int32_t top_k, int32_t router, const gemq_routing_t* routing, uint32_t flags,
+                  void* logits, int32_t* topk_idx, uint16_t* topk_w, void* workspace, size_t workspace_bytes,
+                  void* stream) {
   TraceRange trace("gemq_route");
   if (num_tokens < 0) return fail(GEMQ_ERR_INVALID_ARGUMENT, "negative token count");
   if (num_tokens == 0) return GEMQ_OK;
@@ -818,6 +843,8 @@ int gemq_route(const uint16_t* x, int64_t num_tokens, int32_t hidden, const uint
   if (router != GEMQ_ROUTER_FP16 && router != GEMQ_ROUTER_FP32)
     return fail(GEMQ_ERR_INVALID_ARGUMENT, "unknown router flavour");
   if (reinterpret_cast<uintptr_t>(x) & 15u) return fail(GEMQ_ERR_UNSUPPORTED, "x must be 16-byte aligned");
+  const gemq_routing_t ro = routing ? *routing : gemq_routing_t{0, 1, 1, 1.0f};
+  if (int rc = check_routing(ro, num_experts, top_k)) return rc;
   Carver c(workspace);
   Seg* seg = c.take<Seg>(1);
   int32_t* tp = c.take<int32_t>(2);
@@ -828,11 +855,19 @@ int gemq_route(const uint16_t* x, int64_t num_tokens, int32_t hidden, const uint
   d.hidden = hidden;
   d.num_experts = num_experts;
   d.top_k = top_k;
-  d.norm_topk_prob = norm_topk_prob;
+  d.norm_topk_prob = ro.norm_topk_prob;
   d.router = router;
   d.gate_weight = gate_weight;
-  return run_router(d, device_sm_count(), x, num_tokens, logits, (flags & GEMQ_FWD_GIVEN_LOGITS) != 0, topk_idx,
+  return run_router(d, ro, device_sm_count(), x, num_tokens, logits, (flags & GEMQ_FWD_GIVEN_LOGITS) != 0, topk_idx,
                     topk_w, flags, seg, tp, static_cast<cudaStream_t>(stream));
+}
+
+int gemq_layer_set_routing(gemq_layer_t* layer, const gemq_routing_t* routing) {
+  if (layer == nullptr || routing == nullptr) return fail(GEMQ_ERR_INVALID_ARGUMENT, "null argument");
+  if (int rc = check_routing(*routing, layer->d.num_experts, layer->d.top_k)) return rc;
+  layer->ro = *routing;
+  layer->d.norm_topk_prob = routing->norm_topk_prob;
+  return GEMQ_OK;
 }
 
 int gemq_moe_combine(const uint16_t* y, const int32_t* slot_row, const int32_t* topk_idx, int64_t num_tokens,

@@ -137,8 +137,11 @@ cudaError_t launch_build_index_segs(const int32_t* indices, int num_indices, int
 // Gate logits of a small batch over many CTAs (then launch_topk).
 cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16_t* gate, int E, bool fp32_logits,
                                void* logits, cudaStream_t stream);
+// n_group > 1: group-limited greedy over n_group equal expert groups, keeping
+// topk_group of them; scale multiplies the weights when not renormalising.
 cudaError_t launch_topk(const void* logits, bool logits_fp32, int64_t T, int E, int k, bool norm, bool fp16_softmax,
-                        int32_t* topk_idx, uint16_t* topk_w, cudaStream_t stream);
+                        int n_group, int topk_group, float scale, int32_t* topk_idx, uint16_t* topk_w,
+                        cudaStream_t stream);
 bool small_dispatch_ok(int64_t P, int E);
 // Segments of rows grouped as [group][expert] (n = groups * E counts, n <= 1024).
 cudaError_t launch_group_segs(const int32_t* counts, int n, int E, int nt, Seg* segs, int32_t* tile_prefix,

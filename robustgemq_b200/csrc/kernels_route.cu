@@ -2,7 +2,10 @@
 //
 // Reference behaviour restated (paths relative to the RobustGEMQ root):
 //   router     gemq/inference/moe_block.py:790-797 (fp16 logits), 549-556 (fp32 logits),
-//              280-283 (Mixtral one-token: fp16 softmax / top-k / renorm)
+//              280-283 (Mixtral one-token: fp16 softmax / top-k / renorm); DeepSeek-V2's
+//              group-limited greedy selection and routed_scaling_factor, which the
+//              reference's fused block rejects (moe_block.py:18-66), as transformers'
+//              DeepseekV2Moe.route_tokens_to_experts computes them
 //   dispatch   gemq/inference/moe_block.py:804-810 (one_hot / nonzero / where / gather)
 //   combine    gemq/inference/moe_block.py:799-812 (fp16 index_add_ in ascending expert order)
 #include <cuda_fp16.h>
@@ -24,6 +27,15 @@ namespace {
 
 constexpr int kMaxExperts = 256;
 
+// Routing options of the top-k step beyond the plain greedy selection.
+struct TopkOpts {
+  int norm;          // renormalise: w / (sum of the k weights)
+  int fp16_softmax;  // Mixtral one-token router: probabilities and sums rounded to fp16
+  int n_group;       // group-limited greedy: E experts in n_group equal groups (1 = off)
+  int topk_group;    // groups kept per token
+  float scale;       // factor on the weights when not renormalising (routed_scaling_factor)
+};
+
 // Top-k of one token's probabilities v (slot i of lane l = expert 32 i + l; NV slots
 // in use) in k rounds of a warp argmax, in the order "larger probability first,
 // lower expert id on ties", NaN ahead of every number (torch.topk's order). Each
@@ -32,17 +44,51 @@ constexpr int kMaxExperts = 256;
 // either sign as +0), 0 for a slot out of range or already taken. A round takes the
 // warp maximum of the lanes' best keys, then the lowest expert id holding it (two
 // redux.sync). The selected weights are summed in selection order, then lane r
-// writes the rank-r expert and its (renormalised) weight.
+// writes the rank-r expert and its weight: w / sum when renormalising, else w * scale.
+//
+// Group-limited greedy (n_group > 1): each group's score is the largest probability
+// among its E / n_group consecutive experts; the topk_group best groups are kept
+// (larger score first, lower group id on ties; lane g holds group g's key), and the
+// probabilities of every other group's experts become 0.0 before the k rounds, as
+// masked_fill(~mask, 0.0) does, so they stay selectable only behind every kept one.
 template <int NV>
-__device__ __forceinline__ void select_topk(const float (&v)[kMaxExperts / 32], int E, int k, int norm,
-                                            int fp16_softmax, int32_t* __restrict__ idx_out,
-                                            __half* __restrict__ w_out) {
+__device__ __forceinline__ void select_topk(float (&v)[kMaxExperts / 32], int E, int k, const TopkOpts& o,
+                                            int32_t* __restrict__ idx_out, __half* __restrict__ w_out) {
   const int lane = threadIdx.x & 31;
   uint32_t key[NV];
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const uint32_t bits = __float_as_uint(v[i] != v[i] ? FLT_MAX : v[i]);
     key[i] = (i * 32 + lane >= E) ? 0u : (bits & 0x80000000u) ? 1u : bits + 1u;
+  }
+  if (o.n_group > 1) {
+    const int gsize = E / o.n_group;
+    int grp[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) grp[i] = (i * 32 + lane < E) ? (i * 32 + lane) / gsize : -1;
+    uint32_t gkey = 0u;
+    for (int g = 0; g < o.n_group; ++g) {
+      uint32_t m = 0u;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) m = (grp[i] == g && key[i] > m) ? key[i] : m;
+      m = __reduce_max_sync(0xffffffffu, m);
+      if (lane == g) gkey = m;
+    }
+    uint32_t keep = 0u;  // bit g: group g kept (warp-uniform)
+    for (int r = 0; r < o.topk_group; ++r) {
+      const uint32_t gmax = __reduce_max_sync(0xffffffffu, gkey);
+      if (gmax == 0u) break;
+      const uint32_t win = __reduce_min_sync(0xffffffffu, gkey == gmax ? static_cast<uint32_t>(lane) : 32u);
+      keep |= 1u << win;
+      if (lane == static_cast<int>(win)) gkey = 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (grp[i] >= 0 && !((keep >> grp[i]) & 1u)) {
+        v[i] = 0.f;
+        key[i] = 1u;  // +0.0
+      }
+    }
   }
   float wsum = 0.f, myw = 0.f;
   int mye = 0;
@@ -75,9 +121,9 @@ __device__ __forceinline__ void select_topk(const float (&v)[kMaxExperts / 32], 
     }
   }
   if (lane < k) {
-    if (fp16_softmax) wsum = __half2float(__float2half_rn(wsum));
+    if (o.fp16_softmax) wsum = __half2float(__float2half_rn(wsum));
     idx_out[lane] = mye;
-    w_out[lane] = __float2half_rn(norm ? myw / wsum : myw);
+    w_out[lane] = __float2half_rn(o.norm ? myw / wsum : myw * o.scale);
   }
 }
 
@@ -87,8 +133,8 @@ __device__ __forceinline__ void select_topk(const float (&v)[kMaxExperts / 32], 
 // the selected ids are always valid. fp16_softmax rounds the probabilities, their
 // sum and the quotients to fp16 as the fp16 tensors of moe_block.py:280-283 do.
 template <typename GetLogit>
-__device__ __forceinline__ void topk_warp(GetLogit get, int E, int k, int norm, int fp16_softmax,
-                                          int32_t* __restrict__ idx_out, __half* __restrict__ w_out) {
+__device__ __forceinline__ void topk_warp(GetLogit get, int E, int k, const TopkOpts& o, int32_t* __restrict__ idx_out,
+                                          __half* __restrict__ w_out) {
   const int lane = threadIdx.x & 31;
   float v[kMaxExperts / 32];
   float mx = -FLT_MAX;
@@ -114,20 +160,20 @@ __device__ __forceinline__ void topk_warp(GetLogit get, int E, int k, int norm, 
   for (int i = 0; i < kMaxExperts / 32; ++i) {
     const int e = i * 32 + lane;
     float pr = (e < E) ? v[i] / sum : -1.f;
-    if (fp16_softmax && e < E) pr = __half2float(__float2half_rn(pr));
+    if (o.fp16_softmax && e < E) pr = __half2float(__float2half_rn(pr));
     v[i] = pr;
   }
   const int nv = (E + 31) / 32;  // value slots per lane in use
-  if (nv <= 1) select_topk<1>(v, E, k, norm, fp16_softmax, idx_out, w_out);
-  else if (nv <= 2) select_topk<2>(v, E, k, norm, fp16_softmax, idx_out, w_out);
-  else if (nv <= 4) select_topk<4>(v, E, k, norm, fp16_softmax, idx_out, w_out);
-  else select_topk<8>(v, E, k, norm, fp16_softmax, idx_out, w_out);
+  if (nv <= 1) select_topk<1>(v, E, k, o, idx_out, w_out);
+  else if (nv <= 2) select_topk<2>(v, E, k, o, idx_out, w_out);
+  else if (nv <= 4) select_topk<4>(v, E, k, o, idx_out, w_out);
+  else select_topk<8>(v, E, k, o, idx_out, w_out);
 }
 
 // One warp per token, logits from global memory (the tensor-core router's output
 // or given logits).
-__global__ void k_topk(const void* __restrict__ logits, int logits_fp32, int64_t T, int E, int k, int norm,
-                       int fp16_softmax, int32_t* __restrict__ topk_idx, __half* __restrict__ topk_w) {
+__global__ void k_topk(const void* __restrict__ logits, int logits_fp32, int64_t T, int E, int k, TopkOpts o,
+                       int32_t* __restrict__ topk_idx, __half* __restrict__ topk_w) {
   grid_dep_wait();
   const int64_t t = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   if (t >= T) return;
@@ -135,7 +181,7 @@ __global__ void k_topk(const void* __restrict__ logits, int logits_fp32, int64_t
     return logits_fp32 ? static_cast<const float*>(logits)[t * E + e]
                        : __half2float(static_cast<const __half*>(logits)[t * E + e]);
   };
-  topk_warp(get, E, k, norm, fp16_softmax, topk_idx + t * k, topk_w + t * k);
+  topk_warp(get, E, k, o, topk_idx + t * k, topk_w + t * k);
 }
 
 // Gate logits for small batches, spread over many CTAs: CTA (i, j) computes experts
@@ -633,11 +679,12 @@ __global__ void __launch_bounds__(32 * kCombineWarps, KMAX == 8 ? 2 : 1)
 }  // namespace
 
 cudaError_t launch_topk(const void* logits, bool logits_fp32, int64_t T, int E, int k, bool norm, bool fp16_softmax,
-                        int32_t* topk_idx, uint16_t* topk_w, cudaStream_t stream) {
+                        int n_group, int topk_group, float scale, int32_t* topk_idx, uint16_t* topk_w,
+                        cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
+  const TopkOpts o{norm ? 1 : 0, fp16_softmax ? 1 : 0, n_group, topk_group, scale};
   return launch_dep(k_topk, dim3(static_cast<unsigned>((T * 32 + 255) / 256)), dim3(256), 0, stream, logits,
-                    logits_fp32 ? 1 : 0, T, E, k, norm ? 1 : 0, fp16_softmax ? 1 : 0, topk_idx,
-                    reinterpret_cast<__half*>(topk_w));
+                    logits_fp32 ? 1 : 0, T, E, k, o, topk_idx, reinterpret_cast<__half*>(topk_w));
 }
 
 cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16_t* gate, int E, bool fp32_logits,

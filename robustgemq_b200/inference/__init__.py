@@ -11,4 +11,5 @@ from .moe_block import (  # noqa: F401
     check_deepseek_gate_matches,
     check_deepseek_routing_supported,
     check_w1_w3_aligned,
+    deepseek_group_routing,
 )

@@ -5,7 +5,7 @@ projection (the stacked packed layout of ``from_hf``, sliced by expert with its
 strides rebased, or built from the rank's experts alone with ``from_shard``). A
 forward on a rank's own tokens:
 
-1. routes them over all ``E`` experts (``gemq_route``; the gate is replicated);
+1. routes them over all ``E`` experts (``gemq_route_ex``; the gate is replicated);
 2. groups the ``T * k`` token-expert slots by expert id on the device
    (``gemq_moe_dispatch``: histogram, scan, scatter of the activation rows and
    routing weights). Experts are contiguous per rank, so the rows come out grouped
@@ -52,6 +52,8 @@ no CPU fallback.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 from typing import Callable, Optional, Tuple
 
@@ -128,6 +130,8 @@ class ExpertParallelMoE(nn.Module):
         self.e0 = self.rank * self.experts_per_rank
         self.router_fp32 = src.router_fp32
         self.norm = bool(src.norm_topk_prob or src.always_normalize)
+        # group-limited selection and the routing scale span all E experts
+        self.routing = (self.norm, src.n_group, src.topk_group, src.routed_scaling_factor)
         self.returns_logits = src.returns_logits
         self.gate_weight = gate_weight.detach().to(torch.float16).contiguous()
         self.shared = src if getattr(src, "has_shared", False) else None
@@ -192,9 +196,10 @@ class ExpertParallelMoE(nn.Module):
         w = torch.empty((T, self.top_k), dtype=torch.float16, device=x.device)
         ws = torch.empty(_lib.ROUTE_WORKSPACE_BYTES, dtype=torch.uint8, device=x.device)
         router = _lib.GEMQ_ROUTER_FP32 if self.router_fp32 else _lib.GEMQ_ROUTER_FP16
-        check(_lib.load().gemq_route(ptr(x), T, self.hidden_dim, ptr(gw), self.num_experts, self.top_k, router,
-                                     int(self.norm), 0, ptr(logits), ptr(idx), ptr(w), ptr(ws), ws.numel(),
-                                     stream_ptr(x.device)))
+        r = _lib.RoutingT(int(self.routing[0]), *self.routing[1:])
+        check(_lib.load().gemq_route_ex(ptr(x), T, self.hidden_dim, ptr(gw), self.num_experts, self.top_k, router,
+                                        ctypes.byref(r), 0, ptr(logits), ptr(idx), ptr(w), ptr(ws), ws.numel(),
+                                        stream_ptr(x.device)))
         return logits, idx, w
 
     def rows_permuted(self) -> bool:

@@ -38,40 +38,54 @@ from ..ops import dequant_gemm, dequant_group_gemm, make_proj
 # --------------------------------------------------------------------------- guards
 def check_deepseek_routing_supported(config):
     """Expert-selection features the fused DeepSeek forward does not implement
-    (moe_block.py:18-28)."""
+    (moe_block.py:18-28). The reference accepts only ``topk_method='greedy'``; this
+    block also runs DeepSeek-V2's ``group_limited_greedy`` (``n_group`` groups of
+    experts, ``topk_group`` kept per token, as transformers'
+    ``DeepseekV2Moe.route_tokens_to_experts`` selects them). Scoring stays softmax."""
     scoring_func = getattr(config, "scoring_func", "softmax")
     assert scoring_func == "softmax", (
         f"fused block always uses softmax scoring, config asks for '{scoring_func}'"
     )
-    assert getattr(config, "topk_method", "greedy") == "greedy", (
-        f"fused block only implements topk_method='greedy', got '{config.topk_method}'"
+    method = getattr(config, "topk_method", "greedy")
+    assert method in ("greedy", "group_limited_greedy"), (
+        f"fused block implements topk_method 'greedy' and 'group_limited_greedy', got '{method}'"
     )
+    if method == "group_limited_greedy":
+        n_group, topk_group = int(config.n_group), int(config.topk_group)
+        assert 1 <= n_group <= 32 and config.n_routed_experts % n_group == 0, (
+            f"n_group ({n_group}) must be in [1, 32] and divide n_routed_experts ({config.n_routed_experts})"
+        )
+        assert 1 <= topk_group <= n_group, f"topk_group ({topk_group}) must be in [1, n_group]"
+        assert topk_group * (config.n_routed_experts // n_group) >= config.num_experts_per_tok, (
+            "the kept groups must hold at least num_experts_per_tok experts"
+        )
+
+
+def deepseek_group_routing(config):
+    """``(n_group, topk_group)`` of the config's expert selection; (1, 1) for greedy."""
+    if getattr(config, "topk_method", "greedy") == "group_limited_greedy":
+        return int(config.n_group), int(config.topk_group)
+    return 1, 1
 
 
 def check_deepseek_gate_matches(config, hf_block):
-    """The fused block combines routing weights as ``w /= w.sum()`` when
-    ``norm_topk_prob`` and never applies ``routed_scaling_factor``; accept only
-    configurations where the block it replaces does the same (moe_block.py:31-66)."""
+    """How the replaced block combines its routing weights, as ``(normalize, scale)``:
+    the fused block computes ``w / w.sum()`` when ``normalize``, else
+    ``w * scale`` (moe_block.py:31-66 lists the two gates):
+
+        official modeling_deepseek.py:  w /= w.sum()  if top_k > 1 and norm_topk_prob
+                                        else  w *= routed_scaling_factor
+        HF built-in:                    w *= routed_scaling_factor  (norm_topk_prob unused)
+
+    The reference's fused block never scales, so it asserts that the replaced gate
+    does not either; this block applies the scale and accepts every combination."""
     is_builtin = type(hf_block).__module__.startswith("transformers.models.deepseek_v2")
-    normalizes = bool(config.norm_topk_prob)
-    top_k = config.num_experts_per_tok
-    scaling = getattr(config, "routed_scaling_factor", 1.0)
+    scaling = float(getattr(config, "routed_scaling_factor", 1.0))
     if is_builtin:
-        assert not normalizes, (
-            "HF's built-in gate ignores norm_topk_prob while the fused block honours it; "
-            "they agree only while it is False"
-        )
-        assert scaling == 1.0, (
-            f"built-in gate always scales by routed_scaling_factor ({scaling}), which the fused block never applies"
-        )
-        return
-    assert not (normalizes and top_k == 1), (
-        "at top_k=1 the official gate scales, while the fused block would normalize the single weight to 1.0"
-    )
-    if not (normalizes and top_k > 1):
-        assert scaling == 1.0, (
-            f"the official gate scales by routed_scaling_factor ({scaling}) whenever it does not normalize"
-        )
+        return False, scaling
+    if bool(config.norm_topk_prob) and config.num_experts_per_tok > 1:
+        return True, 1.0
+    return False, scaling
 
 
 def check_w1_w3_aligned(fused_block):
@@ -123,6 +137,8 @@ class _QuantFusedMoEBlock(nn.Module):
         self.w1_wq_strides, self.w1_zs_strides = None, None
         self.w2_wq_strides, self.w2_zs_strides = None, None
         self.w3_wq_strides, self.w3_zs_strides = None, None
+        self.n_group, self.topk_group = 1, 1
+        self.routed_scaling_factor = 1.0
         self._handle = None
         self._workspaces = {}
         self._fwd_flags = 0
@@ -166,6 +182,29 @@ class _QuantFusedMoEBlock(nn.Module):
         self.block_group_size = int(block_group_size.item())
         check_w1_w3_aligned(self)
         self.invalidate()
+
+    def set_routing(self, norm_topk_prob: Optional[bool] = None, routed_scaling_factor: Optional[float] = None,
+                    n_group: Optional[int] = None, topk_group: Optional[int] = None):
+        """Change the router's weight rule (``w / sum`` when ``norm_topk_prob``, else
+        ``w * routed_scaling_factor``) or its group-limited selection."""
+        if norm_topk_prob is not None:
+            self.norm_topk_prob = bool(norm_topk_prob)
+        if routed_scaling_factor is not None:
+            self.routed_scaling_factor = float(routed_scaling_factor)
+        if n_group is not None:
+            self.n_group = int(n_group)
+        if topk_group is not None:
+            self.topk_group = int(topk_group)
+        if self._handle is not None:
+            self._apply_routing(self._handle)
+
+    def routing_options(self) -> "_lib.RoutingT":
+        return _lib.RoutingT(int(self.norm_topk_prob or self.always_normalize), self.n_group, self.topk_group,
+                             self.routed_scaling_factor)
+
+    def _apply_routing(self, handle):
+        r = self.routing_options()
+        check(_lib.load().gemq_layer_set_routing(handle, ctypes.byref(r)))
 
     def invalidate(self):
         """Drop the native layer handle (call after replacing weight tensors)."""
@@ -211,6 +250,11 @@ class _QuantFusedMoEBlock(nn.Module):
             self._fill_shared(d)
             handle = ctypes.c_void_p()
             check(_lib.load().gemq_layer_create(ctypes.byref(d), ctypes.byref(handle)))
+            try:
+                self._apply_routing(handle)
+            except Exception:
+                _lib.load().gemq_layer_destroy(handle)
+                raise
             self._handle = handle
         return self._handle
 
@@ -361,6 +405,7 @@ class QuantFusedDeepseekV2MoEBlock(_QuantFusedMoEBlock):
         check_deepseek_routing_supported(config)
         self._init_common(config.hidden_size, config.moe_intermediate_size, config.n_routed_experts,
                           config.num_experts_per_tok, config.norm_topk_prob)
+        self.n_group, self.topk_group = deepseek_group_routing(config)
         self.num_shared_experts = config.n_shared_experts
         for name in ("shared_w1", "shared_w2", "shared_w3"):
             setattr(self, f"{name}_wq", None)
@@ -370,8 +415,9 @@ class QuantFusedDeepseekV2MoEBlock(_QuantFusedMoEBlock):
 
     @classmethod
     def from_hf(cls, config, hf_block):
-        check_deepseek_gate_matches(config, hf_block)
+        normalize, scale = check_deepseek_gate_matches(config, hf_block)
         fused_block = super().from_hf(config, hf_block)
+        fused_block.set_routing(norm_topk_prob=normalize, routed_scaling_factor=scale)
         se = hf_block.shared_experts
         fused_block.load_shared(se.gate_proj, se.up_proj, se.down_proj)
         return fused_block

@@ -168,30 +168,54 @@ class _BuiltinBlockStub:
 _BuiltinBlockStub.__module__ = "transformers.models.deepseek_v2.modeling_deepseek_v2"
 
 
-@pytest.mark.parametrize("field,value", [("topk_method", "group_limited_greedy"), ("scoring_func", "sigmoid")])
-def test_deepseek_feature_guard(field, value):
-    from robustgemq_b200.inference import check_deepseek_routing_supported
+@pytest.mark.parametrize("fields", [
+    dict(scoring_func="sigmoid"), dict(topk_method="noaux_tc"),
+    dict(topk_method="group_limited_greedy", n_group=3, topk_group=1),   # 3 does not divide 4 experts
+    dict(topk_method="group_limited_greedy", n_group=2, topk_group=3),   # more kept groups than groups
+    dict(topk_method="group_limited_greedy", n_group=4, topk_group=1),   # 1 kept expert < top_k = 2
+])
+def test_deepseek_feature_guard(fields):
+    from robustgemq_b200.inference import check_deepseek_routing_supported, deepseek_group_routing
 
     check_deepseek_routing_supported(_ds_config())
+    ok = _ds_config(topk_method="group_limited_greedy", n_group=2, topk_group=1)
+    check_deepseek_routing_supported(ok)
+    assert deepseek_group_routing(ok) == (2, 1)
+    assert deepseek_group_routing(_ds_config(n_group=2, topk_group=1)) == (1, 1)  # greedy ignores the groups
     with pytest.raises(AssertionError):
-        check_deepseek_routing_supported(_ds_config(**{field: value}))
+        check_deepseek_routing_supported(_ds_config(**fields))
 
 
-@pytest.mark.parametrize("official,norm,top_k,scaling,ok", [
-    (True, False, 2, 1.0, True), (True, False, 2, 16.0, False), (True, True, 2, 16.0, True),
-    (True, True, 1, 1.0, False), (False, False, 2, 1.0, True), (False, True, 2, 1.0, False),
-    (False, False, 2, 16.0, False),
+# (official gate?, norm_topk_prob, top_k, routed_scaling_factor) -> (renormalise, scale) of the
+# replaced gate (moe_block.py:31-42 states both rules); the reference's fused block accepts only
+# the rows whose rule is (norm_topk_prob, 1.0).
+@pytest.mark.parametrize("official,norm,top_k,scaling,rule", [
+    (True, False, 2, 1.0, (False, 1.0)), (True, False, 2, 16.0, (False, 16.0)), (True, True, 2, 16.0, (True, 1.0)),
+    (True, True, 1, 2.0, (False, 2.0)), (False, False, 2, 1.0, (False, 1.0)), (False, True, 2, 1.0, (False, 1.0)),
+    (False, False, 2, 16.0, (False, 16.0)),
 ])
-def test_deepseek_gate_guard_truth_table(official, norm, top_k, scaling, ok):
+def test_deepseek_gate_rule_table(official, norm, top_k, scaling, rule):
     from robustgemq_b200.inference import check_deepseek_gate_matches
 
     cfg = _ds_config(norm_topk_prob=norm, num_experts_per_tok=top_k, routed_scaling_factor=scaling)
     blk = _OfficialBlockStub() if official else _BuiltinBlockStub()
-    if ok:
-        check_deepseek_gate_matches(cfg, blk)
-    else:
-        with pytest.raises(AssertionError):
-            check_deepseek_gate_matches(cfg, blk)
+    assert check_deepseek_gate_matches(cfg, blk) == rule
+
+
+@pytest.mark.parametrize("n_group,topk_group,scale", [(3, 1, 1.0), (0, 1, 1.0), (33, 1, 1.0), (4, 5, 1.0),
+                                                      (8, 1, 1.0), (4, 2, float("inf")), (4, 2, float("nan"))])
+def test_route_ex_rejects_bad_routing_options(n_group, topk_group, scale):
+    """Option checks run before any device work (E = 64, k = 16: 8 groups keeping 1 hold
+    only 8 experts)."""
+    from robustgemq_b200 import _lib
+
+    lib = _lib.load()
+    r = _lib.RoutingT(0, n_group, topk_group, scale)
+    fake = ctypes.c_void_p(1 << 20)  # never dereferenced: the options fail first
+    rc = lib.gemq_route_ex(fake, 4, 64, fake, 64, 16, _lib.GEMQ_ROUTER_FP32, ctypes.byref(r), 0, fake, fake, fake,
+                           fake, 1 << 16, None)
+    assert rc != 0
+    assert lib.gemq_layer_set_routing(None, ctypes.byref(r)) != 0
 
 
 def test_from_hf_requires_packed_linears():
