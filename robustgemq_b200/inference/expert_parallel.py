@@ -27,6 +27,15 @@ forward on a rank's own tokens:
    ``forward_n_tokens`` (moe_block.py:799-812), so a rank's output equals the 1-GPU
    block's on the same tokens whenever the per-row GEMM results do.
 
+``placement`` (a permutation of the expert ids) replaces the contiguous ranges: rank
+``r`` then holds experts ``placement[r * E / P:(r + 1) * E / P]``, and the dispatch
+groups slots by an expert's position in ``placement`` (one gather of the routed ids),
+so rows still come out grouped by destination rank. The combine reads the original
+ids, so its ascending-expert order, and with it the output, does not depend on the
+placement. ``balanced_placement`` builds one from per-expert loads (the token counts
+every forward accumulates in ``expert_load``, or any other estimate), largest load
+first onto the least loaded rank that still has room.
+
 DeepSeek's shared experts are replicated and run on the token's own rank; their
 output is added in fp16 after the combine (moe_block.py:575).
 
@@ -55,7 +64,7 @@ from __future__ import annotations
 
 import ctypes
 
-from typing import Callable, Optional, Tuple
+from typing import Callable, List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
@@ -93,6 +102,67 @@ def slice_projection(block: _QuantFusedMoEBlock, name: str, e0: int, e1: int, k:
     }
 
 
+def gather_projection(block: _QuantFusedMoEBlock, name: str, experts: Sequence[int], k: int) -> dict:
+    """Experts ``experts`` (any order) of a stacked projection, in that order, strides
+    rebased; a contiguous ascending run is one slice."""
+    experts = [int(e) for e in experts]
+    if experts == list(range(experts[0], experts[0] + len(experts))):
+        return slice_projection(block, name, experts[0], experts[0] + len(experts), k)
+    parts = [slice_projection(block, name, e, e + 1, k) for e in experts]
+    out = {key: torch.cat([p[key] for p in parts]).contiguous()
+           for key in ("wq", "scales", "zeros", "nbits", "group_sizes")}
+    n = out["wq"].shape[1]
+    dev = out["wq"].device
+    w_sizes = [p["wq"].numel() for p in parts]
+    z_sizes = [p["scales"].numel() for p in parts]
+    out["wq_strides"] = torch.tensor([sum(w_sizes[:i]) for i in range(len(parts))], dtype=torch.int32, device=dev)
+    out["zs_strides"] = torch.tensor([sum(z_sizes[:i]) for i in range(len(parts))], dtype=torch.int32, device=dev)
+    assert all(int(v) % n == 0 for v in out["wq_strides"].tolist())
+    return out
+
+
+def balanced_placement(load: Sequence[float], world: int) -> List[int]:
+    """An expert order whose ``world`` equal slices (one per rank) have balanced total
+    load. Experts go by decreasing load (lower id first on ties) onto the rank with the
+    least load so far among those with a free slot (lower rank on ties); then, while
+    it lowers the heaviest rank's load, the best swap of one of its experts with a
+    lighter expert of another rank is made. Returns the concatenation of the ranks'
+    expert lists, each ascending."""
+    load = [float(v) for v in load]
+    E = len(load)
+    if world <= 0 or E % world != 0:
+        raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+    epr = E // world
+    bins: List[List[int]] = [[] for _ in range(world)]
+    tot = [0.0] * world
+    for e in sorted(range(E), key=lambda i: (-load[i], i)):
+        r = min((r for r in range(world) if len(bins[r]) < epr), key=lambda r: (tot[r], r))
+        bins[r].append(e)
+        tot[r] += load[e]
+    for _ in range(E * E):
+        h = max(range(world), key=lambda r: (tot[r], -r))
+        best = None  # (new max of the pair, a, r, b)
+        for r in range(world):
+            if r == h:
+                continue
+            for a in bins[h]:
+                for b in bins[r]:
+                    d = load[a] - load[b]
+                    if d > 0:
+                        m = max(tot[h] - d, tot[r] + d)
+                        if m < tot[h] and (best is None or m < best[0]):
+                            best = (m, a, r, b)
+        if best is None:
+            break
+        _, a, r, b = best
+        d = load[a] - load[b]
+        bins[h][bins[h].index(a)] = b
+        bins[r][bins[r].index(b)] = a
+        tot[h] -= d
+        tot[r] += d
+    return [e for b in bins for e in sorted(b)]
+
+
 class _LocalExperts(_QuantFusedMoEBlock):
     """A rank's slice of the routed experts, run with given routing and ``top_k = 1``."""
 
@@ -110,7 +180,7 @@ class ExpertParallelMoE(nn.Module):
     def __init__(self, block: Optional[_QuantFusedMoEBlock], group=None, route_fn: Optional[Callable] = None,
                  experts_fn: Optional[Callable] = None, combine_fn: Optional[Callable] = None,
                  dispatch_fn: Optional[Callable] = None, time_stages: bool = False, sm_budget: int = 0,
-                 _shard: Optional[tuple] = None):
+                 placement: Optional[Sequence[int]] = None, _shard: Optional[tuple] = None):
         super().__init__()
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -127,7 +197,15 @@ class ExpertParallelMoE(nn.Module):
         self.num_experts, self.top_k = E, src.top_k
         self.hidden_dim, self.ffn_dim = src.hidden_dim, src.ffn_dim
         self.experts_per_rank = E // self.world
-        self.e0 = self.rank * self.experts_per_rank
+        self.e0 = self.rank * self.experts_per_rank  # first slot of this rank in the placement
+        order = list(range(E)) if placement is None else [int(e) for e in placement]
+        if sorted(order) != list(range(E)):
+            raise ValueError(f"placement must be a permutation of the {E} expert ids")
+        self.placement = order
+        self.local_experts = order[self.e0:self.e0 + self.experts_per_rank]  # global ids, slot order
+        self._identity = order == list(range(E))
+        self._slot_of = None  # device int32 [E]: expert id -> position in the placement
+        self.expert_load = None  # token-expert slots routed to each expert (device int64 [E])
         self.router_fp32 = src.router_fp32
         self.norm = bool(src.norm_topk_prob or src.always_normalize)
         # group-limited selection and the routing scale span all E experts
@@ -151,7 +229,8 @@ class ExpertParallelMoE(nn.Module):
         # gate/up bit-widths of all E experts (the dispatch writes each row in the K
         # order its owner's tensor-memory GEMM reads); a shard gathers them once
         if _shard is None:
-            self.w1_nbits_all = block.w1_nbits
+            self.w1_nbits_all = block.w1_nbits if self._identity else block.w1_nbits[torch.tensor(
+                order, device=block.w1_nbits.device)]
         elif self.world > 1:
             nb = local_block.w1_nbits.to(torch.int32).contiguous()
             allnb = nb.new_empty(E)
@@ -175,13 +254,13 @@ class ExpertParallelMoE(nn.Module):
         """Build from this rank's experts alone: ``local_block`` holds experts
         ``[rank * E / P, (rank + 1) * E / P)`` (its own gate is not used), and
         ``gate_weight`` is the full ``[E, hidden]`` router weight. No rank ever holds
-        the whole layer."""
+        the whole layer. With ``placement=...`` the block holds experts
+        ``placement[rank * E / P:(rank + 1) * E / P]`` in that order."""
         return cls(None, group=group, _shard=(local_block, gate_weight, num_experts), **kw)
 
     def _load_local(self, block: _QuantFusedMoEBlock):
-        e1 = self.e0 + self.experts_per_rank
         for name, k in (("w1", block.hidden_dim), ("w3", block.hidden_dim), ("w2", block.ffn_dim)):
-            for key, t in slice_projection(block, name, self.e0, e1, k).items():
+            for key, t in gather_projection(block, name, self.local_experts, k).items():
                 setattr(self.local, f"{name}_{key}", t)
         self.local.block_group_size = block.block_group_size
         self.local.invalidate()
@@ -201,6 +280,24 @@ class ExpertParallelMoE(nn.Module):
                                         ctypes.byref(r), 0, ptr(logits), ptr(idx), ptr(w), ptr(ws), ws.numel(),
                                         stream_ptr(x.device)))
         return logits, idx, w
+
+    def _count_load(self, counts: Tensor) -> None:
+        c = counts.to(torch.int64)
+        if self.expert_load is None or self.expert_load.device != c.device:
+            self.expert_load = torch.zeros(self.num_experts, dtype=torch.int64, device=c.device)
+        if self._identity:
+            self.expert_load += c
+        else:
+            self.expert_load.index_add_(0, torch.tensor(self.placement, device=c.device), c)
+
+    def measured_load(self) -> Tensor:
+        """Token-expert slots routed to each expert since construction, summed over
+        all ranks (a collective: every rank calls it)."""
+        load = self.expert_load.clone() if self.expert_load is not None else torch.zeros(
+            self.num_experts, dtype=torch.int64, device=self.gate_weight.device)
+        if self.world > 1:
+            dist.all_reduce(load, group=self.group)
+        return load
 
     def rows_permuted(self) -> bool:
         """Whether the local experts' GEMM takes rows in the tensor-memory GEMM's K order
@@ -288,8 +385,18 @@ class ExpertParallelMoE(nn.Module):
         logits, idx, w = self.route_fn(x)
         self._mark(1, dev)
         flat = idx.reshape(-1)
-        bad = ((flat < 0) | (flat >= self.num_experts)).any().to(torch.int32).reshape(1)
-        counts, slot_row, w_rows, x_rows = self.dispatch_fn(idx, w, x)
+        valid = (flat >= 0) & (flat < self.num_experts)
+        bad = (~valid).any().to(torch.int32).reshape(1)
+        didx = idx
+        if not self._identity:  # dispatch by position in the placement; invalid ids pass through
+            if self._slot_of is None or self._slot_of.device != idx.device:
+                slot = torch.empty(self.num_experts, dtype=torch.int32)
+                slot[torch.tensor(self.placement)] = torch.arange(self.num_experts, dtype=torch.int32)
+                self._slot_of = slot.to(idx.device)
+            didx = torch.where(valid, self._slot_of[flat.clamp(0, self.num_experts - 1).long()],
+                               flat.to(torch.int32)).reshape(idx.shape).to(idx.dtype)
+        counts, slot_row, w_rows, x_rows = self.dispatch_fn(didx, w, x)
+        self._count_load(counts)
         self._mark(2, dev)
         # counts first, each destination's block with this rank's routing status, so
         # every rank can size its receives; the only host synchronisation

@@ -92,7 +92,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _cpu_ep(route_hook=None):
+def _cpu_ep(route_hook=None, placement=None):
     """An ExpertParallelMoE on the golden OLMoE block whose router, local experts and
     combine are the oracle's; ``route_hook(idx)`` may rewrite the routed expert ids."""
     from oracle import gemq_oracle as O
@@ -122,7 +122,7 @@ def _cpu_ep(route_hook=None):
             for e in range(gc.shape[1]):
                 c = int(gc[g, e])
                 if c:
-                    ye = O.expert_ffn_n_tokens(ow, ep.e0 + e, rows_np[off:off + c])
+                    ye = O.expert_ffn_n_tokens(ow, ep.local_experts[e], rows_np[off:off + c])
                     y[off:off + c] = (ye.astype(F32) * w_np[off:off + c].astype(F32)[:, None]).astype(F16)
                 off += c
         return torch.from_numpy(y)
@@ -137,7 +137,7 @@ def _cpu_ep(route_hook=None):
         return torch.from_numpy(out)
 
     ep = ExpertParallelMoE(blk, route_fn=route_fn, experts_fn=experts_fn, combine_fn=combine_fn,
-                           dispatch_fn=dispatch_fn)
+                           dispatch_fn=dispatch_fn, placement=placement)
     return ep, ow, d
 
 
@@ -150,31 +150,78 @@ def _matches_oracle(ep, ow, d, rank, world):
     return bool(np.array_equal(out.numpy().view(np.uint16), ref.view(np.uint16)))
 
 
-def _cpu_rank(rank, world, port, results):
+def _cpu_rank(rank, world, port, results, placement=None):
     import torch.distributed as dist
+    from oracle import gemq_oracle as O
 
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
-        ep, ow, d = _cpu_ep()
-        results[rank] = _matches_oracle(ep, ow, d, rank, world)
+        ep, ow, d = _cpu_ep(placement=placement)
+        ok = _matches_oracle(ep, ow, d, rank, world)
+        # the measured load, summed over ranks, counts every rank's routed slots
+        load = ep.measured_load().numpy()
+        x = d["x"].astype(F16)
+        want = np.zeros(ow.w1.num_experts, dtype=np.int64)
+        for r in range(world):
+            idx = O.route(np.ascontiguousarray(x[r::world]), ow.gate_w, ow.top_k, ow.norm_topk_prob).topk_idx
+            want += np.bincount(idx.reshape(-1), minlength=ow.w1.num_experts)
+        results[rank] = (ok, bool(np.array_equal(load, want)))
     finally:
         dist.destroy_process_group()
 
 
-def test_expert_parallel_two_gloo_ranks_match_the_single_block():
+@pytest.mark.parametrize("placement", [None, "shuffled"])
+def test_expert_parallel_two_gloo_ranks_match_the_single_block(placement):
+    """Contiguous expert ranges, and a shuffled placement (rank 0 holds the odd-indexed
+    half of a permutation): both bit-identical to the 1-process block."""
     import torch.multiprocessing as mp
 
+    if placement == "shuffled":
+        E = int(load_golden("block_olmoe.npz")["w1_nbits"].shape[0])
+        placement = [int(e) for e in np.random.default_rng(3).permutation(E)]
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     results = manager.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_cpu_rank, args=(r, 2, port, results)) for r in range(2)]
+    procs = [ctx.Process(target=_cpu_rank, args=(r, 2, port, results, placement)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    assert dict(results) == {0: True, 1: True}
+    assert dict(results) == {0: (True, True), 1: (True, True)}
+
+
+def test_balanced_placement():
+    from robustgemq_b200.inference.expert_parallel import balanced_placement
+
+    load = [90, 5, 5, 40, 40, 10, 10, 0]
+    order = balanced_placement(load, 2)
+    assert sorted(order) == list(range(8))
+    halves = [order[:4], order[4:]]
+    assert all(h == sorted(h) for h in halves)
+    totals = sorted(sum(load[e] for e in h) for h in halves)
+    assert totals == [100, 100]  # {0, 1, 2, 7} and {3, 4, 5, 6}
+    # contiguous ranges would give 140 / 60; one expert per rank is the identity
+    assert balanced_placement(load, 8) == sorted(range(8), key=lambda e: (-load[e], e))
+    with pytest.raises(ValueError):
+        balanced_placement(load, 3)
+
+
+def test_gather_projection_keeps_each_experts_dequant():
+    from oracle import gemq_oracle as O
+    from robustgemq_b200.inference.expert_parallel import gather_projection
+
+    blk, d = _golden_block()
+    full = proj_from(d, "w1")
+    experts = [5, 0, 3, 6]
+    sl = gather_projection(blk, "w1", experts, int(d["w1_K"]))
+    part = O.PackedProj(wq=sl["wq"].numpy(), scales=sl["scales"].numpy(), zeros=sl["zeros"].numpy(),
+                        nbits=sl["nbits"].numpy(), group_sizes=sl["group_sizes"].numpy(),
+                        wq_strides=sl["wq_strides"].numpy(), zs_strides=sl["zs_strides"].numpy(), K=full.K, N=full.N)
+    for j, e in enumerate(experts):
+        assert np.array_equal(O.dequantize_expert(part, j).view(np.uint16),
+                              O.dequantize_expert(full, e).view(np.uint16))
 
 
 def _bad_routing_rank(rank, world, port, results):
@@ -313,6 +360,14 @@ def test_expert_parallel_one_rank_matches_block_on_gpu():
     ep2 = ExpertParallelMoE.from_shard(loc, blk.gate.weight, blk.num_experts)
     out2, _ = ep2.forward_tokens(x)
     assert torch.equal(out2, out)
+    # a shuffled placement (the local experts gathered in its order, slots dispatched
+    # by position, the combine by expert id) gives the same bits
+    perm = [int(e) for e in np.random.default_rng(4).permutation(blk.num_experts)]
+    ep3 = ExpertParallelMoE(blk, placement=perm)
+    out3, _ = ep3.forward_tokens(x)
+    assert torch.equal(out3, out)
+    counts = torch.bincount(ep3.route_fn(x)[1].reshape(-1).long(), minlength=blk.num_experts)
+    assert torch.equal(ep3.measured_load().cpu(), counts.cpu())
     assert _lib.device_error() == 0
 
 
