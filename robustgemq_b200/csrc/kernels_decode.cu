@@ -49,10 +49,11 @@ __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, 
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
-// x values of one word row (codes j = 0..eps-1 at k0 + j), read from shared memory
-// with 16-byte loads (pow2 widths: a row starts on a multiple of eps elements, so on
-// a 16-byte boundary) or 4-byte loads (3-bit: ten fp16 / fp32 values at 20 / 40-byte
-// offsets).
+// x values of one word row, read from shared memory with 16-byte loads (pow2 widths:
+// a row starts on a multiple of eps elements, so on a 16-byte boundary) or 8-byte
+// loads (3-bit: ten fp32 values at 40-byte offsets). The staging interleaves each row
+// by code pair: slot 2p holds code p, slot 2p + 1 code p + eps/2 (p + 5 at 3 bits),
+// so the two inputs of a pair's fma.rn.f32x2 are one aligned register pair.
 template <int NB, bool XF16>
 struct XRow {
   static constexpr int kN = (NB == 3) ? 10 : 32 / NB;
@@ -124,7 +125,7 @@ __device__ __forceinline__ void word_pow2(uint32_t w, __half2 s2, __half2 z2, co
       wq = u32_as_h2(dq_pair(((w >> (NB * j)) & kMask) | 0x64006400u, s2, z2));
     }
     const float2 wf = __half22float2(wq);
-    ffma2(acc0, acc1, x.f(j), x.f(j + kHalf), wf.x, wf.y);
+    ffma2(acc0, acc1, x.f(2 * j), x.f(2 * j + 1), wf.x, wf.y);
   }
 }
 
@@ -152,7 +153,7 @@ __device__ __forceinline__ void word_3bit(uint32_t w, __half sa, __half za, __ha
       wq = u32_as_h2(dq_pair(m, s2, z2));
     }
     const float2 wf = __half22float2(wq);
-    ffma2(acc0, acc1, x.f(j), x.f(j + 5), wf.x, wf.y);
+    ffma2(acc0, acc1, x.f(2 * j), x.f(2 * j + 1), wf.x, wf.y);
   }
 }
 
@@ -396,7 +397,10 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) k_gemv(ProjDev w
     for (int j = 0; j < kXB; ++j) {
       const int i = base + j * kGemvThreads + threadIdx.x;
       if (i < kspan) {
-        reinterpret_cast<float*>(s_raw)[i] = v[j];  // fp32 (fp16 inputs convert exactly)
+        // code c of word row r at slot r * eps + (c < eps/2 ? 2c : 2(c - eps/2) + 1)
+        const int r = i / eps, c = i - r * eps, h = eps >> 1;
+        const int slot = r * eps + (c < h ? 2 * c : 2 * (c - h) + 1);
+        reinterpret_cast<float*>(s_raw)[slot] = v[j];  // fp32 (fp16 inputs convert exactly)
       }
     }
   }
