@@ -47,6 +47,8 @@ extern "C" {
 #define GEMQ_FWD_TIME_STAGES 128u    /* record CUDA events around each stage (read with gemq_layer_stage_times) */
 #define GEMQ_FWD_SMEM_DEQUANT 256u   /* use the shared-memory dequant GEMM instead of the tensor-memory one (cross-checking) */
 #define GEMQ_FWD_PERMUTED_ROWS 512u  /* gemq_moe_experts: rows are in the tensor-memory GEMM's K order (see there) */
+#define GEMQ_FWD_NO_CHAIN 1024u      /* start the down GEMM after the gate/up GEMM completes, not on the SMs it
+                                        leaves as its token tiles finish (cross-checking) */
 
 /* Stage indices reported by gemq_layer_stage_times. */
 #define GEMQ_STAGE_ROUTE 0    /* gate GEMM + softmax/top-k */

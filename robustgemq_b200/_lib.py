@@ -36,6 +36,7 @@ FWD_RESIDUAL = 64
 FWD_TIME_STAGES = 128
 FWD_SMEM_DEQUANT = 256
 FWD_PERMUTED_ROWS = 512
+FWD_NO_CHAIN = 1024
 ROUTE_WORKSPACE_BYTES = 1024
 STAGES = ("route", "dispatch", "up", "down", "shared", "combine")
 

@@ -492,6 +492,8 @@ struct FwdBufs {
   int32_t* topk_idx = nullptr;
   uint16_t* topk_w = nullptr;
   int32_t *counts = nullptr, *cursor = nullptr, *tile_prefix = nullptr, *slot_pos = nullptr;
+  int32_t* tile_done = nullptr;  // per token tile: gate/up epilogue warps done (chained launch)
+  int n_tile_done = 0;
   Seg* segs = nullptr;
   Seg* one_seg = nullptr;
   int32_t* one_tp = nullptr;
@@ -534,6 +536,9 @@ FwdBufs carve(const gemq_layer_t* L, int64_t T, uint32_t flags, void* base, cons
     b.cursor = c.take<int32_t>(E);
     b.segs = c.take<Seg>(E);
     b.tile_prefix = c.take<int32_t>(E + 1);
+    // token tiles of at least 16 rows: at most P / 16 + E of them
+    b.n_tile_done = static_cast<int>(P / kNtTiny + E + 1);
+    b.tile_done = c.take<int32_t>(b.n_tile_done);
     b.slot_pos = c.take<int32_t>(P);
     b.w_perm = c.take<uint16_t>(P);
     b.x_perm = c.take<uint16_t>(static_cast<size_t>(P) * D);
@@ -693,9 +698,22 @@ int forward_n_tokens(gemq_layer_t* L, const uint16_t* x, int64_t T, uint16_t* ou
   // by dequant cost so the decode GEMM's last wave holds its cheapest items. With
   // more waves a mix of bit-widths on the SMs at any time measured faster.
   const bool sort_segs = dec && P <= 2 * static_cast<int64_t>(E);
+  // Chained launch: the down GEMM starts on the SMs the gate/up GEMM's CTAs leave and
+  // takes each token tile once all of its gate/up items stored their h columns (the
+  // counters are zeroed by the dispatch of this forward). With stage events between
+  // the launches the down launch follows the gate/up completion and finds every
+  // counter full. Decode batches only (16 / 32-token tiles, a few waves of items, where
+  // the gate/up tail left SMs idle): measured on B200, the OLMoE decode stack 2-3%
+  // faster, the Qwen3-shaped prefill (26 waves, 64-token tiles) 3% slower.
+  const bool chain = dec && up.nt != kNtMid && (flags & GEMQ_FWD_NO_CHAIN) == 0;
+  if (chain) {
+    up.chain_done = dn.chain_done = b.tile_done;
+    dn.chain_target = (F / 128) * 4;  // gate/up feature tiles x epilogue warps per tile
+  }
   tm.begin(GEMQ_STAGE_DISPATCH);
   GEMQ_CUDA(launch_dispatch(idx, w, x, T, k, E, D, up.nt, b.counts, b.cursor, b.segs, b.tile_prefix, b.slot_pos,
-                            b.w_perm, b.x_perm, dec ? L->w1.nbits : nullptr, sort_segs ? L->w1.nbits : nullptr, s),
+                            b.w_perm, b.x_perm, dec ? L->w1.nbits : nullptr, sort_segs ? L->w1.nbits : nullptr,
+                            chain ? b.tile_done : nullptr, chain ? b.n_tile_done : 0, s),
             "dispatch");
   tm.end(GEMQ_STAGE_DISPATCH);
   tm.begin(GEMQ_STAGE_UP);
@@ -927,7 +945,7 @@ int gemq_moe_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uin
   Seg* segs = c.take<Seg>(num_experts);
   int32_t* tp = c.take<int32_t>(num_experts + 1);
   GEMQ_CUDA(launch_dispatch(topk_idx, topk_w, x, num_tokens, top_k, num_experts, hidden, kNtLarge, expert_counts,
-                            cursor, segs, tp, slot_row, w_rows, x_rows, perm_nbits, nullptr, s),
+                            cursor, segs, tp, slot_row, w_rows, x_rows, perm_nbits, nullptr, nullptr, 0, s),
             "dispatch");
   return GEMQ_OK;
 }

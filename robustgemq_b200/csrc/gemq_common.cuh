@@ -34,6 +34,7 @@ enum DeviceError : uint32_t {
   kDevBadExpert = 8,
   kDevBadBits = 9,
   kDevBadCachePos = 10,  // a KV-cache write past the cache's length (model harness)
+  kDevTimeoutChain = 11,  // a down-projection item waited too long for its gate/up tiles
 };
 
 // g_device_error: first error recorded (any kind), reported by gemq_get_device_error.
@@ -181,6 +182,52 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 // one-CTA-per-SM kernel behind them needs), while launching at completion through the
 // programmatic edge gains about 1% over plain stream order.
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// The one exception: the gate/up GEMM of a layer forward lets its down-projection
+// GEMM be scheduled (onto SMs its own CTAs have left) once each of its CTAs has begun
+// its last item; the down GEMM then waits per token tile on counters instead of on
+// grid completion (tile_done_signal / tile_done_wait).
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Counter handshake between CTAs of two kernels. The producer: every lane stores its
+// part, the warp converges, then one lane orders the warp's stores for the async proxy
+// and at GPU scope and adds 1. The consumer: one lane polls with acquire loads until the
+// count is reached, then a proxy fence so that its later TMA loads read those stores.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void tile_done_signal(int32_t* cnt) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    fence_proxy_async_global();
+    __threadfence();
+    atomicAdd(cnt, 1);
+  }
+  __syncwarp();
+}
+__device__ __forceinline__ int32_t ld_acquire_gpu(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// One thread; bounded like every wait (records kDevTimeoutChain and returns false).
+__device__ __forceinline__ bool tile_done_wait(const int32_t* cnt, int32_t target) {
+  if (ld_acquire_gpu(cnt) < target) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t polls = 1;; ++polls) {
+      __nanosleep(200);
+      if (ld_acquire_gpu(cnt) >= target) break;
+      if ((polls & 15) == 0) {
+        if (device_error_set()) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          set_device_abort(kDevTimeoutChain);
+          return false;
+        }
+      }
+    }
+  }
+  fence_proxy_async_global();
+  return true;
+}
 
 // ------------------------------------------------------------------ TMA (no multicast)
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x,

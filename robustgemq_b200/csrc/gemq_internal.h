@@ -107,6 +107,11 @@ struct GemmArgs {
   const uint16_t* row_weight;  // kRouteWeight: fp16 per output row
   int num_sms;
   const int32_t* perm_out_nbits;  // decode GEMM, kSwiGLU: store h in the slot order of these bit-widths
+  // decode GEMM, chained gate/up -> down of one forward (zeroed per forward by the
+  // dispatch): per token tile, gate/up epilogue warps done; the down launch waits
+  // for chain_target of them per tile
+  int32_t* chain_done;
+  int chain_target;
 };
 
 // Tensor-core (tcgen05) grouped GEMM; cudaErrorNotSupported for shapes it does not
@@ -149,7 +154,7 @@ cudaError_t launch_group_segs(const int32_t* counts, int n, int E, int nt, Seg* 
 cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t T, int k,
                             int E, int D, int nt, int32_t* counts, int32_t* cursor, Seg* segs, int32_t* tile_prefix,
                             int32_t* slot_pos, uint16_t* w_perm, uint16_t* x_perm, const int32_t* perm_nbits,
-                            const int32_t* order_nbits, cudaStream_t stream);
+                            const int32_t* order_nbits, int32_t* zero_buf, int zero_n, cudaStream_t stream);
 cudaError_t launch_combine(const uint16_t* y_perm, const int32_t* slot_pos, const int32_t* topk_idx, int64_t T, int k,
                            int D, bool fp32_sum, const uint16_t* add, const uint16_t* residual, uint16_t* out,
                            cudaStream_t stream);

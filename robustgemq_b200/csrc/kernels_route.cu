@@ -379,8 +379,10 @@ __global__ void k_count(const int32_t* __restrict__ topk_idx, int64_t P, int E, 
 
 // Single block: exclusive scans over experts (E <= 1024).
 __global__ void k_scan_segs(const int32_t* __restrict__ counts, int E, int nt, Seg* __restrict__ segs,
-                            int32_t* __restrict__ tile_prefix, int32_t* __restrict__ cursor) {
+                            int32_t* __restrict__ tile_prefix, int32_t* __restrict__ cursor,
+                            int32_t* __restrict__ zero_buf, int zero_n) {
   grid_dep_wait();
+  for (int i = threadIdx.x; i < zero_n; i += blockDim.x) zero_buf[i] = 0;  // per-forward tile counters
   __shared__ int s_rows[1024];
   __shared__ int s_tiles[1024];
   const int e = threadIdx.x;
@@ -495,8 +497,11 @@ __global__ void __launch_bounds__(256) k_dispatch_small(const int32_t* __restric
                                                         int32_t* __restrict__ slot_pos, __half* __restrict__ w_perm,
                                                         __half* __restrict__ x_perm,
                                                         const int32_t* __restrict__ perm_nbits,
-                                                        const int32_t* __restrict__ order_nbits) {
+                                                        const int32_t* __restrict__ order_nbits,
+                                                        int32_t* __restrict__ zero_buf, int zero_n) {
   grid_dep_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < zero_n; i += gridDim.x * blockDim.x)
+    zero_buf[i] = 0;  // per-forward tile counters
   __shared__ int s_idx[kSmallDispatchMaxSlots];
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_tiles[kMaxExperts];
@@ -748,7 +753,7 @@ bool small_dispatch_ok(int64_t P, int E) { return P <= kSmallDispatchMaxSlots &&
 cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, const uint16_t* x, int64_t T, int k,
                             int E, int D, int nt, int32_t* counts, int32_t* cursor, Seg* segs, int32_t* tile_prefix,
                             int32_t* slot_pos, uint16_t* w_perm, uint16_t* x_perm, const int32_t* perm_nbits,
-                            const int32_t* order_nbits, cudaStream_t stream) {
+                            const int32_t* order_nbits, int32_t* zero_buf, int zero_n, cudaStream_t stream) {
   const int64_t P = T * k;
   if (perm_nbits != nullptr && D % kperm::kStageK != 0) return cudaErrorInvalidValue;
   // permuted copies stage each warp's row in shared memory (8 warps per block)
@@ -766,14 +771,15 @@ cudaError_t launch_dispatch(const int32_t* topk_idx, const uint16_t* topk_w, con
     return launch_dep(k_dispatch_small, dim3(grid), dim3(256), row_smem, stream, topk_idx,
                       reinterpret_cast<const __half*>(topk_w), reinterpret_cast<const __half*>(x), static_cast<int>(P),
                       k, E, D, nt, counts, segs, tile_prefix, slot_pos, reinterpret_cast<__half*>(w_perm),
-                      reinterpret_cast<__half*>(x_perm), perm_nbits, order_nbits);
+                      reinterpret_cast<__half*>(x_perm), perm_nbits, order_nbits, zero_buf, zero_n);
   }
   err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, stream);
   if (err != cudaSuccess) return err;
   err = launch_dep(k_count, dim3(static_cast<unsigned>((P + kCountSlotsPerCta - 1) / kCountSlotsPerCta)), dim3(256), 0,
                    stream, topk_idx, P, E, counts);
   if (err != cudaSuccess) return err;
-  err = launch_dep(k_scan_segs, dim3(1), dim3(1024), 0, stream, counts, E, nt, segs, tile_prefix, cursor);
+  err = launch_dep(k_scan_segs, dim3(1), dim3(1024), 0, stream, counts, E, nt, segs, tile_prefix, cursor, zero_buf,
+                   zero_n);
   if (err != cudaSuccess) return err;
   return launch_dep(k_scatter, dim3(static_cast<unsigned>((T + kScatterWarps - 1) / kScatterWarps)),
                     dim3(32 * kScatterWarps), row_smem, stream, topk_idx, reinterpret_cast<const __half*>(topk_w),

@@ -128,6 +128,12 @@ struct KArgsD {
   int64_t out_ld;
   const __half* row_weight;
   const int32_t* perm_out_nbits;  // kSwiGLU: store h in the slot order of these bit-widths
+  // Chained gate/up -> down launch of one forward: per token tile, the number of
+  // gate/up epilogue warps that have stored their h columns. kSwiGLU adds to it and
+  // lets the down launch start early; kRouteWeight waits for chain_target before
+  // loading a tile's h rows (and skips the grid-completion wait).
+  int32_t* chain_done;
+  int chain_target;
 };
 
 // Packed-word maps per matrix and box height (4, 8, 14, 16 rows for b = 1, 2, 3, 4).
@@ -561,8 +567,11 @@ __global__ void __launch_bounds__(kThreadsD, 1)
     tmem_relinquish();
   }
   // everything above is private to this CTA; from here on it reads the segment
-  // table, activations and weights, and writes outputs other kernels use
-  grid_dep_wait();
+  // table, activations and weights, and writes outputs other kernels use. A chained
+  // down launch reads the segment table and routing weights the dispatch wrote before
+  // the gate/up launch got past its own wait, and waits per tile for h instead.
+  const bool chained_down = MODE == GemmMode::kRouteWeight && p.chain_done != nullptr;
+  if (!chained_down) grid_dep_wait();
   Meta& meta = *reinterpret_cast<Meta*>(smem + C::kMetaOff);
   tcw::stage_meta(meta, p, false);
   __syncthreads();
@@ -617,6 +626,14 @@ __global__ void __launch_bounds__(kThreadsD, 1)
         const CUtensorMap* wmap = &tm_words.m[mat][box_index(nb)];
         const int wrow = first ? wk.wrow0 : wk.wrow1;
         const int ncol = C::kPairTiles ? 2 * wk.n0 + mat * 128 : wk.n0;
+        if (chained_down) {  // the tile's h rows: every gate/up item of the tile stored
+          bool done = true;
+          if (elect_one()) done = tile_done_wait(p.chain_done + w / p.n_tiles, p.chain_target);
+          if (__any_sync(0xffffffffu, !done)) {
+            ok = false;
+            break;
+          }
+        }
         for (int kt = 0; kt < KT; ++kt) {
           if (!warp_wait(&empty[s], ph ^ 1u, kDevTimeoutTmaEmpty, kIdleSleepNs)) { ok = false; break; }
           uint8_t* st = smem + s * C::kStageBytes;
@@ -693,7 +710,10 @@ __global__ void __launch_bounds__(kThreadsD, 1)
       bool ok = true;
       ItemWalk items(total);
       int w;
+      const bool chain_up = MODE == GemmMode::kSwiGLU && p.chain_done != nullptr;
+      if (chain_up && items.n == 0) grid_dep_launch();
       for (; ok && items.next(w); ++it) {
+        if (chain_up && items.j == items.n) grid_dep_launch();  // this CTA's last item
         const int buf = it % C::kAccBufs;
         const uint32_t d_base = tmem + static_cast<uint32_t>(buf * C::kAccCols);
         if (!warp_wait(&acc_empty[buf], ((it / C::kAccBufs) & 1) ^ 1u, kDevTimeoutAccEmpty, kBusySleepNs)) break;
@@ -821,6 +841,9 @@ __global__ void __launch_bounds__(kThreadsD, 1)
           __syncwarp();
         }
       }
+      // this warp's h columns of the item are stored: one count on the token tile
+      if constexpr (MODE == GemmMode::kSwiGLU)
+        if (p.chain_done != nullptr) tile_done_signal(p.chain_done + w / p.n_tiles);
     }
   } else {
     // ------------------------------------------------------------ dequant
@@ -939,6 +962,8 @@ cudaError_t launch_d(const GemmArgs& a, cudaStream_t stream) {
   p.out_ld = a.out_ld;
   p.row_weight = reinterpret_cast<const __half*>(a.row_weight);
   p.perm_out_nbits = a.perm_out_nbits;
+  p.chain_done = a.chain_done;
+  p.chain_target = a.chain_target;
   auto kern = k_moe_tcd<NT, MODE, SUB>;
   // set once per instantiation and device (outside any graph capture)
   static std::atomic<size_t> smem_done[kMaxDevices];
