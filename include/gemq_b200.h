@@ -49,6 +49,9 @@ extern "C" {
 #define GEMQ_FWD_PERMUTED_ROWS 512u  /* gemq_moe_experts: rows are in the tensor-memory GEMM's K order (see there) */
 #define GEMQ_FWD_NO_CHAIN 1024u      /* start the down GEMM after the gate/up GEMM completes, not on the SMs it
                                         leaves as its token tiles finish (cross-checking) */
+#define GEMQ_FWD_TEST_WAIT_EXPIRY 2048u /* testing: the chained down GEMM of a decode batch waits for a tile count
+                                        nothing reaches, so its bounded wait expires; the device error word
+                                        then reads 11 and this forward's output is undefined */
 
 /* Stage indices reported by gemq_layer_stage_times. */
 #define GEMQ_STAGE_ROUTE 0    /* gate GEMM + softmax/top-k */
@@ -105,7 +108,13 @@ typedef struct gemq_layer gemq_layer_t;
 /* ---------------------------------------------------------------- status */
 const char* gemq_last_error_string(void); /* host string, thread-local */
 int gemq_version(void);
-/* Synchronises the device, returns the device error word (0 = none) and clears it. */
+/* Synchronises the device, returns the device error word (0 = none) and clears it.
+ * The first error recorded since the last call: 1-7 a bounded wait of the GEMM
+ * pipeline expired (copies landed, stage freed, A stage written, A stage read,
+ * accumulator full, accumulator free, drain), 8 an expert id out of range, 9 a
+ * bit-width outside 1..4, 10 a KV-cache position past the cache, 11 a chained
+ * down-projection item waited too long for its gate/up tiles. After an expired wait
+ * the kernels of that forward drain and return; its outputs are undefined. */
 int gemq_get_device_error(uint32_t* code_out /* host */);
 
 /* ---------------------------------------------------------------- packing */

@@ -37,6 +37,7 @@ FWD_TIME_STAGES = 128
 FWD_SMEM_DEQUANT = 256
 FWD_PERMUTED_ROWS = 512
 FWD_NO_CHAIN = 1024
+FWD_TEST_WAIT_EXPIRY = 2048
 ROUTE_WORKSPACE_BYTES = 1024
 STAGES = ("route", "dispatch", "up", "down", "shared", "combine")
 

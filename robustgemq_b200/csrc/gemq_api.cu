@@ -709,6 +709,7 @@ int forward_n_tokens(gemq_layer_t* L, const uint16_t* x, int64_t T, uint16_t* ou
   if (chain) {
     up.chain_done = dn.chain_done = b.tile_done;
     dn.chain_target = (F / 128) * 4;  // gate/up feature tiles x epilogue warps per tile
+    if (flags & GEMQ_FWD_TEST_WAIT_EXPIRY) dn.chain_target = INT32_MAX;  // a count no tile reaches
   }
   tm.begin(GEMQ_STAGE_DISPATCH);
   GEMQ_CUDA(launch_dispatch(idx, w, x, T, k, E, D, up.nt, b.counts, b.cursor, b.segs, b.tile_prefix, b.slot_pos,

@@ -87,3 +87,32 @@ def test_chained_down_launch_in_a_cuda_graph():
         torch.cuda.synchronize()
         assert torch.equal(out, ref), f"replay {i}"
     assert _lib.device_error() == 0
+
+
+def test_expired_wait_is_reported_and_the_context_stays_usable():
+    """A wait that runs out (the chained down GEMM waits for a tile count nothing
+    reaches, GEMQ_FWD_TEST_WAIT_EXPIRY) ends the forward within its time bound with
+    a wait-expiry error recorded; the next forward on the same context is correct."""
+    import time
+
+    from robustgemq_b200 import _lib, synth
+
+    blk = _block(synth.olmoe_config)
+    x = torch.randn((64, blk.hidden_dim), generator=torch.Generator(device="cuda").manual_seed(5),
+                    device="cuda").half()
+    ref = _fwd(blk, x, chain=True)
+    assert _lib.device_error() == 0
+    blk._fwd_flags = _lib.FWD_TEST_WAIT_EXPIRY
+    try:
+        t0 = time.monotonic()
+        blk.forward_n_tokens(x.unsqueeze(0))
+        code = _lib.device_error()  # synchronises
+        waited = time.monotonic() - t0
+    finally:
+        blk._fwd_flags = 0
+    # 11: the chained wait; a pipeline wait of the same kernel (1-7) may run out a
+    # moment earlier and be the one recorded
+    assert code & 0xFF in (1, 2, 3, 4, 5, 6, 7, 11), code
+    assert waited < 20.0
+    assert torch.equal(_fwd(blk, x, chain=True), ref)
+    assert _lib.device_error() == 0
