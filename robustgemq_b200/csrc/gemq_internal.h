@@ -146,7 +146,7 @@ cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16
 // topk_group of them; scale multiplies the weights when not renormalising.
 cudaError_t launch_topk(const void* logits, bool logits_fp32, int64_t T, int E, int k, bool norm, bool fp16_softmax,
                         int n_group, int topk_group, float scale, int32_t* topk_idx, uint16_t* topk_w,
-                        cudaStream_t stream);
+                        cudaStream_t stream, int32_t* zero_buf = nullptr, int zero_n = 0);
 bool small_dispatch_ok(int64_t P, int E);
 // Segments of rows grouped as [group][expert] (n = groups * E counts, n <= 1024).
 cudaError_t launch_group_segs(const int32_t* counts, int n, int E, int nt, Seg* segs, int32_t* tile_prefix,
@@ -184,6 +184,12 @@ struct GemvSrc {
   int64_t x_stride;     // elements between rows a (0: one row shared by all a)
   const float* part;    // kGemvPart*: up partials [2][part_splits][part_rows][part_n]
   int part_splits, part_rows, part_n;
+  // Chained one-token up -> down GEMVs (counters [rows], zeroed by the forward's
+  // router): kGemvX adds 1 to done[a] per CTA once its partials are stored and lets
+  // the down launch start at once; kGemvPartF32 waits for done_target on its row's
+  // counter instead of the grid-completion wait before reading the partials.
+  int32_t* done;
+  int done_target;
 };
 // Split-K factor of a GEMV over rows_a rows and nmat matrices. Fewer matrices never
 // give fewer splits, so a workspace sized with nmat = 1 also fits nmat = 2.

@@ -298,7 +298,13 @@ template <bool SUB>
 __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) k_gemv(ProjDev w0, ProjDev w1, const int32_t* __restrict__ idx,
                                                           int rows_a, GemvSrc src, float* __restrict__ part,
                                                           int splits, int bulk_words) {
-  grid_dep_wait();
+  // chained one-token GEMVs: the up launch signals per row, the down launch waits per
+  // row (the routing ids and weights it reads were complete before the up launch got
+  // past its own wait)
+  const bool chain_out = src.done != nullptr && src.mode == kGemvX;
+  const bool chain_in = src.done != nullptr && src.mode == kGemvPartF32;
+  if (!chain_in) grid_dep_wait();
+  if (chain_out) grid_dep_launch();
   extern __shared__ __align__(16) unsigned char s_raw[];
   __shared__ float s_red[8][kGemvCols];
   __shared__ uint64_t s_wbar;
@@ -306,14 +312,23 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) k_gemv(ProjDev w
   const int mat = blockIdx.z / rows_a, a = blockIdx.z - mat * rows_a;
   const ProjDev& w = (mat == 0) ? w0 : w1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // a chained up CTA that stores nothing still counts itself done
+  auto signal_row = [&]() {
+    if (chain_out && threadIdx.x == 0) {
+      __threadfence();
+      atomicAdd(src.done + a, 1);
+    }
+  };
   const int e = (idx != nullptr) ? idx[a] : a;
   if (e < 0 || e >= w.num_experts) {
     if (threadIdx.x == 0) set_device_error(kDevBadExpert);
+    signal_row();
     return;
   }
   const int nb = w.nbits[e];
   if (nb < 1 || nb > 4) {
     if (threadIdx.x == 0) set_device_error(kDevBadBits);
+    signal_row();
     return;
   }
   const int eps = 32 / nb;
@@ -349,61 +364,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) k_gemv(ProjDev w
   } else if (n < N) {
     load_words(wbase, N, n, wr0, wr1, wv);
   }
-  // Stage x and the scale / zero rows. Every thread first issues all of its loads
-  // for a batch of elements into registers and only then stores them, so a batch
-  // costs one memory round trip instead of one per element.
-  constexpr int kXB = 4;  // elements per thread per batch
-  for (int base = 0; base < kspan; base += kXB * kGemvThreads) {
-    float v[kXB];
-    if (src.mode == kGemvX || src.mode == kGemvSwiGLU) {
-      __half x1[kXB], x3[kXB];
-#pragma unroll
-      for (int j = 0; j < kXB; ++j) {
-        const int kk = k0 + base + j * kGemvThreads + threadIdx.x;
-        const bool in = (base + j * kGemvThreads + threadIdx.x < kspan) && kk < K;
-        x1[j] = in ? src.x[a * src.x_stride + kk] : __float2half_rn(0.f);
-        x3[j] = (in && src.mode == kGemvSwiGLU) ? src.x3[a * src.x_stride + kk] : __float2half_rn(0.f);
-      }
-#pragma unroll
-      for (int j = 0; j < kXB; ++j)
-        v[j] = (src.mode == kGemvX) ? __half2float(x1[j]) : silu_f32(__half2float(x1[j])) * __half2float(x3[j]);
-    } else {
-      const int64_t mstride = static_cast<int64_t>(src.part_splits) * src.part_rows * src.part_n;
-      float g1[kXB], g3[kXB];
-#pragma unroll
-      for (int j = 0; j < kXB; ++j) g1[j] = g3[j] = 0.f;
-      // split-major: the loads of all elements of one split issue together
-      for (int q = 0; q < src.part_splits; ++q) {
-#pragma unroll
-        for (int j = 0; j < kXB; ++j) {
-          const int kk = k0 + base + j * kGemvThreads + threadIdx.x;
-          if (base + j * kGemvThreads + threadIdx.x < kspan && kk < K) {
-            const int64_t off = (static_cast<int64_t>(q) * src.part_rows + a) * src.part_n + kk;
-            g1[j] += src.part[off];
-            g3[j] += src.part[mstride + off];
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kXB; ++j) {
-        const float x1 = __half2float(__float2half_rn(g1[j]));
-        const float x3 = __half2float(__float2half_rn(g3[j]));
-        v[j] = (src.mode == kGemvPartF32)
-                   ? silu_f32(x1) * x3
-                   : __half2float(__float2half_rn(__half2float(__float2half_rn(silu_f32(x1))) * x3));
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kXB; ++j) {
-      const int i = base + j * kGemvThreads + threadIdx.x;
-      if (i < kspan) {
-        // code c of word row r at slot r * eps + (c < eps/2 ? 2c : 2(c - eps/2) + 1)
-        const int r = i / eps, c = i - r * eps, h = eps >> 1;
-        const int slot = r * eps + (c < h ? 2 * c : 2 * (c - h) + 1);
-        reinterpret_cast<float*>(s_raw)[slot] = v[j];  // fp32 (fp16 inputs convert exactly)
-      }
-    }
-  }
+  constexpr int kXB = 4;  // elements per thread per batch of a staging loop
   // the scale / zero rows of the groups [g0, g1] this block's K range touches
   const int xbytes = 4 * gemv_x_elems(K, splits);
   __half* s_s = reinterpret_cast<__half*>(s_raw + ((xbytes + 15) & ~15));
@@ -450,6 +411,67 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) k_gemv(ProjDev w
       }
     }
   }
+  // Stage x (after the scale / zero rows above, which do not depend on the up
+  // projection). Every thread first issues all of its loads for a batch of elements
+  // into registers and only then stores them, so a batch costs one memory round trip
+  // instead of one per element. A chained down launch first waits for its row's up
+  // partials (one thread polls; the barrier passes the acquire on) and reads them past
+  // L1.
+  if (chain_in) {
+    if (threadIdx.x == 0) tile_done_wait(src.done + a, src.done_target);
+    __syncthreads();
+  }
+  for (int base = 0; base < kspan; base += kXB * kGemvThreads) {
+    float v[kXB];
+    if (src.mode == kGemvX || src.mode == kGemvSwiGLU) {
+      __half x1[kXB], x3[kXB];
+#pragma unroll
+      for (int j = 0; j < kXB; ++j) {
+        const int kk = k0 + base + j * kGemvThreads + threadIdx.x;
+        const bool in = (base + j * kGemvThreads + threadIdx.x < kspan) && kk < K;
+        x1[j] = in ? src.x[a * src.x_stride + kk] : __float2half_rn(0.f);
+        x3[j] = (in && src.mode == kGemvSwiGLU) ? src.x3[a * src.x_stride + kk] : __float2half_rn(0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < kXB; ++j)
+        v[j] = (src.mode == kGemvX) ? __half2float(x1[j]) : silu_f32(__half2float(x1[j])) * __half2float(x3[j]);
+    } else {
+      const int64_t mstride = static_cast<int64_t>(src.part_splits) * src.part_rows * src.part_n;
+      float g1[kXB], g3[kXB];
+#pragma unroll
+      for (int j = 0; j < kXB; ++j) g1[j] = g3[j] = 0.f;
+      // split-major: the loads of all elements of one split issue together
+      for (int q = 0; q < src.part_splits; ++q) {
+#pragma unroll
+        for (int j = 0; j < kXB; ++j) {
+          const int kk = k0 + base + j * kGemvThreads + threadIdx.x;
+          if (base + j * kGemvThreads + threadIdx.x < kspan && kk < K) {
+            const int64_t off = (static_cast<int64_t>(q) * src.part_rows + a) * src.part_n + kk;
+            g1[j] += __ldcg(src.part + off);
+            g3[j] += __ldcg(src.part + mstride + off);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kXB; ++j) {
+        const float x1 = __half2float(__float2half_rn(g1[j]));
+        const float x3 = __half2float(__float2half_rn(g3[j]));
+        v[j] = (src.mode == kGemvPartF32)
+                   ? silu_f32(x1) * x3
+                   : __half2float(__float2half_rn(__half2float(__float2half_rn(silu_f32(x1))) * x3));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kXB; ++j) {
+      const int i = base + j * kGemvThreads + threadIdx.x;
+      if (i < kspan) {
+        // code c of word row r at slot r * eps + (c < eps/2 ? 2c : 2(c - eps/2) + 1)
+        const int r = i / eps, c = i - r * eps, h = eps >> 1;
+        const int slot = r * eps + (c < h ? 2 * c : 2 * (c - h) + 1);
+        reinterpret_cast<float*>(s_raw)[slot] = v[j];  // fp32 (fp16 inputs convert exactly)
+      }
+    }
+  }
   __syncthreads();
   float acc[4][2] = {};
   const GroupStage gs{s_s, s_z, g0};
@@ -473,6 +495,10 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) k_gemv(ProjDev w
       for (int i = 0; i < 8; ++i) v += s_red[i][threadIdx.x];
       part[((static_cast<int64_t>(mat) * splits + s) * rows_a + a) * N + nn] = v;
     }
+  }
+  if (chain_out) {
+    __syncthreads();
+    signal_row();
   }
 }
 

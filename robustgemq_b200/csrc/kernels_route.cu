@@ -173,8 +173,11 @@ __device__ __forceinline__ void topk_warp(GetLogit get, int E, int k, const Topk
 // One warp per token, logits from global memory (the tensor-core router's output
 // or given logits).
 __global__ void k_topk(const void* __restrict__ logits, int logits_fp32, int64_t T, int E, int k, TopkOpts o,
-                       int32_t* __restrict__ topk_idx, __half* __restrict__ topk_w) {
+                       int32_t* __restrict__ topk_idx, __half* __restrict__ topk_w, int32_t* __restrict__ zero_buf,
+                       int zero_n) {
   grid_dep_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < zero_n; i += gridDim.x * blockDim.x)
+    zero_buf[i] = 0;  // the forward's chained-GEMV counters
   const int64_t t = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   if (t >= T) return;
   auto get = [&](int e) {
@@ -685,11 +688,11 @@ __global__ void __launch_bounds__(32 * kCombineWarps, KMAX == 8 ? 2 : 1)
 
 cudaError_t launch_topk(const void* logits, bool logits_fp32, int64_t T, int E, int k, bool norm, bool fp16_softmax,
                         int n_group, int topk_group, float scale, int32_t* topk_idx, uint16_t* topk_w,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, int32_t* zero_buf, int zero_n) {
   if (T == 0) return cudaSuccess;
   const TopkOpts o{norm ? 1 : 0, fp16_softmax ? 1 : 0, n_group, topk_group, scale};
   return launch_dep(k_topk, dim3(static_cast<unsigned>((T * 32 + 255) / 256)), dim3(256), 0, stream, logits,
-                    logits_fp32 ? 1 : 0, T, E, k, o, topk_idx, reinterpret_cast<__half*>(topk_w));
+                    logits_fp32 ? 1 : 0, T, E, k, o, topk_idx, reinterpret_cast<__half*>(topk_w), zero_buf, zero_n);
 }
 
 cudaError_t launch_gate_logits(const uint16_t* x, int64_t T, int D, const uint16_t* gate, int E, bool fp32_logits,

@@ -1,4 +1,4 @@
-"""Chained gate/up -> down launch of the decode GEMM (``-m gpu``).
+"""Chained gate/up -> down launches of the decode GEMM and of the one-token GEMVs (``-m gpu``).
 
 The down-projection GEMM starts on the SMs the gate/up GEMM leaves and takes each
 token tile once a per-tile counter shows all of its gate/up items stored (the
@@ -115,4 +115,67 @@ def test_expired_wait_is_reported_and_the_context_stays_usable():
     assert code & 0xFF in (1, 2, 3, 4, 5, 6, 7, 11), code
     assert waited < 20.0
     assert torch.equal(_fwd(blk, x, chain=True), ref)
+    assert _lib.device_error() == 0
+
+
+def _fwd_one(blk, x, chain: bool):
+    from robustgemq_b200 import _lib
+
+    blk._fwd_flags = 0 if chain else _lib.FWD_NO_CHAIN
+    try:
+        out = blk.forward_one_token(x.view(1, 1, -1))
+        return out[0] if isinstance(out, tuple) else out
+    finally:
+        blk._fwd_flags = 0
+
+
+@pytest.mark.parametrize("family", ["olmoe", "deepseek"])
+def test_chained_one_token_gemvs_are_bit_identical(family):
+    """One-token path: the down GEMV starts with the up GEMV and waits per routed row
+    for its partials; the output equals the unchained forward's, bit for bit, over
+    several tokens and repeated calls (DeepSeek: the unchained shared experts after)."""
+    from types import SimpleNamespace
+
+    from robustgemq_b200 import _lib, synth
+    from robustgemq_b200.inference import QuantFusedDeepseekV2MoEBlock
+
+    if family == "olmoe":
+        blk = _block(synth.olmoe_config)
+    else:
+        cfg = SimpleNamespace(hidden_size=2048, moe_intermediate_size=1408, n_routed_experts=64,
+                              n_shared_experts=2, num_experts_per_tok=6, norm_topk_prob=False,
+                              topk_method="greedy", scoring_func="softmax", routed_scaling_factor=1.0)
+        blk = synth.random_block(QuantFusedDeepseekV2MoEBlock, cfg, 2048, 1408, 64, 2.75, 64, seed=4,
+                                 device=torch.device("cuda"), shared_inter=2816)
+    g = torch.Generator(device="cuda").manual_seed(17)
+    for i in range(4):
+        x = torch.randn((1, blk.hidden_dim), generator=g, device="cuda").half()
+        ref = _fwd_one(blk, x, chain=False)
+        for _ in range(2):
+            assert torch.equal(_fwd_one(blk, x, chain=True), ref), i
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+
+
+def test_chained_one_token_gemvs_in_a_cuda_graph():
+    from robustgemq_b200 import _lib, synth
+
+    blk = _block(synth.olmoe_config)
+    x = torch.randn((1, blk.hidden_dim), generator=torch.Generator(device="cuda").manual_seed(2),
+                    device="cuda").half()
+    ref = _fwd_one(blk, x, chain=False)
+    xs = x.clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        _fwd_one(blk, xs, chain=True)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = blk.forward_one_token(xs.view(1, 1, -1))[0]
+    for i in range(3):
+        xs.copy_(x)
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref), f"replay {i}"
     assert _lib.device_error() == 0
