@@ -149,3 +149,21 @@ def test_group_limited_block_matches_oracle(T):
     else:
         ref, _ = O.moe_forward_n_tokens(ob, xn, r)
     assert rel_l2(out.reshape(T, -1).float().cpu().numpy(), ref.reshape(T, -1).astype(np.float32)) <= 1e-3
+
+
+def test_expert_parallel_carries_the_group_routing():
+    """An expert-parallel wrapper routes over all experts with the block's group-limited
+    selection and scale (``gemq_route_ex`` options), built on CPU without weights."""
+    from robustgemq_b200.inference import QuantFusedDeepseekV2MoEBlock
+    from robustgemq_b200.inference.expert_parallel import ExpertParallelMoE
+
+    cfg = SimpleNamespace(hidden_size=64, moe_intermediate_size=32, n_routed_experts=E, n_shared_experts=1,
+                          num_experts_per_tok=K, norm_topk_prob=False, topk_method="group_limited_greedy",
+                          n_group=NG, topk_group=TG, scoring_func="softmax", routed_scaling_factor=16.0)
+    blk = QuantFusedDeepseekV2MoEBlock(cfg)
+    assert (blk.n_group, blk.topk_group) == (NG, TG)
+    blk.set_routing(routed_scaling_factor=16.0)
+    ep = ExpertParallelMoE(blk)
+    assert ep.routing == (False, NG, TG, 16.0)
+    r = blk.routing_options()
+    assert (r.norm_topk_prob, r.n_group, r.topk_group, r.scale) == (0, NG, TG, 16.0)
