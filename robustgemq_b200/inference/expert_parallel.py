@@ -384,17 +384,7 @@ class ExpertParallelMoE(nn.Module):
         self._mark(0, dev)
         logits, idx, w = self.route_fn(x)
         self._mark(1, dev)
-        flat = idx.reshape(-1)
-        valid = (flat >= 0) & (flat < self.num_experts)
-        bad = (~valid).any().to(torch.int32).reshape(1)
-        didx = idx
-        if not self._identity:  # dispatch by position in the placement; invalid ids pass through
-            if self._slot_of is None or self._slot_of.device != idx.device:
-                slot = torch.empty(self.num_experts, dtype=torch.int32)
-                slot[torch.tensor(self.placement)] = torch.arange(self.num_experts, dtype=torch.int32)
-                self._slot_of = slot.to(idx.device)
-            didx = torch.where(valid, self._slot_of[flat.clamp(0, self.num_experts - 1).long()],
-                               flat.to(torch.int32)).reshape(idx.shape).to(idx.dtype)
+        bad, didx = self._placed_ids(idx)
         counts, slot_row, w_rows, x_rows = self.dispatch_fn(didx, w, x)
         self._count_load(counts)
         self._mark(2, dev)
@@ -424,6 +414,112 @@ class ExpertParallelMoE(nn.Module):
         out = self.combine_fn(back, slot_row, idx.to(torch.int32).contiguous(), residual)
         self._mark(7, dev)
         return out, logits
+
+    def _placed_ids(self, idx: Tensor) -> Tuple[Tensor, Tensor]:
+        """``(bad [1] int32, ids to dispatch by)``: whether any routed id lies outside
+        ``[0, E)``, and each id's position in the placement (invalid ids pass through,
+        for the dispatch to record and skip)."""
+        flat = idx.reshape(-1)
+        valid = (flat >= 0) & (flat < self.num_experts)
+        bad = (~valid).any().to(torch.int32).reshape(1)
+        if self._identity:
+            return bad, idx
+        if self._slot_of is None or self._slot_of.device != idx.device:
+            slot = torch.empty(self.num_experts, dtype=torch.int32)
+            slot[torch.tensor(self.placement)] = torch.arange(self.num_experts, dtype=torch.int32)
+            self._slot_of = slot.to(idx.device)
+        didx = torch.where(valid, self._slot_of[flat.clamp(0, self.num_experts - 1).long()], flat.to(torch.int32))
+        return bad, didx.reshape(idx.shape).to(idx.dtype)
+
+    def _a2a_start(self, send: Tensor, send_counts, recv_counts, step: str):
+        """Starts an all-to-all; returns ``(recv, wait)``, ``wait()`` completing it (on
+        NCCL the current stream then waits for it; the exchange itself runs on the
+        process group's own stream, beside the GEMMs enqueued meanwhile)."""
+        recv = send.new_empty((int(sum(recv_counts)),) + tuple(send.shape[1:]))
+        if self.world == 1:
+            recv.copy_(send)
+            return recv, lambda: None
+        try:
+            work = dist.all_to_all_single(recv, send.contiguous(), [int(c) for c in recv_counts],
+                                          [int(c) for c in send_counts], group=self.group, async_op=True)
+        except Exception as exc:
+            self._broken = f"exchange of {step} failed on rank {self.rank} of {self.world}: {exc}"
+            raise ExpertParallelError(self._broken) from exc
+
+        def wait():
+            try:
+                work.wait()
+            except Exception as exc:  # a peer is gone, timed out or aborted
+                self._broken = f"exchange of {step} failed on rank {self.rank} of {self.world}: {exc}"
+                raise ExpertParallelError(self._broken) from exc
+
+        return recv, wait
+
+    def forward_tokens_chunked(self, x: Tensor, chunks: int) -> Tuple[Tensor, Tensor]:
+        """``forward_tokens`` over ``chunks`` contiguous token chunks whose exchanges
+        overlap the expert GEMMs: chunk c + 1's activation rows and weights travel
+        while chunk c's experts run, and chunk c's outputs travel back while later
+        chunks compute. The whole batch is routed at once and one counts exchange
+        (the one host synchronisation) covers every chunk. The output equals
+        ``forward_tokens``' bit for bit: each row is computed alone and the combine
+        visits a token's experts in ascending id. Every rank must pass the same
+        ``chunks``. Stage timing is not recorded here."""
+        T = x.shape[0]
+        if chunks <= 1:
+            return self.forward_tokens(x)
+        if self._broken is not None:
+            raise ExpertParallelError(f"an earlier exchange failed ({self._broken}); rebuild the process group")
+        x = x.contiguous()
+        epr, W = self.experts_per_rank, self.world
+        bounds = [T * c // chunks for c in range(chunks + 1)]
+        logits, idx, w = self.route_fn(x)
+        bad, didx = self._placed_ids(idx)
+        parts = []
+        for c in range(chunks):
+            a, b = bounds[c], bounds[c + 1]
+            counts, slot_row, w_rows, x_rows = self.dispatch_fn(didx[a:b].contiguous(), w[a:b].contiguous(),
+                                                                x[a:b].contiguous())
+            self._count_load(counts)
+            parts.append((counts, slot_row, w_rows, x_rows))
+        # one message per destination: every chunk's counts of its experts, then this
+        # rank's routing status
+        cnt = torch.stack([p[0].to(torch.int32).reshape(W, epr) for p in parts], dim=1).reshape(W, chunks * epr)
+        msg = torch.cat([cnt, bad.to(cnt.device).expand(W, 1)], dim=1)
+        n = chunks * epr + 1
+        rmsg = self._a2a(msg.reshape(-1), [n] * W, [n] * W, "counts").reshape(W, n)
+        both = torch.stack([msg, rmsg]).cpu()
+        bad_ranks = [r for r in range(W) if int(both[1, r, n - 1]) != 0]
+        if bad_ranks:
+            raise ExpertParallelError(
+                f"invalid routing table (expert id outside [0, {self.num_experts})) on rank(s) {bad_ranks}; "
+                "no rows were exchanged")
+        sent = both[0, :, :n - 1].reshape(W, chunks, epr).sum(dim=2)  # [destination, chunk]
+        got = both[1, :, :n - 1].reshape(W, chunks, epr).sum(dim=2)   # [source, chunk]
+
+        def start_rows(c):
+            sc, rc = sent[:, c].tolist(), got[:, c].tolist()
+            rows = self._a2a_start(parts[c][3], sc, rc, f"activation rows of chunk {c}")
+            wts = self._a2a_start(parts[c][2], sc, rc, f"routing weights of chunk {c}")
+            return rows, wts
+
+        backs = []
+        nxt = start_rows(0)
+        for c in range(chunks):
+            (rows, wait_rows), (wts, wait_wts) = nxt
+            wait_rows()
+            wait_wts()
+            if c + 1 < chunks:
+                nxt = start_rows(c + 1)
+            y = self.experts_fn(rows, rmsg[:, c * epr:(c + 1) * epr], wts)
+            backs.append(self._a2a_start(y, got[:, c].tolist(), sent[:, c].tolist(), f"expert outputs of chunk {c}"))
+        outs = []
+        for c in range(chunks):
+            back, wait_back = backs[c]
+            wait_back()
+            a, b = bounds[c], bounds[c + 1]
+            residual = self.shared.forward_shared(x[a:b]) if self.shared is not None else None
+            outs.append(self.combine_fn(back, parts[c][1], idx[a:b].to(torch.int32).contiguous(), residual))
+        return torch.cat(outs), logits
 
     def forward(self, hidden_states: Tensor):
         shape = hidden_states.shape

@@ -192,6 +192,55 @@ def test_expert_parallel_two_gloo_ranks_match_the_single_block(placement):
     assert dict(results) == {0: (True, True), 1: (True, True)}
 
 
+def _chunked_rank(rank, world, port, results, chunks, placement):
+    import torch.distributed as dist
+    from oracle import gemq_oracle as O
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        ep, ow, d = _cpu_ep(placement=placement)
+        mine = np.ascontiguousarray(d["x"].astype(F16)[rank::world])
+        out, _ = ep.forward_tokens_chunked(torch.from_numpy(mine), chunks)
+        ref, _ = O.moe_forward_n_tokens(ow, mine)
+        results[rank] = bool(np.array_equal(out.numpy().view(np.uint16), ref.view(np.uint16)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("chunks,shuffled", [(2, False), (3, True)])
+def test_chunked_exchange_two_gloo_ranks_match_the_single_block(chunks, shuffled):
+    """Chunked forward (asynchronous exchanges of chunk c + 1 beside chunk c's experts):
+    bit-identical to the 1-process block on both ranks."""
+    import torch.multiprocessing as mp
+
+    placement = None
+    if shuffled:
+        E = int(load_golden("block_olmoe.npz")["w1_nbits"].shape[0])
+        placement = [int(e) for e in np.random.default_rng(5).permutation(E)]
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_chunked_rank, args=(r, 2, port, results, chunks, placement)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(results) == {0: True, 1: True}
+
+
+def test_chunked_forward_single_process():
+    from oracle import gemq_oracle as O
+
+    ep, ow, d = _cpu_ep()
+    x = np.ascontiguousarray(d["x"].astype(F16))
+    ref, _ = O.moe_forward_n_tokens(ow, x)
+    for chunks in (1, 2, 5):
+        out, _ = ep.forward_tokens_chunked(torch.from_numpy(x), chunks)
+        assert np.array_equal(out.numpy().view(np.uint16), ref.view(np.uint16)), chunks
+
+
 def test_balanced_placement():
     from robustgemq_b200.inference.expert_parallel import balanced_placement
 
