@@ -312,3 +312,24 @@ def test_calls_switch_to_the_inputs_device(monkeypatch):
     assert current["dev"] == 0  # restored after each call
     assert not _lib.off_current_device(_FakeCudaTensor(0))
     assert _lib.off_current_device(_FakeCudaTensor(3))
+
+
+def test_header_constants_match_the_python_binding():
+    """Every status, router, forward-flag and size constant of include/gemq_b200.h has
+    the same value in robustgemq_b200._lib (flags by name without the GEMQ_ prefix)."""
+    from robustgemq_b200 import _lib
+
+    header = (Path(__file__).resolve().parents[1] / "include" / "gemq_b200.h").read_text()
+    defs = dict(re.findall(r"^#define (GEMQ_[A-Z0-9_]+) (\d+)u?\b", header, flags=re.M))
+    assert len(defs) > 20
+    for name, value in defs.items():
+        if name.startswith("GEMQ_STAGE_") or name in ("GEMQ_NUM_STAGES", "GEMQ_NOALLOC_MAX_INDICES"):
+            continue
+        py = getattr(_lib, name, None)
+        if py is None:
+            py = getattr(_lib, name[len("GEMQ_"):], None)
+        assert py is not None, name
+        assert int(py) == int(value), name
+    stages = sorted((int(v), n[len("GEMQ_STAGE_"):].lower()) for n, v in defs.items() if n.startswith("GEMQ_STAGE_"))
+    assert tuple(n for _, n in stages) == _lib.STAGES
+    assert int(defs["GEMQ_NUM_STAGES"]) == len(_lib.STAGES)

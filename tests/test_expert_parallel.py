@@ -458,3 +458,31 @@ def test_expert_parallel_two_nccl_ranks_match_the_single_block():
         p.join(300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert all(results[r] < 1e-3 for r in range(2)), dict(results)
+
+
+def test_balanced_placement_properties():
+    """Random loads: a permutation of the experts, each rank's slice ascending, no
+    rank above the list-scheduling bound (mean load per rank + the largest expert
+    load), never worse than contiguous ranges."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    from robustgemq_b200.inference.expert_parallel import balanced_placement
+
+    @settings(max_examples=60, deadline=None, derandomize=True)
+    @given(st.sampled_from([(8, 1), (8, 2), (8, 4), (8, 8), (64, 4), (64, 8), (128, 8), (160, 8)]),
+           st.integers(min_value=0, max_value=2**31 - 1))
+    def check(shape, seed):
+        E, world = shape
+        load = np.random.default_rng(seed).zipf(1.3, size=E).astype(float)
+        order = balanced_placement(load.tolist(), world)
+        assert sorted(order) == list(range(E))
+        epr = E // world
+        slices = [order[r * epr:(r + 1) * epr] for r in range(world)]
+        assert all(sl == sorted(sl) for sl in slices)
+        worst = max(load[sl].sum() for sl in slices)
+        assert worst <= load.sum() / world + load.max() + 1e-9
+        contiguous = max(load[r * epr:(r + 1) * epr].sum() for r in range(world))
+        assert worst <= contiguous + 1e-9
+
+    check()
