@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--ep-layers", type=int, default=2)
     ap.add_argument("--ep-tokens", type=int, default=8192)
     ap.add_argument("--no-ep", action="store_true")
+    ap.add_argument("--ep-chunks", type=int, default=1,
+                    help="token chunks of the expert-parallel forward (exchanges overlap the previous chunk's GEMMs)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-configs", action="store_true", help="skip the config 0 / config 3 sub-objects")
@@ -485,9 +487,14 @@ def run_ep(args, rank, world, device, bf16_sus):
     gen = torch.Generator(device=device).manual_seed(900 + rank)
     x = torch.randn((T, shp["hidden"]), generator=gen, device=device).half()
 
+    chunks = max(1, args.ep_chunks)
+
+    def run(ep, xx):
+        return ep.forward_tokens_chunked(xx, chunks) if chunks > 1 else ep.forward_tokens(xx)
+
     def fwd():
         for ep in layers:  # every layer reads the same input; outputs are discarded
-            ep.forward_tokens(x)
+            run(ep, x)
 
     for _ in range(2):
         fwd()
@@ -503,8 +510,8 @@ def run_ep(args, rank, world, device, bf16_sus):
     torch.cuda.synchronize()
     ms = torch.tensor([s.elapsed_time(e) / reps], device=device)
     # per-step breakdown of the last layer of the last pass, max over ranks
-    st = layers[-1].stage_times()
-    brk = torch.tensor([st[n] for n in STAGES], device=device)
+    st = layers[-1].stage_times()  # not recorded by the chunked forward: zeros then
+    brk = torch.tensor([st.get(n, 0.0) for n in STAGES], device=device)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         dist.all_reduce(brk, op=dist.ReduceOp.MAX)
@@ -516,7 +523,7 @@ def run_ep(args, rank, world, device, bf16_sus):
     full0, _ = synth.random_block_experts(QuantFusedMixtralMoEBlock, full_cfg, shp["hidden"], shp["inter"], E,
                                           shp["mean_bits"], shp["group_size"], 7000, device)
     xp = x[:256].contiguous()
-    y_ep, _ = layers[0].forward_tokens(xp)
+    y_ep, _ = run(layers[0], xp)
     y_full = full0(xp[None])[0][0]
     err = ((y_ep.double() - y_full.double()).norm() / y_full.double().norm()).reshape(1)
     if world > 1:
@@ -527,7 +534,7 @@ def run_ep(args, rank, world, device, bf16_sus):
     flops = world * T * L * k * 6 * D * F
     return {"workload": f"mixtral-8x7b-shaped prefill, {L} layers, {T} tokens per rank, experts sharded over "
                         f"{world} rank(s), NCCL all-to-all dispatch/combine (config 4)",
-            "layers": L, "tokens_per_rank": T, "n_ranks": world, "ms_per_pass": round(ms, 3),
+            "layers": L, "tokens_per_rank": T, "n_ranks": world, "chunks": chunks, "ms_per_pass": round(ms, 3),
             "tokens_per_s": round(world * T / (ms * 1e-3), 1), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
             "frac_bf16_peak_per_gpu": round(flops / world / (ms * 1e-3) / 1e12 / bf16_sus, 3),
             "peak_tflops_used": bf16_sus,
